@@ -1,0 +1,131 @@
+/* z2b.h — C ABI of the B200 batched backbone decode step (libz2b.so).
+ *
+ * Drop-in for the batched backbone path of zonos2.cpp: the model loader, the
+ * continuous-batching context, per-slot prefill, the batched decode step, per-slot
+ * logits and the multi-codebook sampler. Plain pointers and sizes only; every call
+ * returns Z2B_OK (0) or an error code, and z2b_last_error() describes the last failure
+ * of the calling thread. A context is owned by one thread (as the reference's worker
+ * thread owns its zonos2_batch_ctx, src/server.cpp:13-14, 904-911); one context per GPU.
+ */
+#ifndef Z2B_H
+#define Z2B_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Z2B_OK 0
+#define Z2B_ERR_ARG 1          /* invalid argument or state */
+#define Z2B_ERR_IO 2           /* file cannot be read */
+#define Z2B_ERR_FORMAT 3       /* not a usable zonos2 GGUF */
+#define Z2B_ERR_CUDA 4         /* a CUDA runtime call failed */
+#define Z2B_ERR_OOM 5          /* device or KV-page memory exhausted */
+#define Z2B_ERR_DEVICE 6       /* a kernel reported an error (bad id, missing page, wait timeout) */
+#define Z2B_ERR_UNSUPPORTED 7  /* tensor type or shape this build does not handle */
+
+typedef struct z2b_model z2b_model;
+typedef struct z2b_ctx z2b_ctx;
+
+/* Hyper-parameters read from the GGUF keys zonos2.* (src/zonos2.h:14-50). */
+typedef struct z2b_hparams {
+    uint32_t n_layer, n_embd, head_dim, n_head, n_head_kv, n_ff, n_expert, n_ctx_train;
+    float rope_freq_base, rms_eps, qk_norm_eps, logit_softcap;
+    uint32_t n_codebooks, codebook_size, audio_vocab, eoa_id, audio_pad_id, text_vocab;
+    uint32_t spk_dim, spk_lda_dim, router_dim;
+    int32_t expert_used[128];          /* per layer: 0 dense FFN, else MoE top-k */
+    uint64_t weight_bytes;             /* GGUF bytes of all tensors on the device */
+} z2b_hparams;
+
+/* Sampling parameters of one stream (zonos2_sampling, src/zonos2.h:197-208). */
+typedef struct z2b_sampling {
+    float temperature;                 /* 1.15 */
+    int32_t top_k;                     /* 106 */
+    float top_p;                       /* 0 disables */
+    float min_p;                       /* 0.18 */
+    float rep_penalty;                 /* 1.2 */
+    int32_t rep_window;                /* 50, at most Z2B_MAX_REP_WINDOW */
+    int32_t rep_codebooks;             /* 8 */
+    uint32_t seed;                     /* std::mt19937 seed */
+    int32_t greedy;                    /* argmax, first max wins */
+} z2b_sampling;
+#define Z2B_MAX_REP_WINDOW 256
+
+/* One stream's work in a step. */
+typedef struct z2b_slot_desc {
+    int32_t slot;                      /* cache band / column (zonos2_slot::index) */
+    int32_t n_past;                    /* logical position of the first new row (zonos2_slot::n_past) */
+    int32_t n_new;                     /* rows fed this step: 1 = decode, >1 = prompt chunk */
+    int32_t flags;                     /* Z2B_WANT_* */
+    int32_t cfg_twin;                  /* index (in this step's desc array) of the unconditional
+                                          twin for emotion CFG (src/server.cpp:1125-1142), or -1 */
+    float cfg_scale;                   /* guided = u + scale * (c - u) */
+} z2b_slot_desc;
+#define Z2B_WANT_LOGITS 1              /* compute logits of the stream's last row */
+#define Z2B_WANT_SAMPLE 3              /* logits + sample one frame with the slot's sampler */
+
+/* Load a zonos2 GGUF onto CUDA device `device`, repacking quantised weights into the
+ * kernels' tile layout. Replaces zonos2_model_load (src/zonos2.h:124, src/zonos2.cpp:15-186). */
+int z2b_model_load(const char* path, int device, z2b_model** out);
+/* Replaces zonos2_model_free (src/zonos2.h:125). */
+int z2b_model_free(z2b_model* model);
+int z2b_model_hparams(const z2b_model* model, z2b_hparams* out);
+/* Runtime expert mask: for each listed layer only the listed experts stay routable.
+ * keep_offsets has n_layers+1 entries into keep_ids; n_layers = 0 clears the mask.
+ * Replaces zonos2_set_expert_mask (src/zonos2.h:136, src/zonos2.cpp:203-239). */
+int z2b_set_expert_mask(z2b_model* model, const int32_t* layers, int n_layers,
+                        const int32_t* keep_offsets, const int32_t* keep_ids);
+
+/* Create a batch context of n_slots streams of up to slot_cap_frames rows each (rounded
+ * up to whole 256-row KV pages, allocated on demand from a shared pool).
+ * Replaces zonos2_batch_init (src/zonos2.h:279, src/zonos2-graph.cpp:639-690). */
+int z2b_ctx_create(z2b_model* model, int n_slots, int slot_cap_frames, z2b_ctx** out);
+/* Replaces zonos2_batch_free (src/zonos2.h:280). */
+int z2b_ctx_destroy(z2b_ctx* ctx);
+
+/* Admit a stream into `slot`: frees its KV pages and resets its sampler (history, RNG
+ * seeded with sp->seed). sp may be NULL for greedy. */
+int z2b_slot_reset(z2b_ctx* ctx, int slot, const z2b_sampling* sp);
+
+/* Prefill prompt rows ids[n0][10] (int32, row-major) into `slot` from position 0 and
+ * return the last row's logits [n_codebooks * audio_vocab] in out_logits.
+ * Replaces zonos2_batch_slot_prefill (src/zonos2.h:286-288, src/zonos2-graph.cpp:703-760). */
+int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* out_logits);
+
+/* One batched step over n streams: rows ids[sum(n_new)][10] are fed in desc order
+ * (decode streams feed one row; prompt chunks may be mixed in). For each desc with
+ * Z2B_WANT_SAMPLE, out_codes[i*n_codebooks ..] receives the sampled frame; with
+ * out_logits != NULL, out_logits[i*n_codebooks*audio_vocab ..] receives the logits of
+ * every desc with Z2B_WANT_LOGITS. Replaces zonos2_batch_step + zonos2_slot_sample's
+ * sampling (src/zonos2.h:294, 304-306; src/zonos2-graph.cpp:762-870). The caller keeps
+ * the per-stream state (n_past, EOS countdown) as in zonos2_slot. */
+int z2b_step(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* ids,
+             int32_t* out_codes, float* out_logits);
+
+/* Logits of desc `index` of the last step (host copy, valid until the next step).
+ * Replaces zonos2_batch_slot_logits (src/zonos2.h:298). */
+const float* z2b_step_logits(const z2b_ctx* ctx, int index);
+
+/* Device-resident decode loop for throughput runs: n_steps decode steps over the same
+ * streams, each step feeding every stream its previous sampled frame (+ text pad) and
+ * advancing n_past on the device; descs[i].n_new must be 1. Returns when all steps are
+ * enqueued (asynchronous on the context's stream). */
+int z2b_decode_loop(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps);
+/* Wait for all work on the context's stream and report device errors. */
+int z2b_sync(z2b_ctx* ctx);
+/* The context's cudaStream_t (for event timing by the caller). */
+void* z2b_ctx_stream(z2b_ctx* ctx);
+
+/* Per-step accounting: algorithmic HBM bytes the last step read/wrote (weights touched
+ * according to the actual routed experts, KV read and written, embedding rows). */
+int z2b_last_step_bytes(const z2b_ctx* ctx, uint64_t* weight_bytes, uint64_t* kv_bytes, uint64_t* other_bytes);
+/* Kernel launches issued by the last z2b_step / per decode-loop step. */
+int z2b_last_step_launches(const z2b_ctx* ctx);
+
+const char* z2b_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

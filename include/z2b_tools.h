@@ -1,0 +1,64 @@
+/* z2b_tools.h — host-side tools around the decode-step boundary.
+ *
+ * Two shared libraries export these:
+ *   libz2b_synth.so  z2b_synth_write: synthetic ZONOS2-family GGUF files (no GPU needed).
+ *                    Replaces, for benchmarks, the reference's checkpoint converters and
+ *                    dummy generator (models/convert-zonos2-to-gguf.py,
+ *                    scripts/make-dummy-model.py): same keys, tensor names and shapes.
+ *   libz2b.so        z2b_host_repack / z2b_host_unpack_tiles: the load-time weight repack
+ *                    that z2b_model_load applies before upload, callable on host memory so
+ *                    the tile layout can be checked without a GPU.
+ * All functions return 0 on success.
+ */
+#ifndef Z2B_TOOLS_H
+#define Z2B_TOOLS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Z2B_MAX_LAYERS 128
+
+/* ggml type ids accepted for matrices: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 14 Q6_K. */
+typedef struct z2b_synth_config {
+    uint32_t n_layer, n_embd, head_dim, n_head, n_head_kv, n_ff, n_expert, router_dim, n_ctx;
+    int32_t  expert_used[Z2B_MAX_LAYERS]; /* per layer: 0 = dense FFN, else MoE top-k */
+    float    rope_base, rms_eps, qk_eps, softcap;
+    uint32_t n_codebooks, codebook_size, text_vocab, spk_dim, lda_dim;
+    /* storage types by tensor class */
+    uint32_t t_attn, t_gateup, t_down, t_dense, t_head, t_embd, t_router, t_spk;
+    /* 0: every tensor N(0, std) (the reference dummy model's recipe);
+     * 1: matrices N(0, std), norm weights 1+N(0,std), |attn_temp| near 1 and router MLP
+     *    gains 1/sqrt(router_dim) so routing varies per token instead of collapsing onto
+     *    the balancing bias. */
+    uint32_t init_mode;
+    float    std;
+    uint64_t seed;
+} z2b_synth_config;
+
+/* Writes a GGUF file; on failure returns nonzero and writes a message into err. */
+int z2b_synth_write(const z2b_synth_config* cfg, const char* path, char* err, int errlen);
+
+/* Repack `rows` rows of a GGUF tensor (type, ne0 = k) into the device tile layout.
+ * dst must hold z2b_host_tiles_bytes(type, rows, k) bytes. */
+int64_t z2b_host_tiles_bytes(uint32_t type, int64_t rows, int64_t k);
+int z2b_host_repack(uint32_t type, int64_t rows, int64_t k, const void* src, void* dst);
+/* Decode a tile-layout buffer back to f32 rows [rows][k] on the host (layout check). */
+int z2b_host_unpack_tiles(uint32_t type, int64_t rows, int64_t k, const void* tiles, float* out);
+
+/* Device checks (libz2b.so, need a GPU). z2b_test_dequant decodes `rows` GGUF rows of
+ * type/k on the device to f32 [rows][k], either from the tile image the GEMV reads
+ * (from_tiles = 1) or straight from GGUF rows as the embedding gather does (0), with
+ * gguf-py's rounding order. z2b_test_gemv computes out[n][r] = sum_k W[r][k] x[n][k]
+ * for n_tok f16 activation rows with the projection-mode tile GEMV.
+ * Return 0, 4 (CUDA error), 6 (device error flag) or 7 (unsupported). */
+int z2b_test_dequant(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, int from_tiles, float* out);
+int z2b_test_gemv(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, const uint16_t* x_f16,
+                  int n_tok, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

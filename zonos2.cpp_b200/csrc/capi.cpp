@@ -1,0 +1,135 @@
+// capi.cpp — extern "C" entry points declared in include/z2b.h.
+#include "runtime.h"
+
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+using namespace z2b;
+
+struct z2b_model { Model* m; };
+struct z2b_ctx { Ctx* c; };
+
+extern "C" {
+
+int z2b_model_load(const char* path, int device, z2b_model** out) {
+    if (!path || !out) { set_error("null argument"); return Z2B_ERR_ARG; }
+    int n_dev = 0;
+    if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev == 0) { set_error("no CUDA device"); return Z2B_ERR_CUDA; }
+    if (device < 0 || device >= n_dev) { set_error("device index out of range"); return Z2B_ERR_ARG; }
+    Model* m = nullptr;
+    std::string err;
+    const int rc = model_load(path, device, &m, err);
+    if (rc) { set_error(err); return rc; }
+    *out = new (std::nothrow) z2b_model{m};
+    if (!*out) { delete m; set_error("out of host memory"); return Z2B_ERR_OOM; }
+    return Z2B_OK;
+}
+
+int z2b_model_free(z2b_model* model) {
+    if (!model) return Z2B_OK;
+    cudaSetDevice(model->m->device);
+    delete model->m;
+    delete model;
+    return Z2B_OK;
+}
+
+int z2b_model_hparams(const z2b_model* model, z2b_hparams* out) {
+    if (!model || !out) { set_error("null argument"); return Z2B_ERR_ARG; }
+    *out = model->m->hp;
+    return Z2B_OK;
+}
+
+int z2b_set_expert_mask(z2b_model* model, const int32_t* layers, int n_layers, const int32_t* keep_offsets,
+                        const int32_t* keep_ids) {
+    if (!model) { set_error("null argument"); return Z2B_ERR_ARG; }
+    Model* m = model->m;
+    cudaSetDevice(m->device);
+    for (auto& ly : m->layers) ly.small.rmask = nullptr;     // clear (buffers stay owned by the model)
+    for (int i = 0; i < n_layers; ++i) {
+        const int L = layers[i];
+        if (L < 0 || L >= (int)m->layers.size() || !m->layers[L].is_moe) continue;
+        const int E = m->layers[L].n_expert;
+        std::vector<float> h(E, -INFINITY);
+        for (int j = keep_offsets[i]; j < keep_offsets[i + 1]; ++j)
+            if (keep_ids[j] >= 0 && keep_ids[j] < E) h[keep_ids[j]] = 0.0f;
+        float* d = nullptr;
+        if (cudaMalloc(&d, E * 4) != cudaSuccess) { set_error("cudaMalloc failed"); return Z2B_ERR_OOM; }
+        m->allocs.push_back(d);
+        cudaMemcpy(d, h.data(), E * 4, cudaMemcpyHostToDevice);
+        m->layers[L].small.rmask = d;
+    }
+    return Z2B_OK;
+}
+
+int z2b_ctx_create(z2b_model* model, int n_slots, int slot_cap_frames, z2b_ctx** out) {
+    if (!model || !out) { set_error("null argument"); return Z2B_ERR_ARG; }
+    Ctx* c = nullptr;
+    const int rc = ctx_create(model->m, n_slots, slot_cap_frames, &c);
+    if (rc) return rc;
+    const char* ng = std::getenv("Z2B_NO_GRAPH");
+    c->graphs_enabled = !(ng && ng[0] == '1');
+    *out = new z2b_ctx{c};
+    return Z2B_OK;
+}
+
+int z2b_ctx_destroy(z2b_ctx* ctx) {
+    if (!ctx) return Z2B_OK;
+    cudaSetDevice(ctx->c->m->device);
+    delete ctx->c;
+    delete ctx;
+    return Z2B_OK;
+}
+
+int z2b_slot_reset(z2b_ctx* ctx, int slot, const z2b_sampling* sp) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_slot_reset(ctx->c, slot, sp);
+}
+
+int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* out_logits) {
+    if (!ctx || !ids) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_prefill(ctx->c, slot, ids, n0, out_logits);
+}
+
+int z2b_step(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes,
+             float* out_logits) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_step(ctx->c, descs, n, ids, out_codes, out_logits);
+}
+
+const float* z2b_step_logits(const z2b_ctx* ctx, int index) {
+    if (!ctx || index < 0 || index >= (int)ctx->c->step_has_logits.size() || !ctx->c->step_has_logits[index]) return nullptr;
+    const Dims& D = ctx->c->m->dims;
+    return ctx->c->step_logits.data() + (size_t)index * D.n_codebooks * D.audio_vocab;
+}
+
+int z2b_decode_loop(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_decode_loop(ctx->c, descs, n, first_ids, n_steps);
+}
+
+int z2b_sync(z2b_ctx* ctx) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_sync(ctx->c);
+}
+
+void* z2b_ctx_stream(z2b_ctx* ctx) { return ctx ? (void*)ctx->c->stream : nullptr; }
+
+int z2b_last_step_bytes(const z2b_ctx* ctx, uint64_t* weight_bytes, uint64_t* kv_bytes, uint64_t* other_bytes) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    if (weight_bytes) *weight_bytes = ctx->c->last_wbytes;
+    if (kv_bytes) *kv_bytes = ctx->c->last_kvbytes;
+    if (other_bytes) *other_bytes = ctx->c->last_other;
+    return Z2B_OK;
+}
+
+int z2b_last_step_launches(const z2b_ctx* ctx) { return ctx ? ctx->c->launches : -1; }
+
+const char* z2b_last_error(void) { return last_error(); }
+
+}  // extern "C"

@@ -1,0 +1,335 @@
+// k_attn.cu — QK-norm + RoPE + paged KV append, split-K paged GQA decode attention and
+// the split combine with the per-head sigmoid gate (sm_100a).
+//
+// Reference: build_attention (src/zonos2-graph.cpp:101-176): q,k RMSNorm over head_dim
+// (eps qk_norm_eps), q *= |temp|, interleaved RoPE (GGML_ROPE_TYPE_NORMAL), K/V stored
+// f16 after RoPE at each token's cache position, attention of each token over its own
+// slot's positions [0, pos] with scale 1/sqrt(head_dim), output * sigmoid(gate).
+//
+// KV page layout (KVDev): per (page, layer, kv head) a K block [256 keys][hd] whose
+// 16-byte chunks are XOR-swizzled by key, and a V block stored transposed per 64 keys
+// ([4][hd][64], chunks swizzled by dim). A 64-key slice of either is one contiguous
+// bulk copy, and every mma operand below is a conflict-free 8-byte shared load:
+//   S   = Q K^T   (m = heads of the GQA group, n = 8 keys, k = head_dim, dims permuted
+//                  so lane quad q owns a contiguous quarter of head_dim)
+//   O^T = V^T P^T (m = 16 dims, n = heads, k = 16 keys); the S accumulator of lane
+//                  (head r, quad q) is exactly its P^T B-fragment when S column n holds
+//                  key 4*(n/2) + n%2 (+2 for the second n-tile).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace z2b {
+
+namespace {
+
+constexpr int KCH = 64;          // keys per staged chunk
+
+template <int HD> __device__ __forceinline__ int kswz(int key) {   // K row chunk swizzle
+    constexpr int C = HD / 8;
+    if constexpr (C >= 8) return key & 7;
+    else return (key / (8 / C)) & (C - 1);
+}
+
+// ---------------------------------------------------------------- rope + append
+template <int HD>
+__global__ void rope_append_kernel(const StepBufs b, const KVDev kv, const float* __restrict__ temp,
+                                   const Dims dm, int layer) {
+    const int t = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int slot = b.tok_slot[t];
+    if (slot < 0) return;
+    const int pos = b.tok_pos[t], nh = dm.n_head, nkv = dm.n_head_kv;
+    const float* row = b.qkvg + (size_t)t * b.ldq;
+    const int pg = pos / PAGE, j = pos % PAGE;
+    int page = -1;
+    if (pg < kv.max_pages) page = kv.page_table[(size_t)slot * kv.max_pages + pg];
+    if (page < 0) { if (threadIdx.x == 0) atomicOr(b.err, (uint32_t)DERR_PAGE); return; }
+    __half* lbase = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
+    const float ts = powf(dm.rope_base, -2.0f / (float)HD);
+    // heads: [0, nh) q, [nh, nh+nkv) k, [nh+nkv, nh+2nkv) v
+    for (int h = w; h < nh + 2 * nkv; h += nw) {
+        const bool isq = h < nh, isk = !isq && h < nh + nkv;
+        const float* x = row + (size_t)h * HD;       // q | k | v are contiguous in qkvg
+        if (isq || isk) {
+            float ss = 0.0f;
+            for (int i = lane; i < HD; i += 32) ss += x[i] * x[i];
+            ss = warp_sum(ss);
+            const float sc = 1.0f / sqrtf(ss / (float)HD + dm.qk_eps);
+            const float tm = isq ? temp[h] : 1.0f;
+            for (int i = lane; i < HD / 2; i += 32) {
+                float x0 = x[2 * i] * sc, x1 = x[2 * i + 1] * sc;
+                if (isq) { x0 = x0 * tm; x1 = x1 * tm; }
+                float theta = (float)pos;                     // ggml rope cache: theta *= theta_scale
+                for (int k = 0; k < i; ++k) theta *= ts;
+                const float c = cosf(theta), s = sinf(theta);
+                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+                if (isq) {
+                    __half2* q = (__half2*)(b.qh + ((size_t)t * nh + h) * HD);
+                    q[i] = __floats2half2_rn(y0, y1);
+                } else {
+                    __half* kb = lbase + (size_t)(h - nh) * kv.head_elems + (size_t)j * HD;
+                    const int e = 2 * i, c16 = e / 8;
+                    __half2* dst = (__half2*)(kb + ((c16 ^ kswz<HD>(j)) * 8 + (e % 8)));
+                    *dst = __floats2half2_rn(y0, y1);
+                }
+            }
+        } else {
+            const int hv = h - nh - nkv;
+            __half* vb = lbase + (size_t)(nkv + hv) * kv.head_elems + (size_t)(j / KCH) * HD * KCH;
+            const int col = j % KCH;
+            for (int i = lane; i < HD; i += 32)
+                vb[(size_t)i * KCH + (((col / 8) ^ (i & 7)) * 8) + (col % 8)] = __float2half_rn(x[i]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- attention
+template <int HD>
+struct AttnSmem {
+    static constexpr int CHUNK_BYTES = KCH * HD * 2;          // one K or V slice
+    static constexpr int NS = HD >= 128 ? 3 : 4;
+    static constexpr int STAGE = 2 * CHUNK_BYTES;
+    static constexpr int MERGE = 4 * 8 * (HD + 2) * 4;        // [warp][head][m, l, o]
+    static constexpr int BYTES = 128 + NS * STAGE + MERGE;
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev kv, const Dims dm,
+                                                   int layer, int split_keys) {
+    using SM = AttnSmem<HD>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    uint8_t* stages = smem + 128;
+    float* merge = reinterpret_cast<float*>(stages + SM::NS * SM::STAGE);
+    const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
+    const int slot = b.tok_slot[t];
+    if (slot < 0) return;
+    const int pos = b.tok_pos[t], n_keys = pos + 1;
+    const int key0 = sp * split_keys;
+    if (key0 >= n_keys) return;
+    const int key1 = min(n_keys, key0 + split_keys);
+    const int nchunks = (key1 - key0 + KCH - 1) / KCH;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r = lane >> 2, q = lane & 3;
+    const int nh = dm.n_head;
+    constexpr int KST = HD / 16;                 // k-steps over head_dim, also m-tiles of O^T
+    constexpr int QO = HD / 4;                   // dims owned by a lane quad
+
+    // page pointers for every chunk are looked up by the issuing thread
+    auto chunk_src = [&](int c, const __half** kp, const __half** vp) -> bool {
+        const int key = key0 + c * KCH, pg = key / PAGE;
+        const int page = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
+        if (page < 0) return false;
+        const __half* lb = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
+        *kp = lb + (size_t)hk * kv.head_elems + (size_t)(key % PAGE) * HD;
+        *vp = lb + (size_t)(dm.n_head_kv + hk) * kv.head_elems + (size_t)((key % PAGE) / KCH) * HD * KCH;
+        return true;
+    };
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) {
+        s_bad = 0;
+        for (int s = 0; s < SM::NS; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto issue = [&](int c) {
+        const __half *kp, *vp;
+        uint8_t* st = stages + (c % SM::NS) * SM::STAGE;
+        if (!chunk_src(c, &kp, &vp)) {           // no page: record, arrive without data
+            atomicOr(b.err, (uint32_t)DERR_PAGE);
+            s_bad = 1;
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(&bars[c % SM::NS])) : "memory");
+            return;
+        }
+        mbar_expect_tx(&bars[c % SM::NS], 2 * SM::CHUNK_BYTES);
+        bulk_g2s(st, kp, SM::CHUNK_BYTES, &bars[c % SM::NS]);
+        bulk_g2s(st + SM::CHUNK_BYTES, vp, SM::CHUNK_BYTES, &bars[c % SM::NS]);
+    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < SM::NS && c < nchunks; ++c) issue(c);
+
+    // Q fragments: head r of the group (rows >= G are zero), dims QO*q + 4s + {0..3}
+    uint32_t qa[KST][2];
+    {
+        const bool ok = r < G;
+        const __half* qrow = b.qh + ((size_t)t * nh + hk * G + (ok ? r : 0)) * HD + QO * q;
+#pragma unroll
+        for (int s = 0; s < KST; ++s) {
+            uint2 v = ok ? *(const uint2*)(qrow + 4 * s) : make_uint2(0u, 0u);
+            qa[s][0] = v.x; qa[s][1] = v.y;
+        }
+    }
+    const float scale = 1.0f / sqrtf((float)HD);
+    float m_run = -INFINITY, l_run = 0.0f;       // for head r (quad-uniform)
+    float acc[KST][4];                           // O^T: dims mt*16 + r (+8), heads 2q, 2q+1
+#pragma unroll
+    for (int i = 0; i < KST; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+    bool failed = false;
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int slotc = c % SM::NS;
+        if (!failed) failed = !mbar_wait(&bars[slotc], (uint32_t)((c / SM::NS) & 1), b.err);
+        const uint8_t* Ks = stages + slotc * SM::STAGE;
+        const uint8_t* Vs = Ks + SM::CHUNK_BYTES;
+        const int kb = 16 * warp;                 // this warp's keys within the chunk
+        const int kglob = key0 + c * KCH + kb;
+        if (!failed && !s_bad && kglob < key1) {
+            float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+            const int n = r;                      // B column of this lane
+            const int key_a = kb + 4 * (n >> 1) + (n & 1), key_b = key_a + 2;
+#pragma unroll
+            for (int s = 0; s < KST; ++s) {
+                const int e = QO * q + 4 * s, ch = e / 8, off = (e % 8) * 2;
+                const uint2 ka = *(const uint2*)(Ks + key_a * HD * 2 + ((ch ^ kswz<HD>(key_a)) * 16) + off);
+                const uint2 kbv = *(const uint2*)(Ks + key_b * HD * 2 + ((ch ^ kswz<HD>(key_b)) * 16) + off);
+                mma16816(s0, qa[s][0], 0u, qa[s][1], 0u, ka.x, ka.y);
+                mma16816(s1, qa[s][0], 0u, qa[s][1], 0u, kbv.x, kbv.y);
+            }
+            // lane holds head r, keys kb + 4q + {0, 1} (s0[0..1]) and {2, 3} (s1[0..1])
+            float sv[4] = {s0[0] * scale, s0[1] * scale, s1[0] * scale, s1[1] * scale};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) if (kglob + 4 * q + i >= key1) sv[i] = -INFINITY;
+            float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+            float p[4], ps = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { p[i] = (sv[i] == -INFINITY) ? 0.0f : expf(sv[i] - m_new); ps += p[i]; }
+            l_run = l_run * alpha + ps;
+            m_run = m_new;
+            // rescale O^T columns (heads 2q, 2q+1) by those heads' alpha
+            const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * q) * 4);
+            const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * q + 1) * 4);
+            const uint32_t pb0 = h2u(__floats2half2_rn(p[0], p[1]));
+            const uint32_t pb1 = h2u(__floats2half2_rn(p[2], p[3]));
+#pragma unroll
+            for (int mt = 0; mt < KST; ++mt) {
+                acc[mt][0] *= a0; acc[mt][1] *= a1; acc[mt][2] *= a0; acc[mt][3] *= a1;
+                const int d0 = mt * 16 + r, d1 = d0 + 8;
+                const int colc = (kb + 4 * q) / 8, coff = ((kb + 4 * q) % 8) * 2;
+                const uint2 v0 = *(const uint2*)(Vs + d0 * KCH * 2 + ((colc ^ (d0 & 7)) * 16) + coff);
+                const uint2 v1 = *(const uint2*)(Vs + d1 * KCH * 2 + ((colc ^ (d1 & 7)) * 16) + coff);
+                mma16816(acc[mt], v0.x, v1.x, v0.y, v1.y, pb0, pb1);
+            }
+        }
+        __syncthreads();                         // stage consumed by all warps
+        if (threadIdx.x == 0 && !failed && c + SM::NS < nchunks) { fence_proxy_async(); issue(c + SM::NS); }
+    }
+    // per-warp state -> shared, merged over warps in a fixed order
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    float* mw = merge + (size_t)warp * 8 * (HD + 2);
+    if (q == 0 && r < G) { mw[r * (HD + 2)] = m_run; mw[r * (HD + 2) + 1] = l_run; }
+#pragma unroll
+    for (int mt = 0; mt < KST; ++mt) {
+        const int d0 = mt * 16 + r;
+        if (2 * q < G) { mw[(2 * q) * (HD + 2) + 2 + d0] = acc[mt][0]; mw[(2 * q) * (HD + 2) + 2 + d0 + 8] = acc[mt][2]; }
+        if (2 * q + 1 < G) { mw[(2 * q + 1) * (HD + 2) + 2 + d0] = acc[mt][1]; mw[(2 * q + 1) * (HD + 2) + 2 + d0 + 8] = acc[mt][3]; }
+    }
+    __syncthreads();
+    const int max_split = b.max_split;
+    for (int idx = threadIdx.x; idx < G * (HD + 2); idx += blockDim.x) {
+        const int g = idx / (HD + 2), e = idx % (HD + 2);
+        float M = -INFINITY;
+        for (int w2 = 0; w2 < 4; ++w2) M = fmaxf(M, merge[(size_t)w2 * 8 * (HD + 2) + g * (HD + 2)]);
+        float v = 0.0f;
+        if (e == 0) v = M;
+        else {
+            for (int w2 = 0; w2 < 4; ++w2) {
+                const float* mm = merge + (size_t)w2 * 8 * (HD + 2) + g * (HD + 2);
+                if (mm[0] == -INFINITY) continue;
+                v += expf(mm[0] - M) * mm[e];
+            }
+        }
+        b.apart[(((size_t)t * nh + hk * G + g) * max_split + sp) * (HD + 2) + e] = v;
+    }
+    if (failed) {
+        for (int c = 0; c < SM::NS; ++c) (void)mbar_try_wait(&bars[c], 0);
+    }
+}
+
+// ---------------------------------------------------------------- split combine + gate
+template <int HD>
+__global__ void attn_combine_kernel(const StepBufs b, const Dims dm, int split_keys) {
+    const int t = blockIdx.x, nh = dm.n_head;
+    const int slot = b.tok_slot[t];
+    const int gate_off = nh * HD + 2 * dm.n_head_kv * HD;
+    for (int idx = threadIdx.x; idx < nh * HD; idx += blockDim.x) {
+        const int h = idx / HD, e = idx % HD;
+        float out = 0.0f;
+        if (slot >= 0) {
+            const int ns = (b.tok_pos[t] + 1 + split_keys - 1) / split_keys;
+            const float* base = b.apart + ((size_t)t * nh + h) * b.max_split * (HD + 2);
+            float M = -INFINITY;
+            for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(size_t)s * (HD + 2)]);
+            float L = 0.0f, O = 0.0f;
+            for (int s = 0; s < ns; ++s) {
+                const float* ps = base + (size_t)s * (HD + 2);
+                if (ps[0] == -INFINITY) continue;
+                const float f = expf(ps[0] - M);
+                L += f * ps[1];
+                O += f * ps[2 + e];
+            }
+            const float g = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
+            out = (O / L) * g;
+        }
+        b.o[(size_t)t * nh * HD + idx] = __float2half_rn(out);
+    }
+}
+
+template <int HD, int G>
+void attn_launch_hg(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys,
+                    int max_split, cudaStream_t s) {
+    using SM = AttnSmem<HD>;
+    cudaFuncSetAttribute(attn_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
+    dim3 grid(T, d.n_head_kv, max_split);
+    attn_kernel<HD, G><<<grid, 128, SM::BYTES, s>>>(b, kv, d, layer, split_keys);
+}
+
+template <int HD>
+void attn_launch_h(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys,
+                   int max_split, cudaStream_t s) {
+    const int G = d.n_head / d.n_head_kv;
+    switch (G) {
+        case 1: attn_launch_hg<HD, 1>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        case 2: attn_launch_hg<HD, 2>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        case 4: attn_launch_hg<HD, 4>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        default: attn_launch_hg<HD, 8>(b, kv, d, layer, T, split_keys, max_split, s); break;
+    }
+}
+
+}  // namespace
+
+void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T,
+                        cudaStream_t s) {
+    switch (d.head_dim) {
+        case 16: rope_append_kernel<16><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
+        case 32: rope_append_kernel<32><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
+        case 64: rope_append_kernel<64><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
+        default: rope_append_kernel<128><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
+    }
+}
+
+void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys,
+                      int max_split, cudaStream_t s) {
+    switch (d.head_dim) {
+        case 16: attn_launch_h<16>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        case 32: attn_launch_h<32>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        case 64: attn_launch_h<64>(b, kv, d, layer, T, split_keys, max_split, s); break;
+        default: attn_launch_h<128>(b, kv, d, layer, T, split_keys, max_split, s); break;
+    }
+}
+
+void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s) {
+    (void)max_split;
+    switch (d.head_dim) {
+        case 16: attn_combine_kernel<16><<<T, 256, 0, s>>>(b, d, split_keys); break;
+        case 32: attn_combine_kernel<32><<<T, 256, 0, s>>>(b, d, split_keys); break;
+        case 64: attn_combine_kernel<64><<<T, 256, 0, s>>>(b, d, split_keys); break;
+        default: attn_combine_kernel<128><<<T, 256, 0, s>>>(b, d, split_keys); break;
+    }
+}
+
+}  // namespace z2b

@@ -1,0 +1,398 @@
+// k_gemv.cu — tile GEMV for the decode step (sm_100a).
+//
+// Replaces ggml_mul_mat / ggml_mul_mat_id on quantised weights
+// (src/zonos2-graph.cpp:107-111, 175, 181-184, 223-231, 357): the attention and head
+// projections over all tokens of the step, and the grouped expert gate/up (+SwiGLU) and
+// down (x route probability) passes over the tokens routed to each active expert.
+//
+// Work item = (matrix or expert, row-tile of 16 output rows). A CTA owns a contiguous
+// run of items; its warps split each item's K range. Each warp streams its K-slice of
+// every item through a private ring of shared-memory stages filled by one-lane
+// cp.async.bulk copies (no multicast), decodes the quantised weights in registers
+// straight into mma.sync.m16n8k16 A fragments (tile_layout.h), multiplies them with the
+// activation fragments (f16, 8 tokens per n-tile) and accumulates in f32. Partial sums
+// are reduced across warps in shared memory in a fixed order, so results do not depend
+// on timing, on the other tokens of the batch or on the grid size.
+#include "common.cuh"
+#include "gguf.h"
+#include "kernels.h"
+#include "tile_layout.h"
+
+#include <algorithm>
+
+namespace z2b {
+
+namespace {
+
+constexpr int NTG = 2;       // n-tiles (8 tokens each) per pass over a staged item
+constexpr int MAXKS = 16;    // k-steps per warp per item (register budget for B)
+
+__device__ __forceinline__ __half2 hc(uint16_t bits) { return __half2half2(__ushort_as_half(bits)); }
+
+template <int N> __device__ __forceinline__ uint32_t shr_signed(uint32_t x) {
+    if constexpr (N >= 0) return x >> N; else return x << (-N);
+}
+
+// ---- per-type decoders: prep() reads the chunk's scales, frag() builds A for k-step S ----
+template <int WT> struct Dec;
+
+template <> struct Dec<GT_Q4_K> {
+    static constexpr int KS = 16, KC = 256;
+    __half2 S[2][2], M[2][2];                 // [sub-block 0/1][row r / r+8], M holds -min
+    __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
+        const int r = lane >> 2, q = lane & 3;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 hd = *(const uint4*)(T + (r + 8 * h) * 16);
+            const float d = __half2float(__ushort_as_half((uint16_t)(hd.x & 0xffff)));
+            const float dm = __half2float(__ushort_as_half((uint16_t)(hd.x >> 16)));
+            uint32_t f;
+            if (q == 0) f = hd.y;
+            else if (q == 1) f = __funnelshift_r(hd.y, hd.z, 24);
+            else if (q == 2) f = __funnelshift_r(hd.z, hd.w, 16);
+            else f = hd.w >> 8;
+            S[0][h] = __float2half2_rn(d * (float)(f & 63));
+            S[1][h] = __float2half2_rn(d * (float)((f >> 6) & 63));
+            M[0][h] = __float2half2_rn(-(dm * (float)((f >> 12) & 63)));
+            M[1][h] = __float2half2_rn(-(dm * (float)((f >> 18) & 63)));
+        }
+    }
+    template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
+        const uint4 w = *(const uint4*)(T + Q4K_HDR + ((s >> 2) * 32 + lane) * 16);
+        uint32_t v0 = (s & 2) ? w.y : w.x, v1 = (s & 2) ? w.w : w.z;
+        if (s & 1) { v0 >>= 8; v1 >>= 8; }
+        constexpr int sb = s >> 3;
+        const __half2 k1024 = hc(0x6400), k16 = hc(0x2C00), km64 = hc(0xD400);
+        a[0] = h2u(__hfma2(__hsub2(u2h(lop3_and_or(v0, 0x000F000Fu, 0x64006400u)), k1024), S[sb][0], M[sb][0]));
+        a[1] = h2u(__hfma2(__hsub2(u2h(lop3_and_or(v1, 0x000F000Fu, 0x64006400u)), k1024), S[sb][1], M[sb][1]));
+        a[2] = h2u(__hfma2(__hfma2(u2h(lop3_and_or(v0, 0x00F000F0u, 0x64006400u)), k16, km64), S[sb][0], M[sb][0]));
+        a[3] = h2u(__hfma2(__hfma2(u2h(lop3_and_or(v1, 0x00F000F0u, 0x64006400u)), k16, km64), S[sb][1], M[sb][1]));
+    }
+};
+
+template <> struct Dec<GT_Q6_K> {
+    static constexpr int KS = 16, KC = 256;
+    __half2 S[4][2];
+    __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
+        const int r = lane >> 2, q = lane & 3;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t sc = *(const uint32_t*)(T + (r + 8 * h) * 16 + 4 * q);
+            const float d = __half2float(*(const __half*)(T + 256 + 2 * (r + 8 * h)));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) S[j][h] = __float2half2_rn(d * (float)(int8_t)(sc >> (8 * j)));
+        }
+    }
+    template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
+        const uint4 w = *(const uint4*)(T + Q6K_HDR + ((s >> 2) * 32 + lane) * 16);
+        const uint4 hv = *(const uint4*)(T + Q6K_HDR + Q6K_LO + ((s >> 3) * 32 + lane) * 16);
+        uint32_t v0 = (s & 2) ? w.y : w.x, v1 = (s & 2) ? w.w : w.z;
+        if (s & 1) { v0 >>= 8; v1 >>= 8; }
+        const uint32_t h0 = ((s >> 2) & 1) ? hv.y : hv.x, h1 = ((s >> 2) & 1) ? hv.w : hv.z;
+        constexpr int j4 = s & 3, j = s >> 2;
+        const __half2 k1056 = hc(0x6420), k16 = hc(0x2C00), km96 = hc(0xD600);
+        const uint32_t x0 = lop3_and_or(shr_signed<4 * j4 - 4>(h0), 0x00300030u, lop3_and_or(v0, 0x000F000Fu, 0x64006400u));
+        const uint32_t x1 = lop3_and_or(shr_signed<4 * j4 - 4>(h1), 0x00300030u, lop3_and_or(v1, 0x000F000Fu, 0x64006400u));
+        const uint32_t y0 = lop3_and_or(shr_signed<4 * j4 - 6>(h0), 0x03000300u, lop3_and_or(v0, 0x00F000F0u, 0x64006400u));
+        const uint32_t y1 = lop3_and_or(shr_signed<4 * j4 - 6>(h1), 0x03000300u, lop3_and_or(v1, 0x00F000F0u, 0x64006400u));
+        a[0] = h2u(__hmul2(__hsub2(u2h(x0), k1056), S[j][0]));
+        a[1] = h2u(__hmul2(__hsub2(u2h(x1), k1056), S[j][1]));
+        a[2] = h2u(__hmul2(__hfma2(u2h(y0), k16, km96), S[j][0]));
+        a[3] = h2u(__hmul2(__hfma2(u2h(y1), k16, km96), S[j][1]));
+    }
+};
+
+template <> struct Dec<GT_Q8_0> {
+    static constexpr int KS = 8, KC = 128;
+    __half2 D[2];
+    __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
+        const int r = lane >> 2, q = lane & 3;
+        D[0] = __half2half2(*(const __half*)(T + (r * 4 + q) * 2));
+        D[1] = __half2half2(*(const __half*)(T + ((r + 8) * 4 + q) * 2));
+    }
+    template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
+        const uint4 w = *(const uint4*)(T + Q80_HDR + ((s >> 1) * 32 + lane) * 16);
+        const uint32_t v0 = (s & 1) ? w.y : w.x, v1 = (s & 1) ? w.w : w.z;
+        const __half2 k1152 = hc(0x6480);
+        a[0] = h2u(__hmul2(__hsub2(u2h(prmt(v0, 0x64646464u, 0x4140u)), k1152), D[0]));
+        a[1] = h2u(__hmul2(__hsub2(u2h(prmt(v1, 0x64646464u, 0x4140u)), k1152), D[1]));
+        a[2] = h2u(__hmul2(__hsub2(u2h(prmt(v0, 0x64646464u, 0x4342u)), k1152), D[0]));
+        a[3] = h2u(__hmul2(__hsub2(u2h(prmt(v1, 0x64646464u, 0x4342u)), k1152), D[1]));
+    }
+};
+
+// F16 with KS k-steps per chunk (KS = 4, 2, 1)
+template <int KS_> struct DecF16 {
+    static constexpr int KS = KS_, KC = 16 * KS_;
+    __device__ __forceinline__ void prep(const uint8_t*, int) {}
+    template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
+        const uint4 w = *(const uint4*)(T + (s * 32 + lane) * 16);
+        a[0] = w.x; a[1] = w.z; a[2] = w.y; a[3] = w.w;
+    }
+};
+
+template <int WT, int KSF> struct DecSel { using T = Dec<WT>; };
+template <int KSF> struct DecSel<GT_F16, KSF> { using T = DecF16<KSF>; };
+
+// unrolled k-step loop
+template <class D, int s, int KS> struct KLoop {
+    template <int NMAT>
+    __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, int kbase,
+                                               const uint32_t (&B)[NTG][MAXKS][2], float (&acc)[NMAT][NTG][4],
+                                               int m, int ntv) {
+        uint32_t a[4];
+        dec.template frag<s>(T, lane, a);
+#pragma unroll
+        for (int nt = 0; nt < NTG; ++nt)
+            if (nt < ntv) mma16816(acc[m][nt], a[0], a[1], a[2], a[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
+        KLoop<D, s + 1, KS>::template run<NMAT>(dec, T, lane, kbase, B, acc, m, ntv);
+    }
+};
+template <class D, int KS> struct KLoop<D, KS, KS> {
+    template <int NMAT>
+    __device__ __forceinline__ static void run(const D&, const uint8_t*, int, int, const uint32_t (&)[NTG][MAXKS][2],
+                                               float (&)[NMAT][NTG][4], int, int) {}
+};
+
+struct ItemRef { int expert; int seg; int rt; const uint8_t* src[2]; int n_tok; int tok0; };
+
+template <int MODE>
+__device__ __forceinline__ ItemRef item_ref(const GemvParams& p, int item, int c0) {
+    ItemRef r{};
+    if constexpr (MODE == GM_PROJ) {
+        int s = 0, base = 0;
+        while (s + 1 < p.n_seg && item >= base + p.seg[s].n_row_tiles) { base += p.seg[s].n_row_tiles; ++s; }
+        r.seg = s; r.rt = item - base; r.expert = -1;
+        r.src[0] = p.seg[s].tiles + ((size_t)r.rt * p.chunks + c0) * p.tile_bytes;
+        r.src[1] = nullptr;
+        r.n_tok = p.T; r.tok0 = 0;
+    } else {
+        const int a = item / p.n_row_tiles;
+        r.rt = item % p.n_row_tiles;
+        r.expert = p.active[a];
+        r.seg = 0;
+        const size_t off = (size_t)r.expert * p.expert_stride + ((size_t)r.rt * p.chunks + c0) * p.tile_bytes;
+        r.src[0] = p.w0 + off;
+        r.src[1] = (MODE == GM_GATEUP) ? p.w1 + off : nullptr;
+        r.tok0 = p.seg_off[r.expert];
+        r.n_tok = p.seg_off[r.expert + 1] - r.tok0;
+    }
+    return r;
+}
+
+template <int MODE>
+__device__ __forceinline__ int x_row(const GemvParams& p, const ItemRef& it, int n) {
+    if constexpr (MODE == GM_PROJ) return n;
+    else if constexpr (MODE == GM_GATEUP) return p.route_tok[it.tok0 + n];
+    else return it.tok0 + n;
+}
+
+template <int WT, int KSF, int MODE>
+__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
+    using D = typename DecSel<WT, KSF>::T;
+    constexpr int KS = D::KS, KC = D::KC;
+    constexpr int NMAT = (MODE == GM_GATEUP) ? 2 : 1;
+    constexpr int MAXCPW = MAXKS / KS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, NW = blockDim.x >> 5;
+    const int q = lane & 3, r8 = lane >> 2;
+    const int NS = p.n_stages;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                         // [NW][NS]
+    uint8_t* stages = smem + 128 * ((NW * NS * 8 + 127) / 128);                  // [NW][NS][stage_bytes]
+    float* red = reinterpret_cast<float*>(stages + (size_t)NW * NS * p.stage_bytes);   // [NW][NMAT][NTG][32][4]
+    uint64_t* mybar = bars + warp * NS;
+    uint8_t* mystage = stages + (size_t)warp * NS * p.stage_bytes;
+
+    const int c0 = warp * p.chunks / NW, c1 = (warp + 1) * p.chunks / NW, ncw = c1 - c0;
+    const uint32_t wbytes = (uint32_t)(ncw * p.tile_bytes);
+
+    int n_items;
+    if constexpr (MODE == GM_PROJ) n_items = p.total_items;
+    else n_items = (*p.n_active) * p.n_row_tiles;
+    const int it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
+    const int it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
+    if (it0 >= it1) return;
+
+    if (lane == 0)
+        for (int s = 0; s < NS; ++s) mbar_init(&mybar[s], 1);
+    fence_mbar_init();
+    __syncwarp();
+
+    int issued_upto = it0 - 1;                   // last item whose copy was issued
+    auto issue = [&](int item, int slot) {
+        issued_upto = item;
+        if (lane == 0 && ncw > 0) {
+            const ItemRef it = item_ref<MODE>(p, item, c0);
+            mbar_expect_tx(&mybar[slot], wbytes * NMAT);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+                bulk_g2s(mystage + slot * p.stage_bytes + m * wbytes, it.src[m], wbytes, &mybar[slot]);
+        }
+    };
+    for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
+
+    bool failed = false;
+    uint32_t B[NTG][MAXKS][2];
+    for (int item = it0; item < it1; ++item) {
+        const int j = item - it0, slot = j % NS;
+        const uint32_t parity = (uint32_t)((j / NS) & 1);
+        const ItemRef it = item_ref<MODE>(p, item, c0);
+        if (!failed && ncw > 0 && item <= issued_upto) failed = !mbar_wait(&mybar[slot], parity, p.err);
+        const int waited = item;
+        const uint8_t* st = mystage + slot * p.stage_bytes;
+        const int n_groups = (it.n_tok + 8 * NTG - 1) / (8 * NTG);
+        for (int g = 0; g < n_groups; ++g) {
+            const int ntv = min(NTG, (it.n_tok - g * 8 * NTG + 7) / 8);
+            float acc[NMAT][NTG][4];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int nt = 0; nt < NTG; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[m][nt][e] = 0.0f;
+            if (!failed && ncw > 0) {
+                // activation fragments: token n = lane/4 of each n-tile, k = chunk*KC + q*KC/4 + 4s
+#pragma unroll
+                for (int nt = 0; nt < NTG; ++nt) {
+                    const int n = g * 8 * NTG + nt * 8 + r8;
+                    const bool ok = nt < ntv && n < it.n_tok;
+                    const __half* xr = ok ? p.X + (size_t)x_row<MODE>(p, it, n) * p.ldx : nullptr;
+#pragma unroll
+                    for (int cc = 0; cc < MAXCPW; ++cc)
+#pragma unroll
+                        for (int s = 0; s < KS; ++s) {
+                            uint2 v = make_uint2(0u, 0u);
+                            if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
+                            B[nt][cc * KS + s][0] = v.x;
+                            B[nt][cc * KS + s][1] = v.y;
+                        }
+                }
+#pragma unroll
+                for (int cc = 0; cc < MAXCPW; ++cc) {
+                    if (cc < ncw) {
+#pragma unroll
+                        for (int m = 0; m < NMAT; ++m) {
+                            const uint8_t* T = st + m * wbytes + cc * p.tile_bytes;
+                            D dec;
+                            dec.prep(T, lane);
+                            KLoop<D, 0, KS>::template run<NMAT>(dec, T, lane, cc * KS, B, acc, m, ntv);
+                        }
+                    }
+                }
+            }
+            if (g == n_groups - 1) {                 // stage fully consumed: refill it
+                __syncwarp();
+                fence_proxy_async();
+                if (!failed && item + NS < it1) issue(item + NS, slot);
+            }
+            // cross-warp reduction in a fixed order
+            float* myred = red + (size_t)warp * NMAT * NTG * 128;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+                for (int nt = 0; nt < NTG; ++nt)
+                    *(float4*)(myred + ((m * NTG + nt) * 32 + lane) * 4) =
+                        make_float4(acc[m][nt][0], acc[m][nt][1], acc[m][nt][2], acc[m][nt][3]);
+            __syncthreads();
+            for (int t = threadIdx.x; t < NTG * 128; t += blockDim.x) {
+                const int nt = t >> 7, ln = (t & 127) >> 2, e = t & 3;
+                const int rr = (ln >> 2) + 8 * (e >> 1);
+                const int n = g * 8 * NTG + nt * 8 + 2 * (ln & 3) + (e & 1);
+                if (n >= it.n_tok) continue;
+                float v[NMAT];
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    float s = 0.0f;
+                    for (int w = 0; w < NW; ++w) s += red[(((size_t)w * NMAT + m) * NTG + nt) * 128 + ln * 4 + e];
+                    v[m] = s;
+                }
+                if constexpr (MODE == GM_PROJ) {
+                    const ProjSeg& sg = p.seg[it.seg];
+                    const int row = it.rt * 16 + rr;
+                    if (row < sg.rows) {
+                        float* o = p.out + (size_t)n * p.ldo + sg.out_off + row;
+                        if (p.epi == EPI_ADD) *o = v[0] + *o;
+                        else if (p.epi == EPI_SOFTCAP) *o = tanhf(v[0] * (1.0f / p.cap)) * p.cap;
+                        else *o = v[0];
+                    }
+                } else if constexpr (MODE == GM_GATEUP) {
+                    const int row = it.rt * 16 + rr;
+                    if (row < p.out_rows) {
+                        const float gt = v[0], up = v[1];
+                        const float si = gt / (1.0f + expf(-gt));
+                        p.yout[(size_t)(it.tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
+                    }
+                } else {
+                    const int row = it.rt * 16 + rr;
+                    if (row < p.out_rows) {
+                        const int pr = it.tok0 + n;
+                        p.out[(size_t)pr * p.ldo + row] = v[0] * p.route_w[pr];
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        (void)waited;
+    }
+    // After a failed wait (error already recorded) later copies may still be in flight:
+    // wait for each of them, bounded, before the shared memory goes away. Every warp
+    // stayed in the item loop above, so the block-wide barriers always matched.
+    if (failed && ncw > 0) {
+        for (int item = issued_upto - NS + 1; item <= issued_upto; ++item) {
+            if (item < it0) continue;
+            const int j = item - it0;
+            (void)mbar_wait(&mybar[j % NS], (uint32_t)((j / NS) & 1), nullptr);
+        }
+    }
+}
+
+template <int WT, int KSF>
+void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s) {
+    void (*k)(const GemvParams);
+    if (p.mode == GM_PROJ) k = gemv_kernel<WT, KSF, GM_PROJ>;
+    else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP>;
+    else k = gemv_kernel<WT, KSF, GM_DOWN>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    k<<<grid, nwarps * 32, smem, s>>>(p);
+}
+
+}  // namespace
+
+void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem) {
+    (void)ntg;
+    const int max_cpw = std::max(1, MAXKS / m.steps);       // chunks a warp can hold in registers
+    const int min_nw = (m.chunks + max_cpw - 1) / max_cpw;
+    // smallest warp count >= min(8, chunks) that splits the chunks evenly, else the
+    // register-bound minimum
+    int nw = 0;
+    for (int cand = std::max(min_nw, std::min(8, m.chunks)); cand <= 16; ++cand)
+        if (m.chunks % cand == 0) { nw = cand; break; }
+    if (nw == 0) nw = std::max(min_nw, std::min(16, m.chunks));
+    const int cpw = (m.chunks + nw - 1) / nw;
+    const int sb = cpw * m.tile_bytes * nmat;
+    const int red = nw * nmat * NTG * 128 * 4;
+    const int bars_max = 128 * ((nw * 4 * 8 + 127) / 128);
+    const int budget = 220 * 1024 - red - bars_max;
+    int ns = std::min(4, budget / (nw * sb));
+    if (ns < 1) ns = 1;
+    *nwarps = nw;
+    *n_stages = ns;
+    *stage_bytes = sb;
+    *smem = 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red;
+}
+
+void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s) {
+    switch (p.type) {
+        case GT_Q4_K: launch_typed<GT_Q4_K, 16>(p, nwarps, grid, smem, s); break;
+        case GT_Q6_K: launch_typed<GT_Q6_K, 16>(p, nwarps, grid, smem, s); break;
+        case GT_Q8_0: launch_typed<GT_Q8_0, 8>(p, nwarps, grid, smem, s); break;
+        case GT_F16:
+            if (p.steps == 4) launch_typed<GT_F16, 4>(p, nwarps, grid, smem, s);
+            else if (p.steps == 2) launch_typed<GT_F16, 2>(p, nwarps, grid, smem, s);
+            else launch_typed<GT_F16, 1>(p, nwarps, grid, smem, s);
+            break;
+        default: break;
+    }
+}
+
+}  // namespace z2b

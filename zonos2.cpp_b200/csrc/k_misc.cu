@@ -1,0 +1,345 @@
+// k_misc.cu — step packing, embedding, MoE combine and the device sampler (sm_100a).
+#include "common.cuh"
+#include "gguf.h"
+#include "kernels.h"
+#include "quant.h"
+
+namespace z2b {
+
+namespace {
+
+// ---------------------------------------------------------------- packer
+// Device-side ragged packing: exclusive prefix sum over the per-stream row counts gives
+// each stream's token range; every token gets (slot, logical position, input row) and
+// streams that want logits get an output row. Replaces the host fill of ids / pos /
+// mask in zonos2_batch_step (src/zonos2-graph.cpp:784-812); no dense mask is built,
+// attention reads each token's slot and position directly.
+__global__ void pack_kernel(const StepBufs b, int T) {
+    __shared__ int s_start[1024], s_out[1024];
+    const int n = b.n_desc, tid = threadIdx.x;
+    if (tid < n) {
+        s_start[tid] = b.descs[tid].n_new;
+        s_out[tid] = (b.descs[tid].flags & SD_OUTPUT) ? 1 : 0;
+    }
+    __syncthreads();
+    // Hillis-Steele inclusive scans (n <= 1024)
+    for (int off = 1; off < n; off <<= 1) {
+        int a = 0, c = 0;
+        if (tid < n && tid >= off) { a = s_start[tid - off]; c = s_out[tid - off]; }
+        __syncthreads();
+        if (tid < n && tid >= off) { s_start[tid] += a; s_out[tid] += c; }
+        __syncthreads();
+    }
+    for (int i = tid; i < n; i += blockDim.x) {
+        const SlotDesc d = b.descs[i];
+        const int start = s_start[i] - d.n_new;
+        const int orow = (d.flags & SD_OUTPUT) ? s_out[i] - 1 : -1;
+        b.desc_out[i] = orow;
+        for (int r = 0; r < d.n_new; ++r) {
+            const int t = start + r;
+            if (t >= T) { atomicOr(b.err, (uint32_t)DERR_BOUNDS); break; }
+            b.tok_slot[t] = d.slot;
+            b.tok_pos[t] = d.n_past + r;
+            b.tok_desc[t] = i;
+            b.tok_out[t] = (r == d.n_new - 1) ? orow : -1;
+            for (int c = 0; c < NCOL; ++c) b.ids[t * NCOL + c] = b.ids_in[t * NCOL + c];
+        }
+        if (orow >= 0) { b.out_tok[orow] = start + d.n_new - 1; b.out_desc[orow] = i; }
+    }
+}
+
+// ---------------------------------------------------------------- embedding
+// Element j of row `id` of a GGUF table, dequantised with gguf-py's rounding order.
+__device__ __forceinline__ float emb_elem(const uint8_t* tbl, uint32_t type, size_t row_bytes, int id, int j) {
+    const uint8_t* row = tbl + (size_t)id * row_bytes;
+    switch (type) {
+        case GT_F32: return ((const float*)row)[j];
+        case GT_F16: return __half2float(((const __half*)row)[j]);
+        case GT_Q8_0: {
+            const uint8_t* blk = row + (j / 32) * 34;
+            return __fmul_rn((float)(int8_t)blk[2 + (j % 32)], __half2float(*(const __half*)blk));
+        }
+        case GT_Q4_K: {
+            const uint8_t* blk = row + (j / 256) * 144;
+            const int n = j % 256, sb = n / 32, i = n % 32;
+            const uint8_t* s = blk + 4;
+            int sc, m;
+            if (sb < 4) { sc = s[sb] & 63; m = s[sb + 4] & 63; }
+            else { sc = (s[sb + 4] & 0x0f) | ((s[sb - 4] >> 6) << 4); m = (s[sb + 4] >> 4) | ((s[sb] >> 6) << 4); }
+            const float d = __half2float(*(const __half*)blk), dmin = __half2float(*(const __half*)(blk + 2));
+            const int q = (blk[16 + (sb / 2) * 32 + i] >> (4 * (sb & 1))) & 15;
+            return __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+        }
+        case GT_Q6_K: {
+            const uint8_t* blk = row + (j / 256) * 210;
+            const int n = j % 256, g = n / 32, i = n % 32;
+            const int lo = (blk[(g / 4) * 64 + (g % 2) * 32 + i] >> (4 * ((g % 4) / 2))) & 15;
+            const int hi = (blk[128 + (g / 4) * 32 + i] >> (2 * (g % 4))) & 3;
+            const float d = __half2float(*(const __half*)(blk + 208));
+            return __fmul_rn(__fmul_rn(d, (float)(int8_t)blk[192 + n / 16]), (float)((lo | (hi << 4)) - 32));
+        }
+        default: return 0.0f;
+    }
+}
+
+// emb = sum of 10 table rows (src/zonos2-graph.cpp:249-259), x = rms_norm(emb) seeds the
+// residual (:300), cur = rms_norm(x) * attn_norm[0] feeds layer 0 (:343).
+__global__ void embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0, const Dims dm) {
+    extern __shared__ float sh[];
+    float* emb = sh;                      // [d]
+    float* red = sh + dm.n_embd;          // [32]
+    const int t = blockIdx.x, d = dm.n_embd;
+    const int* id = b.ids + t * NCOL;
+    int idc[NCOL];
+    bool bad = false;
+    for (int c = 0; c < NCOL; ++c) {
+        int v = id[c];
+        const int lim = c < dm.n_codebooks ? dm.audio_vocab : dm.text_vocab + 1;
+        if (v < 0 || v >= lim) { bad = true; v = 0; }
+        idc[c] = v;
+    }
+    if (bad && threadIdx.x == 0) atomicOr(b.err, (uint32_t)DERR_BOUNDS);
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int c = 0; c < NCOL; ++c) {
+            const uint8_t* tbl = c < dm.n_codebooks ? e.audio[c] : e.text;
+            const float v = emb_elem(tbl, e.type, e.row_bytes, idc[c], j);
+            acc = (c == 0) ? v : __fadd_rn(acc, v);
+        }
+        emb[j] = acc;
+        ss += acc * acc;
+    }
+    ss = block_sum(ss, red);
+    const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
+    float ss2 = 0.0f;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        const float x = emb[j] * sc;
+        emb[j] = x;
+        b.res[(size_t)t * d + j] = x;
+        ss2 += x * x;
+    }
+    ss2 = block_sum(ss2, red);
+    const float sc2 = 1.0f / sqrtf(ss2 / (float)d + dm.rms_eps);
+    for (int j = threadIdx.x; j < d; j += blockDim.x)
+        b.cur[(size_t)t * d + j] = __float2half_rn((emb[j] * sc2) * w0[j]);
+}
+
+// ---------------------------------------------------------------- MoE combine
+// x = sum_j out_route[pos(t, j)] in top-k order (src/zonos2-graph.cpp:232-238), then the
+// residual fold res = x + res (:332/:353) and the next block's input norm
+// (attn_norm of layer L+1, or output_norm after the last layer for output tokens).
+__global__ void moe_combine_kernel(const StepBufs b, int k, const float* __restrict__ next_norm,
+                                   const float* __restrict__ out_norm, const Dims dm, int last) {
+    __shared__ float red[32];
+    const int t = blockIdx.x, d = dm.n_embd;
+    const bool active = b.tok_slot[t] >= 0;
+    int pos[8];
+    for (int j = 0; j < k && j < 8; ++j) pos[j] = active ? b.route_pos[t * b.kmax + j] : -1;
+    float* res = b.res + (size_t)t * d;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float x = 0.0f;
+        for (int j = 0; j < k && j < 8; ++j) {
+            if (pos[j] < 0) continue;
+            const float v = b.out_route[(size_t)pos[j] * d + i];
+            x = (j == 0) ? v : __fadd_rn(x, v);
+        }
+        const float r = __fadd_rn(x, res[i]);
+        res[i] = r;
+        ss += r * r;
+    }
+    const int orow = b.tok_out[t];
+    if (last && orow < 0) return;              // uniform per block
+    ss = block_sum(ss, red);
+    const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
+    if (!last) {
+        for (int i = threadIdx.x; i < d; i += blockDim.x)
+            b.cur[(size_t)t * d + i] = __float2half_rn((res[i] * sc) * next_norm[i]);
+    } else {
+        for (int i = threadIdx.x; i < d; i += blockDim.x)
+            b.hout[(size_t)orow * d + i] = __float2half_rn((res[i] * sc) * out_norm[i]);
+    }
+}
+
+// ---------------------------------------------------------------- sampler
+// One block per (output row, codebook); mirrors zonos2_sampler::sample
+// (src/zonos2-sampler.cpp:16-77) and the history update of accept() (:9-14).
+constexpr int SORT_N = 2048;
+
+__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {   // descending value, ascending index
+    return va > vb || (va == vb && ia < ib);
+}
+
+__global__ void __launch_bounds__(256) sampler_kernel(const StepBufs b, const SampDev* __restrict__ samp,
+                                                      int* hist, int* hist_len, int hist_cap, const Dims dm) {
+    __shared__ float lv[SORT_N];
+    __shared__ int li[SORT_N];
+    __shared__ float pv[SORT_N];
+    __shared__ unsigned char drop_p[SORT_N];   // top-p rejections
+    __shared__ int s_code;
+    const int o = blockIdx.x, cb = blockIdx.y, av = dm.audio_vocab;
+    const int di = b.out_desc[o];
+    const SlotDesc D = b.descs[di];
+    if (!(D.flags & SD_SAMPLE)) return;
+    const SampDev sp = samp[D.samp];
+    const float* lg = b.logits + ((size_t)o * dm.n_codebooks + cb) * av;
+    const float* lu = nullptr;
+    if (D.twin >= 0) {
+        const int to = b.desc_out[D.twin];
+        if (to >= 0) lu = b.logits + ((size_t)to * dm.n_codebooks + cb) * av;
+    }
+    for (int i = threadIdx.x; i < av; i += blockDim.x) {
+        float v = lg[i];
+        if (lu) v = lu[i] + D.cfg_scale * (v - lu[i]);       // src/zonos2-graph.cpp:917-918
+        lv[i] = v;
+        li[i] = i;
+    }
+    __syncthreads();
+    int* h = hist + ((size_t)D.slot * dm.n_codebooks + cb) * hist_cap;
+    int* hl = hist_len + D.slot * dm.n_codebooks + cb;
+    if (sp.greedy) {
+        if (threadIdx.x == 0) {
+            int best = 0; float bv = lv[0];
+            for (int i = 1; i < av; ++i) if (lv[i] > bv) { bv = lv[i]; best = i; }
+            s_code = best;
+        }
+    } else {
+        if (threadIdx.x == 0) {
+            if (sp.rep_penalty != 1.0f && cb < sp.rep_codebooks) {
+                const int n = *hl, from = max(0, n - sp.rep_window);
+                for (int i = from; i < n; ++i) {
+                    const int tk = h[i % hist_cap];
+                    if (tk >= 0 && tk < av) lv[tk] = lv[tk] > 0.0f ? lv[tk] / sp.rep_penalty : lv[tk] * sp.rep_penalty;
+                }
+            }
+        }
+        __syncthreads();
+        if (sp.temperature > 0.0f)
+            for (int i = threadIdx.x; i < av; i += blockDim.x) lv[i] = lv[i] / sp.temperature;
+        const int k = (sp.top_k > 0 && sp.top_k < av) ? sp.top_k : av;
+        if (k < av) {
+            for (int i = av + threadIdx.x; i < SORT_N; i += blockDim.x) { lv[i] = -INFINITY; li[i] = 0x7fffffff; }
+            __syncthreads();
+            for (int size = 2; size <= SORT_N; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    for (int i = threadIdx.x; i < SORT_N; i += blockDim.x) {
+                        const int j = i ^ stride;
+                        if (j > i) {
+                            const bool asc = (i & size) == 0;     // segment direction
+                            const bool sw = asc ? before(lv[j], li[j], lv[i], li[i]) : before(lv[i], li[i], lv[j], li[j]);
+                            if (sw) { float tv = lv[i]; lv[i] = lv[j]; lv[j] = tv; int ti = li[i]; li[i] = li[j]; li[j] = ti; }
+                        }
+                    }
+                    __syncthreads();
+                }
+        }
+        __syncthreads();
+        __shared__ double s_sum;
+        __shared__ float s_pmax;
+        if (threadIdx.x == 0) {
+            float mx = -1e30f;
+            for (int j = 0; j < k; ++j) mx = fmaxf(mx, lv[j]);
+            double sum = 0.0;
+            for (int j = 0; j < k; ++j) { pv[j] = expf(lv[j] - mx); sum += (double)pv[j]; }
+            float pm = 0.0f;
+            for (int j = 0; j < k; ++j) { pv[j] = (float)((double)pv[j] / sum); pm = fmaxf(pm, pv[j]); }
+            s_pmax = pm;
+        }
+        __syncthreads();
+        // top-p over candidates ordered by probability (descending, ties by position)
+        if (sp.top_p > 0.0f && sp.top_p < 1.0f) {
+            for (int j = threadIdx.x; j < k; j += blockDim.x) {
+                double c = 0.0;
+                for (int i = 0; i < k; ++i)
+                    if (pv[i] > pv[j] || (pv[i] == pv[j] && i < j)) c += (double)pv[i];
+                // kept iff the mass before it has not yet reached top_p
+                drop_p[j] = c >= (double)sp.top_p ? 1 : 0;
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            const bool use_p = sp.top_p > 0.0f && sp.top_p < 1.0f;
+            const float thr = sp.min_p * s_pmax;
+            int best = 0;
+            for (int j = 1; j < k; ++j) if (pv[j] > pv[best]) best = j;
+            double s2 = 0.0;
+            for (int j = 0; j < k; ++j) {
+                bool keep = true;
+                if (use_p && drop_p[j]) keep = false;
+                if (sp.min_p > 0.0f && pv[j] < thr) keep = false;
+                if (!keep) pv[j] = 0.0f;
+                s2 += (double)pv[j];
+            }
+            int code = li[best];
+            if (s2 > 0.0) {
+                const double r = b.canon[(size_t)o * dm.n_codebooks + cb] * s2;
+                double acc = 0.0;
+                for (int j = 0; j < k; ++j) { acc += (double)pv[j]; if (acc >= r) { code = li[j]; break; } }
+            }
+            s_code = code;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        b.codes[(size_t)o * dm.n_codebooks + cb] = s_code;
+        const int n = *hl;
+        h[n % hist_cap] = s_code;
+        *hl = n + 1;
+    }
+}
+
+__global__ void feed_kernel(SlotDesc* descs, int n, int* ids_in, const int* codes, const int* desc_out,
+                            double* canon_dst, const double* canon_src, int ncb, int text_pad, int advance) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (advance) {
+        const int o = desc_out[i];
+        for (int c = 0; c < ncb; ++c) ids_in[i * NCOL + c] = o >= 0 ? codes[o * ncb + c] : 0;
+        ids_in[i * NCOL + ncb] = text_pad;
+        descs[i].n_past += 1;
+    }
+    for (int c = 0; c < ncb; ++c) canon_dst[i * ncb + c] = canon_src[i * ncb + c];
+}
+
+__global__ void dequant_rows_kernel(const uint8_t* rows, uint32_t type, size_t row_bytes, int n_rows, int K, float* out) {
+    const int r = blockIdx.x;
+    if (r >= n_rows) return;
+    for (int j = threadIdx.x; j < K; j += blockDim.x) out[(size_t)r * K + j] = emb_elem(rows, type, row_bytes, r, j);
+}
+
+}  // namespace
+
+void launch_dequant_rows(const uint8_t* rows_dev, uint32_t type, size_t row_bytes, int rows, int K, float* out,
+                         cudaStream_t s) {
+    dequant_rows_kernel<<<rows, 256, 0, s>>>(rows_dev, type, row_bytes, rows, K, out);
+}
+
+void launch_feed(SlotDesc* descs, int n, int* ids_in, const int* codes, const int* desc_out, double* canon_dst,
+                 const double* canon_src, int ncb, int text_pad, int advance, cudaStream_t s) {
+    feed_kernel<<<(n + 127) / 128, 128, 0, s>>>(descs, n, ids_in, codes, desc_out, canon_dst, canon_src, ncb,
+                                                text_pad, advance);
+}
+
+void launch_pack(const StepBufs& b, int T, int n_out, cudaStream_t s) {
+    (void)n_out;
+    pack_kernel<<<1, 1024, 0, s>>>(b, T);
+}
+
+void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s) {
+    embed_kernel<<<T, 256, (d.n_embd + 32) * sizeof(float), s>>>(b, e, attn_norm0, d);
+}
+
+void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,
+                        const Dims& d, int T, int last, cudaStream_t s) {
+    moe_combine_kernel<<<T, 256, 0, s>>>(b, ly.is_moe ? ly.top_k : 1, next_norm, out_norm, d, last);
+}
+
+void launch_sampler(const StepBufs& b, const SampDev* samp, int* hist, int* hist_len, int hist_cap,
+                    const Dims& d, int n_out, cudaStream_t s) {
+    if (n_out <= 0) return;
+    dim3 grid(n_out, d.n_codebooks);
+    sampler_kernel<<<grid, 256, 0, s>>>(b, samp, hist, hist_len, hist_cap, d);
+}
+
+}  // namespace z2b

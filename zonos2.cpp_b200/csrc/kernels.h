@@ -1,0 +1,159 @@
+// kernels.h — host-side launch interface of the sm_100a kernels.
+// Plain structs of device pointers and sizes; no torch / ggml types.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace z2b {
+
+constexpr int MAX_EXPERTS = 256;
+constexpr int NCOL = 10;            // input columns per row: 9 audio codebooks + text
+constexpr int PAGE = 256;           // KV page length (tokens)
+
+// A weight matrix in tile layout (tile_layout.h).
+struct DevMat {
+    const uint8_t* tiles = nullptr;
+    uint32_t type = 0;
+    int rows = 0, K = 0;
+    int n_row_tiles = 0;            // per expert for expert stacks
+    int chunks = 0, tile_bytes = 0, steps = 0;
+    int64_t expert_stride = 0;      // bytes between experts (stacks only)
+    int n_expert = 1;
+    size_t gguf_bytes = 0;          // bytes of the same weights in the GGUF file
+};
+
+// ---- tile GEMV ---------------------------------------------------------------------
+enum GemvMode { GM_PROJ = 0, GM_GATEUP = 1, GM_DOWN = 2 };
+enum GemvEpi { EPI_STORE = 0, EPI_ADD = 1, EPI_SOFTCAP = 2 };
+
+struct ProjSeg { const uint8_t* tiles; int n_row_tiles; int rows; int out_off; };
+
+struct GemvParams {
+    int mode, epi;
+    uint32_t type;
+    int K, chunks, tile_bytes, steps, n_row_tiles;
+    // projection mode: up to 4 matrices of the same type / K, all tokens
+    ProjSeg seg[4];
+    int n_seg, total_items;
+    // expert mode: stacked experts, routed tokens
+    const uint8_t* w0;              // gate (GM_GATEUP) or down (GM_DOWN)
+    const uint8_t* w1;              // up   (GM_GATEUP)
+    int64_t expert_stride;
+    const int* n_active;            // device: number of experts with routes
+    const int* active;              // device: active expert ids (ascending)
+    const int* seg_off;             // device: [E+1] route offsets in expert order
+    const int* route_tok;           // device: token of each route (expert order)
+    const float* route_w;           // device: route probability (GM_DOWN)
+    // activations
+    const __half* X; int ldx;       // GM_PROJ / GM_GATEUP: [T][ldx]; GM_DOWN: y [routes][ldx]
+    int T;                          // GM_PROJ token count
+    float* out; int ldo;            // GM_PROJ / GM_DOWN output (f32)
+    __half* yout; int ldy;          // GM_GATEUP output y (f16)
+    int out_rows;                   // valid rows per expert (GM_GATEUP / GM_DOWN)
+    float cap;                      // EPI_SOFTCAP
+    uint32_t* err;
+    // launch geometry (host-filled)
+    int n_stages, stage_bytes;
+};
+
+// Chooses warps/stages for a weight matrix and fills the launch geometry.
+void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem);
+void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s);
+
+// ---- decode-step kernels -----------------------------------------------------------
+struct Dims {
+    int n_embd, head_dim, n_head, n_head_kv, n_ff, rd, n_layer;
+    int n_codebooks, audio_vocab, text_vocab;
+    float rms_eps, qk_eps, rope_base, softcap;
+};
+
+// One step's input descriptor per active stream (uploaded by the host each step).
+struct SlotDesc {
+    int slot;        // cache band / column
+    int n_past;      // logical position of the first new row
+    int n_new;       // rows this step
+    int flags;       // SD_* bits
+    int twin;        // desc index of the unconditional CFG twin, or -1
+    float cfg_scale;
+    int samp;        // index into the per-slot sampling table (= slot)
+    int pad_;
+};
+enum SlotFlags { SD_OUTPUT = 1, SD_SAMPLE = 2 };
+
+// Sampling parameters per slot, device copy (mirrors zonos2_sampling).
+struct SampDev {
+    float temperature, top_p, min_p, rep_penalty;
+    int top_k, rep_window, rep_codebooks, greedy;
+};
+
+// Paged KV cache: page p holds PAGE tokens of every layer:
+//   [p][layer][kvh] K block: [PAGE][hd] f16, rows swizzled (16-byte chunk c of key j at c ^ swz(j))
+//                   V block: [PAGE/64][hd][64] f16 (V transposed per 64 keys, rows swizzled by dim)
+struct KVDev {
+    __half* pool;
+    const int* page_table;          // [n_slots][max_pages]
+    int max_pages;
+    size_t page_elems;              // elements per page (all layers)
+    size_t layer_elems;             // elements per layer within a page
+    size_t head_elems;              // elements per (K or V) block of one kv head
+};
+
+// Per-step device buffers (capacity T_max tokens, R_max routes, O_max output rows).
+struct StepBufs {
+    const SlotDesc* descs; int n_desc;
+    const int* ids_in;              // [T][NCOL] packed host input rows
+    int* tok_slot; int* tok_pos; int* tok_desc; int* ids;   // [T], [T][NCOL]
+    int* out_tok;                   // [n_out] token of each output row
+    int* out_desc;                  // [n_out] desc of each output row
+    int* tok_out;                   // [T] output row of a token, or -1
+    int* desc_out;                  // [n_desc] output row of a desc, or -1
+    float* res; __half* cur;        // [T][d]
+    float* qkvg; int ldq;           // [T][ldq]
+    __half* qh;                     // [T][nh][hd]
+    float* apart; int max_split;    // [T][nh][max_split][hd+2]
+    __half* o;                      // [T][nh*hd]
+    float* rstate;                  // [T][rd]
+    int* sel; float* selw; int kmax;// [T][kmax]
+    int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
+    int* ticket;
+    __half* y;                      // [R][ff]
+    float* out_route;               // [R][d]
+    __half* hout;                   // [O][d]
+    float* logits;                  // [O][ncb*av]
+    int* codes;                     // [O][ncb]
+    const double* canon;            // [O][ncb] host-drawn uniform(0,1) values
+    int* layer_active;              // [n_layer] experts with routes, per layer (accounting)
+    uint32_t* err;
+};
+
+// Per-layer small tensors kept as f32 on the device.
+struct LayerSmall {
+    const float *attn_norm, *ffn_norm, *attn_temp;
+    const float *rdown_w, *rdown_b, *m0_w, *m0_b, *m2_w, *m2_b, *m4_w, *rnorm, *rbias, *eda, *rmask;
+    int is_moe, top_k, n_expert;
+};
+
+// Embedding tables in GGUF block format (rows dequantised in the kernel).
+struct EmbedDev {
+    const uint8_t* audio[16]; const uint8_t* text; uint32_t type; size_t row_bytes;
+};
+
+void launch_pack(const StepBufs& b, int T, int n_out, cudaStream_t s);
+void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s);
+void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T, cudaStream_t s);
+void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys, int max_split, cudaStream_t s);
+void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s);
+void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
+                   cudaStream_t s);
+// Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the
+// next input row, advance n_past, and copy this step's host-drawn uniforms.
+void launch_feed(SlotDesc* descs, int n, int* ids_in, const int* codes, const int* desc_out, double* canon_dst,
+                 const double* canon_src, int ncb, int text_pad, int advance, cudaStream_t s);
+void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,
+                        const Dims& d, int T, int last, cudaStream_t s);
+void launch_sampler(const StepBufs& b, const SampDev* samp, int* hist, int* hist_len, int hist_cap,
+                    const Dims& d, int n_out, cudaStream_t s);
+
+}  // namespace z2b

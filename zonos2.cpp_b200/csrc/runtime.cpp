@@ -1,0 +1,503 @@
+// runtime.cpp — batch context and the decode step (host side).
+//
+// Replaces the continuous-batching runtime of src/zonos2-graph.cpp:606-870. Differences
+// by design: the KV cache is a pool of 256-token pages allocated to slots on demand
+// (the reference reserves a fixed band per slot); a step carries only active streams
+// (no ladder of fixed-width graphs, no idle columns, no dense mask); prompt rows and
+// decode rows can share a step; sampling runs on the device after the head.
+#include "runtime.h"
+
+#include <algorithm>
+#include <cstring>
+#include <random>
+
+namespace z2b {
+
+namespace {
+
+thread_local std::string g_err;
+
+#define CK(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { set_error(std::string(#x) + ": " + cudaGetErrorString(e_)); return Z2B_ERR_CUDA; } } while (0)
+
+template <class T> T* carve(uint8_t*& p, size_t n) {
+    T* r = reinterpret_cast<T*>(p);
+    p += (n * sizeof(T) + 255) / 256 * 256;
+    return r;
+}
+
+}  // namespace
+
+void set_error(const std::string& e) { g_err = e; }
+const char* last_error() { return g_err.c_str(); }
+
+Ctx::~Ctx() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    if (d_canon_all) cudaFree(d_canon_all);
+    if (h_canon_all) cudaFreeHost(h_canon_all);
+    for (void* p : dallocs) cudaFree(p);
+    for (void* p : hallocs) cudaFreeHost(p);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
+    if (n_slots < 1 || n_slots > 1024 || slot_cap_frames < 1) { set_error("bad n_slots / slot_cap"); return Z2B_ERR_ARG; }
+    std::unique_ptr<Ctx> c(new Ctx());
+    c->m = m;
+    if (cudaSetDevice(m->device) != cudaSuccess) { set_error("cudaSetDevice failed"); return Z2B_ERR_CUDA; }
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    const Dims& D = m->dims;
+    c->n_slots = n_slots;
+    c->slot_cap = (slot_cap_frames + PAGE - 1) / PAGE * PAGE;
+    c->pages_per_slot = c->slot_cap / PAGE;
+    c->T_max = std::max(n_slots, 512);
+    c->O_max = n_slots;
+    c->D_max = std::min(1024, c->T_max);
+    c->kmax = 1;
+    for (auto& ly : m->layers) c->kmax = std::max(c->kmax, ly.top_k);
+    c->R_max = c->T_max * c->kmax;
+    c->split_keys = 256;
+    c->max_split = (c->slot_cap + c->split_keys - 1) / c->split_keys;
+    const int d = D.n_embd, hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv, ncb = D.n_codebooks, av = D.audio_vocab;
+
+    // KV pool: every slot can reach its full capacity
+    c->n_pages = n_slots * c->pages_per_slot;
+    c->head_elems = (size_t)PAGE * hd;
+    c->layer_elems = 2 * (size_t)nkv * c->head_elems;
+    c->page_elems = (size_t)D.n_layer * c->layer_elems;
+    auto dal = [&](size_t n) -> void* {
+        void* p = nullptr;
+        if (cudaMalloc(&p, n ? n : 16) != cudaSuccess) return nullptr;
+        c->dallocs.push_back(p);
+        return p;
+    };
+    c->kv_pool = (__half*)dal((size_t)c->n_pages * c->page_elems * sizeof(__half));
+    if (!c->kv_pool) { set_error("KV pool allocation failed (" + std::to_string(c->n_pages) + " pages)"); return Z2B_ERR_OOM; }
+    CK(cudaMemset(c->kv_pool, 0, (size_t)c->n_pages * c->page_elems * sizeof(__half)));
+    c->free_pages.resize(c->n_pages);
+    for (int i = 0; i < c->n_pages; ++i) c->free_pages[i] = c->n_pages - 1 - i;
+    c->slot_pages.assign(n_slots, {});
+    c->h_pt.assign((size_t)n_slots * c->pages_per_slot, -1);
+
+    // staging (host pinned + device mirror): page table | descs | ids | canon
+    c->st_pt = 0;
+    c->st_descs = (size_t)n_slots * c->pages_per_slot * 4;
+    c->st_descs = (c->st_descs + 255) / 256 * 256;
+    c->st_ids = c->st_descs + (size_t)c->D_max * sizeof(SlotDesc);
+    c->st_ids = (c->st_ids + 255) / 256 * 256;
+    c->st_canon = c->st_ids + (size_t)c->T_max * NCOL * 4;
+    c->st_canon = (c->st_canon + 255) / 256 * 256;
+    c->st_bytes = c->st_canon + (size_t)c->O_max * ncb * 8;
+    CK(cudaMallocHost(&c->h_stage, c->st_bytes));
+    c->hallocs.push_back(c->h_stage);
+    c->d_stage = (uint8_t*)dal(c->st_bytes);
+    if (!c->d_stage) { set_error("staging allocation failed"); return Z2B_ERR_OOM; }
+    std::memset(c->h_stage, 0, c->st_bytes);
+
+    // per-step device buffers
+    const size_t ldq = (size_t)nh * hd + 2 * (size_t)nkv * hd + nh;
+    size_t need = 0;
+    auto acc = [&](size_t bytes) { need += (bytes + 255) / 256 * 256; };
+    const int T = c->T_max, R = c->R_max + 8 * MAX_EXPERTS, O = c->O_max;
+    acc(T * 4); acc(T * 4); acc(T * 4); acc(T * NCOL * 4); acc(O * 4); acc(O * 4); acc(T * 4); acc(c->D_max * 4);
+    acc((size_t)T * d * 4); acc((size_t)T * d * 2); acc((size_t)T * ldq * 4); acc((size_t)T * nh * hd * 2);
+    acc((size_t)T * nh * c->max_split * (hd + 2) * 4); acc((size_t)T * nh * hd * 2); acc((size_t)T * std::max(D.rd, 1) * 4);
+    acc((size_t)T * c->kmax * 4); acc((size_t)T * c->kmax * 4);
+    acc(4); acc(MAX_EXPERTS * 4); acc((MAX_EXPERTS + 1) * 4); acc((size_t)R * 4); acc((size_t)R * 4); acc((size_t)T * c->kmax * 4);
+    acc(4); acc((size_t)R * D.n_ff * 2); acc((size_t)R * d * 4); acc((size_t)O * d * 2);
+    acc((size_t)O * ncb * av * 4); acc((size_t)O * ncb * 4); acc(D.n_layer * 4); acc(4);
+    uint8_t* base = (uint8_t*)dal(need);
+    if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
+    CK(cudaMemset(base, 0, need));
+    uint8_t* p = base;
+    StepBufs& B = c->B;
+    B.descs = (const SlotDesc*)(c->d_stage + c->st_descs);
+    B.ids_in = (const int*)(c->d_stage + c->st_ids);
+    B.canon = (const double*)(c->d_stage + c->st_canon);
+    B.tok_slot = carve<int>(p, T); B.tok_pos = carve<int>(p, T); B.tok_desc = carve<int>(p, T);
+    B.ids = carve<int>(p, (size_t)T * NCOL); B.out_tok = carve<int>(p, O); B.out_desc = carve<int>(p, O);
+    B.tok_out = carve<int>(p, T); B.desc_out = carve<int>(p, c->D_max);
+    B.res = carve<float>(p, (size_t)T * d); B.cur = carve<__half>(p, (size_t)T * d);
+    B.qkvg = carve<float>(p, (size_t)T * ldq); B.ldq = (int)ldq;
+    B.qh = carve<__half>(p, (size_t)T * nh * hd);
+    B.apart = carve<float>(p, (size_t)T * nh * c->max_split * (hd + 2)); B.max_split = c->max_split;
+    B.o = carve<__half>(p, (size_t)T * nh * hd);
+    B.rstate = carve<float>(p, (size_t)T * std::max(D.rd, 1));
+    B.sel = carve<int>(p, (size_t)T * c->kmax); B.selw = carve<float>(p, (size_t)T * c->kmax); B.kmax = c->kmax;
+    B.n_active = carve<int>(p, 1); B.active = carve<int>(p, MAX_EXPERTS); B.seg_off = carve<int>(p, MAX_EXPERTS + 1);
+    B.route_tok = carve<int>(p, R); B.route_w = carve<float>(p, R); B.route_pos = carve<int>(p, (size_t)T * c->kmax);
+    B.ticket = carve<int>(p, 1);
+    B.y = carve<__half>(p, (size_t)R * D.n_ff); B.out_route = carve<float>(p, (size_t)R * d);
+    B.hout = carve<__half>(p, (size_t)O * d); B.logits = carve<float>(p, (size_t)O * ncb * av);
+    B.codes = carve<int>(p, (size_t)O * ncb); B.layer_active = carve<int>(p, D.n_layer);
+    B.err = carve<uint32_t>(p, 1);
+
+    c->kv.pool = c->kv_pool;
+    c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
+    c->kv.max_pages = c->pages_per_slot;
+    c->kv.page_elems = c->page_elems;
+    c->kv.layer_elems = c->layer_elems;
+    c->kv.head_elems = c->head_elems;
+
+    // sampler state
+    c->d_samp = (SampDev*)dal((size_t)n_slots * sizeof(SampDev));
+    c->hist_cap = Z2B_MAX_REP_WINDOW;
+    c->d_hist = (int*)dal((size_t)n_slots * ncb * c->hist_cap * 4);
+    c->d_hist_len = (int*)dal((size_t)n_slots * ncb * 4);
+    if (!c->d_samp || !c->d_hist || !c->d_hist_len) { set_error("sampler state allocation failed"); return Z2B_ERR_OOM; }
+    CK(cudaMemset(c->d_hist_len, 0, (size_t)n_slots * ncb * 4));
+    c->h_samp.resize(n_slots);
+    c->greedy.assign(n_slots, 1);
+    c->rng.resize(n_slots);
+    for (int i = 0; i < n_slots; ++i) {
+        SampDev& s = c->h_samp[i];
+        s.temperature = 1.15f; s.top_k = 106; s.top_p = 0.0f; s.min_p = 0.18f; s.rep_penalty = 1.2f;
+        s.rep_window = 50; s.rep_codebooks = 8; s.greedy = 1;
+        c->rng[i].seed(0);
+    }
+    CK(cudaMemcpy(c->d_samp, c->h_samp.data(), (size_t)n_slots * sizeof(SampDev), cudaMemcpyHostToDevice));
+
+    // pinned outputs
+    CK(cudaMallocHost(&c->h_codes, (size_t)O * ncb * 4)); c->hallocs.push_back(c->h_codes);
+    CK(cudaMallocHost(&c->h_logits, (size_t)O * ncb * av * 4)); c->hallocs.push_back(c->h_logits);
+    CK(cudaMallocHost(&c->h_misc, 4096)); c->hallocs.push_back(c->h_misc);
+    c->step_logits.assign((size_t)c->D_max * ncb * av, 0.0f);
+    c->step_has_logits.assign(c->D_max, 0);
+    *out = c.release();
+    return Z2B_OK;
+}
+
+int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp) {
+    if (slot < 0 || slot >= c->n_slots) { set_error("slot out of range"); return Z2B_ERR_ARG; }
+    for (int pg : c->slot_pages[slot]) c->free_pages.push_back(pg);
+    c->slot_pages[slot].clear();
+    for (int i = 0; i < c->pages_per_slot; ++i) c->h_pt[(size_t)slot * c->pages_per_slot + i] = -1;
+    SampDev& s = c->h_samp[slot];
+    if (sp) {
+        if (sp->rep_window < 0 || sp->rep_window > Z2B_MAX_REP_WINDOW) { set_error("rep_window out of range"); return Z2B_ERR_ARG; }
+        s.temperature = sp->temperature; s.top_k = sp->top_k; s.top_p = sp->top_p; s.min_p = sp->min_p;
+        s.rep_penalty = sp->rep_penalty; s.rep_window = sp->rep_window; s.rep_codebooks = sp->rep_codebooks;
+        s.greedy = sp->greedy ? 1 : 0;
+        c->rng[slot].seed(sp->seed);
+    } else {
+        s.greedy = 1;
+        c->rng[slot].seed(0);
+    }
+    c->greedy[slot] = s.greedy;
+    const int ncb = c->m->dims.n_codebooks;
+    CK(cudaMemcpyAsync(c->d_samp + slot, &s, sizeof(SampDev), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemsetAsync(c->d_hist_len + (size_t)slot * ncb, 0, (size_t)ncb * 4, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return Z2B_OK;
+}
+
+// ---------------------------------------------------------------- launch sequence
+
+namespace {
+
+int ctas_per_sm(int smem) { return std::max(1, std::min(4, (227 * 1024) / (smem + 1024))); }
+
+void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int T, const __half* X, int ldx,
+               float* out, int ldo, int epi, float cap) {
+    GemvParams p{};
+    p.mode = GM_PROJ; p.epi = epi;
+    p.type = mats[0]->type; p.K = mats[0]->K; p.chunks = mats[0]->chunks;
+    p.tile_bytes = mats[0]->tile_bytes; p.steps = mats[0]->steps;
+    p.n_seg = nmat;
+    int items = 0;
+    for (int i = 0; i < nmat; ++i) {
+        p.seg[i] = ProjSeg{mats[i]->tiles, mats[i]->n_row_tiles, mats[i]->rows, offs[i]};
+        items += mats[i]->n_row_tiles;
+    }
+    p.total_items = items;
+    p.X = X; p.ldx = ldx; p.T = T; p.out = out; p.ldo = ldo; p.cap = cap; p.err = c->B.err;
+    int nw, smem;
+    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem);
+    const int grid = std::min(items, c->m->n_sm * ctas_per_sm(smem));
+    launch_gemv(p, nw, grid, smem, c->stream);
+    c->launches++;
+}
+
+void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
+    const Dims& D = c->m->dims;
+    GemvParams p{};
+    const DevMat& w0 = mode == GM_GATEUP ? ly.gate_exps : ly.down_exps;
+    p.mode = mode; p.epi = EPI_STORE;
+    p.type = w0.type; p.K = w0.K; p.chunks = w0.chunks; p.tile_bytes = w0.tile_bytes; p.steps = w0.steps;
+    p.n_row_tiles = w0.n_row_tiles;
+    p.w0 = w0.tiles;
+    p.w1 = mode == GM_GATEUP ? ly.up_exps.tiles : nullptr;
+    p.expert_stride = w0.expert_stride;
+    p.n_active = c->B.n_active; p.active = c->B.active; p.seg_off = c->B.seg_off;
+    p.route_tok = c->B.route_tok; p.route_w = c->B.route_w;
+    if (mode == GM_GATEUP) {
+        p.X = c->B.cur; p.ldx = D.n_embd; p.yout = c->B.y; p.ldy = D.n_ff; p.out_rows = D.n_ff;
+    } else {
+        p.X = c->B.y; p.ldx = D.n_ff; p.out = c->B.out_route; p.ldo = D.n_embd; p.out_rows = D.n_embd;
+    }
+    p.err = c->B.err;
+    int nw, smem;
+    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem);
+    const int grid = c->m->n_sm * ctas_per_sm(smem);
+    launch_gemv(p, nw, grid, smem, c->stream);
+    c->launches++;
+}
+
+}  // namespace
+
+void enqueue_step(Ctx* c, int T, int n_out) {
+    Model* m = c->m;
+    const Dims& D = m->dims;
+    StepBufs B = c->B;
+    B.n_desc = c->cur_n_desc;
+    c->launches = 0;
+    cudaMemsetAsync(B.err, 0, 4, c->stream);
+    launch_pack(B, T, n_out, c->stream); c->launches++;
+    launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->stream); c->launches++;
+    const int hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv;
+    bool first_moe = true;
+    for (int L = 0; L < D.n_layer; ++L) {
+        const LayerDev& ly = m->layers[L];
+        if (ly.qkvg_fused) {
+            const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
+            const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
+            gemv_proj(c, mats, offs, 4, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f);
+        } else {
+            const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
+            const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
+            for (int i = 0; i < 4; ++i) gemv_proj(c, &mats[i], &offs[i], 1, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f);
+        }
+        launch_rope_append(B, c->kv, ly.small.attn_temp, D, L, T, c->stream); c->launches++;
+        launch_attention(B, c->kv, D, L, T, c->split_keys, c->max_split, c->stream); c->launches++;
+        launch_attn_combine(B, D, T, c->split_keys, c->max_split, c->stream); c->launches++;
+        {
+            const DevMat* mats[1] = {&ly.wo};
+            const int offs[1] = {0};
+            gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f);
+        }
+        launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches++;
+        if (ly.is_moe) first_moe = false;
+        gemv_moe(c, ly, GM_GATEUP);
+        gemv_moe(c, ly, GM_DOWN);
+        const bool last = L == D.n_layer - 1;
+        launch_moe_combine(B, ly.small, last ? nullptr : m->layers[L + 1].small.attn_norm, m->out_norm, D, T,
+                           last ? 1 : 0, c->stream);
+        c->launches++;
+    }
+    if (n_out > 0) {
+        const DevMat* mats[1] = {&m->head};
+        const int offs[1] = {0};
+        gemv_proj(c, mats, offs, 1, n_out, B.hout, D.n_embd, B.logits, D.n_codebooks * D.audio_vocab, EPI_SOFTCAP,
+                  D.softcap);
+        launch_sampler(B, c->d_samp, c->d_hist, c->d_hist_len, c->hist_cap, D, n_out, c->stream);
+        c->launches++;
+    }
+}
+
+int run_step(Ctx* c, int T, int n_out) {
+    const bool use_graph = c->graphs_enabled;
+    if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
+    const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48);
+    auto it = c->graphs.find(key);
+    if (it == c->graphs.end()) {
+        cudaGraph_t g;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+        enqueue_step(c, T, n_out);
+        CK(cudaStreamEndCapture(c->stream, &g));
+        cudaGraphExec_t ge;
+        const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { set_error(std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e)); return Z2B_ERR_CUDA; }
+        it = c->graphs.emplace(key, ge).first;
+        c->graph_launches[key] = c->launches;
+    }
+    c->launches = c->graph_launches[key];
+    CK(cudaGraphLaunch(it->second, c->stream));
+    return Z2B_OK;
+}
+
+// ---------------------------------------------------------------- step API
+
+int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_desc, int* T_out, int* n_out_out) {
+    const Dims& D = c->m->dims;
+    if (n < 1 || n > c->D_max) { set_error("number of descs out of range"); return Z2B_ERR_ARG; }
+    int T = 0, n_out = 0;
+    std::vector<char> seen(c->n_slots, 0);
+    for (int i = 0; i < n; ++i) {
+        const z2b_slot_desc& d = descs[i];
+        if (d.slot < 0 || d.slot >= c->n_slots) { set_error("desc slot out of range"); return Z2B_ERR_ARG; }
+        if (seen[d.slot]) { set_error("slot listed twice in one step"); return Z2B_ERR_ARG; }
+        seen[d.slot] = 1;
+        if (d.n_new < 1 || d.n_past < 0) { set_error("desc n_new/n_past out of range"); return Z2B_ERR_ARG; }
+        if (d.n_past + d.n_new + extra_rows_per_desc > c->slot_cap) { set_error("stream exceeds slot capacity"); return Z2B_ERR_ARG; }
+        if (d.cfg_twin >= n || d.cfg_twin == i) { set_error("bad cfg_twin"); return Z2B_ERR_ARG; }
+        T += d.n_new;
+        if (d.flags & Z2B_WANT_LOGITS) ++n_out;
+    }
+    if (T > c->T_max) { set_error("rows per step exceed capacity (" + std::to_string(c->T_max) + ")"); return Z2B_ERR_ARG; }
+    if (n_out > c->O_max) { set_error("too many output rows"); return Z2B_ERR_ARG; }
+    // KV pages for every position this call can write
+    for (int i = 0; i < n; ++i) {
+        const z2b_slot_desc& d = descs[i];
+        const int need = (d.n_past + d.n_new + extra_rows_per_desc - 1) / PAGE + 1;
+        auto& pages = c->slot_pages[d.slot];
+        while ((int)pages.size() < need) {
+            if (c->free_pages.empty()) { set_error("KV page pool exhausted"); return Z2B_ERR_OOM; }
+            const int pg = c->free_pages.back();
+            c->free_pages.pop_back();
+            c->h_pt[(size_t)d.slot * c->pages_per_slot + pages.size()] = pg;
+            pages.push_back(pg);
+        }
+    }
+    std::memcpy(c->h_stage + c->st_pt, c->h_pt.data(), c->h_pt.size() * 4);
+    SlotDesc* sd = (SlotDesc*)(c->h_stage + c->st_descs);
+    int o = 0;
+    for (int i = 0; i < n; ++i) {
+        const z2b_slot_desc& d = descs[i];
+        SlotDesc s{};
+        s.slot = d.slot; s.n_past = d.n_past; s.n_new = d.n_new;
+        s.flags = ((d.flags & Z2B_WANT_LOGITS) ? SD_OUTPUT : 0) | (((d.flags & Z2B_WANT_SAMPLE) == Z2B_WANT_SAMPLE) ? SD_SAMPLE : 0);
+        s.twin = d.cfg_twin; s.cfg_scale = d.cfg_scale; s.samp = d.slot;
+        sd[i] = s;
+        c->desc_out_host[i] = (s.flags & SD_OUTPUT) ? o++ : -1;
+    }
+    (void)D;
+    c->cur_n_desc = n;
+    *T_out = T;
+    *n_out_out = n_out;
+    return Z2B_OK;
+}
+
+// host-drawn uniforms for non-greedy sampling: one per (sampled stream, codebook) in
+// codebook order, exactly as std::uniform_real_distribution<double> consumes mt19937
+// in zonos2_sampler::sample (src/zonos2-sampler.cpp:73-74)
+void draw_canon(Ctx* c, const z2b_slot_desc* descs, int n, double* dst) {
+    const int ncb = c->m->dims.n_codebooks;
+    for (int i = 0; i < n; ++i) {
+        const int o = c->desc_out_host[i];
+        if (o < 0) continue;
+        const bool sample = (descs[i].flags & Z2B_WANT_SAMPLE) == Z2B_WANT_SAMPLE;
+        for (int cb = 0; cb < ncb; ++cb)
+            dst[(size_t)o * ncb + cb] = (sample && !c->greedy[descs[i].slot])
+                ? std::generate_canonical<double, 53>(c->rng[descs[i].slot]) : 0.0;
+    }
+}
+
+int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes, float* out_logits) {
+    const Dims& D = c->m->dims;
+    if (!descs || !ids) { set_error("null argument"); return Z2B_ERR_ARG; }
+    int T, n_out;
+    c->desc_out_host.assign(std::max(n, 1), -1);
+    int rc = ctx_prepare(c, descs, n, 0, &T, &n_out);
+    if (rc) return rc;
+    std::memcpy(c->h_stage + c->st_ids, ids, (size_t)T * NCOL * 4);
+    draw_canon(c, descs, n, (double*)(c->h_stage + c->st_canon));
+    CK(cudaMemcpyAsync(c->d_stage, c->h_stage, c->st_bytes, cudaMemcpyHostToDevice, c->stream));
+    rc = run_step(c, T, n_out);
+    if (rc) return rc;
+    const int ncb = D.n_codebooks, av = D.audio_vocab;
+    if (n_out > 0) {
+        CK(cudaMemcpyAsync(c->h_codes, c->B.codes, (size_t)n_out * ncb * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaMemcpyAsync(c->h_logits, c->B.logits, (size_t)n_out * ncb * av * 4, cudaMemcpyDeviceToHost, c->stream));
+    }
+    CK(cudaMemcpyAsync(c->h_misc, c->B.err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_misc + 1, c->B.layer_active, (size_t)D.n_layer * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    const uint32_t derr = c->h_misc[0];
+    if (derr) { set_error("device error flags 0x" + std::to_string(derr)); return Z2B_ERR_DEVICE; }
+    for (int i = 0; i < n; ++i) {
+        const int o = c->desc_out_host[i];
+        c->step_has_logits[i] = o >= 0;
+        if (o < 0) continue;
+        std::memcpy(&c->step_logits[(size_t)i * ncb * av], c->h_logits + (size_t)o * ncb * av, (size_t)ncb * av * 4);
+        if (out_codes) std::memcpy(out_codes + (size_t)i * ncb, c->h_codes + (size_t)o * ncb, (size_t)ncb * 4);
+        if (out_logits) std::memcpy(out_logits + (size_t)i * ncb * av, c->h_logits + (size_t)o * ncb * av, (size_t)ncb * av * 4);
+    }
+    account(c, descs, n, T);
+    return Z2B_OK;
+}
+
+void account(Ctx* c, const z2b_slot_desc* descs, int n, int T) {
+    const Model* m = c->m;
+    const Dims& D = m->dims;
+    uint64_t w = m->head_bytes, kvb = 0, other = 0;
+    for (int L = 0; L < D.n_layer; ++L) {
+        const LayerDev& ly = m->layers[L];
+        w += m->attn_bytes_per_layer;
+        const int na = (int)c->h_misc[1 + L];
+        if (ly.is_moe) {
+            w += m->router_bytes_per_layer;
+            w += (uint64_t)na * ((ly.gate_exps.gguf_bytes + ly.up_exps.gguf_bytes + ly.down_exps.gguf_bytes) / ly.n_expert);
+        } else {
+            w += ly.gate_exps.gguf_bytes + ly.up_exps.gguf_bytes + ly.down_exps.gguf_bytes;
+        }
+    }
+    const uint64_t kv_tok = (uint64_t)D.n_layer * 2 * D.n_head_kv * D.head_dim * 2;
+    for (int i = 0; i < n; ++i)
+        for (int r = 0; r < descs[i].n_new; ++r) kvb += (uint64_t)(descs[i].n_past + r + 1) * kv_tok;
+    kvb += (uint64_t)T * kv_tok;                       // writes
+    other = (uint64_t)T * NCOL * m->emb_row_bytes;
+    c->last_wbytes = w; c->last_kvbytes = kvb; c->last_other = other;
+}
+
+int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits) {
+    if (n0 < 1 || n0 > c->slot_cap) { set_error("prefill n0 out of range"); return Z2B_ERR_ARG; }
+    const int chunk = c->T_max;
+    for (int off = 0; off < n0; off += chunk) {
+        const int nn = std::min(chunk, n0 - off);
+        const bool last = off + nn == n0;
+        z2b_slot_desc d{slot, off, nn, last ? Z2B_WANT_LOGITS : 0, -1, 1.0f};
+        const int rc = ctx_step(c, &d, 1, ids + (size_t)off * NCOL, nullptr, last ? out_logits : nullptr);
+        if (rc) return rc;
+    }
+    return Z2B_OK;
+}
+
+int ctx_decode_loop(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps) {
+    const Dims& D = c->m->dims;
+    if (!descs || !first_ids || n_steps < 1) { set_error("bad decode-loop arguments"); return Z2B_ERR_ARG; }
+    for (int i = 0; i < n; ++i)
+        if (descs[i].n_new != 1 || (descs[i].flags & Z2B_WANT_SAMPLE) != Z2B_WANT_SAMPLE) {
+            set_error("decode loop needs n_new == 1 and Z2B_WANT_SAMPLE for every stream");
+            return Z2B_ERR_ARG;
+        }
+    int T, n_out;
+    c->desc_out_host.assign(n, -1);
+    int rc = ctx_prepare(c, descs, n, n_steps - 1, &T, &n_out);
+    if (rc) return rc;
+    const int ncb = D.n_codebooks;
+    std::memcpy(c->h_stage + c->st_ids, first_ids, (size_t)T * NCOL * 4);
+    // uniforms for every step, drawn in step order
+    const size_t per = (size_t)n_out * ncb;
+    if (c->canon_all_cap < per * n_steps) {
+        if (c->d_canon_all) cudaFree(c->d_canon_all);
+        if (c->h_canon_all) cudaFreeHost(c->h_canon_all);
+        CK(cudaMalloc(&c->d_canon_all, per * n_steps * 8));
+        CK(cudaMallocHost(&c->h_canon_all, per * n_steps * 8));
+        c->canon_all_cap = per * n_steps;
+    }
+    for (int s = 0; s < n_steps; ++s) draw_canon(c, descs, n, c->h_canon_all + per * s);
+    CK(cudaMemcpyAsync(c->d_stage, c->h_stage, c->st_bytes, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_canon_all, c->h_canon_all, per * n_steps * 8, cudaMemcpyHostToDevice, c->stream));
+    // desc_out on the device is written by the pack kernel of the first step
+    SlotDesc* d_descs = (SlotDesc*)(c->d_stage + c->st_descs);
+    int* d_ids = (int*)(c->d_stage + c->st_ids);
+    double* d_canon = (double*)(c->d_stage + c->st_canon);
+    for (int s = 0; s < n_steps; ++s) {
+        launch_feed(d_descs, n, d_ids, c->B.codes, c->B.desc_out, d_canon, c->d_canon_all + per * s, ncb,
+                    D.text_vocab, s > 0 ? 1 : 0, c->stream);
+        rc = run_step(c, T, n_out);
+        if (rc) return rc;
+    }
+    c->loop_launches = c->launches + 1;
+    return Z2B_OK;
+}
+
+int ctx_sync(Ctx* c) {
+    CK(cudaMemcpyAsync(c->h_misc, c->B.err, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (c->h_misc[0]) { set_error("device error flags 0x" + std::to_string(c->h_misc[0])); return Z2B_ERR_DEVICE; }
+    return Z2B_OK;
+}
+
+}  // namespace z2b

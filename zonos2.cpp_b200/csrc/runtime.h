@@ -1,0 +1,78 @@
+// runtime.h — batch context (host side of the decode step).
+#pragma once
+
+#include "kernels.h"
+#include "model.h"
+#include "../../include/z2b.h"
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <random>
+#include <string>
+#include <vector>
+
+namespace z2b {
+
+struct Ctx {
+    Model* m = nullptr;
+    cudaStream_t stream = nullptr;
+    int n_slots = 0, slot_cap = 0, pages_per_slot = 0;
+    int T_max = 0, O_max = 0, D_max = 0, R_max = 0, kmax = 1;
+    int split_keys = 256, max_split = 1;
+    // KV page pool and the host page allocator
+    int n_pages = 0;
+    size_t head_elems = 0, layer_elems = 0, page_elems = 0;
+    __half* kv_pool = nullptr;
+    std::vector<int> free_pages;
+    std::vector<std::vector<int>> slot_pages;
+    std::vector<int> h_pt;                   // [n_slots][pages_per_slot]
+    KVDev kv{};
+    // per-step staging: page table | descs | ids | canon (pinned host + device mirror)
+    size_t st_pt = 0, st_descs = 0, st_ids = 0, st_canon = 0, st_bytes = 0;
+    uint8_t* h_stage = nullptr;
+    uint8_t* d_stage = nullptr;
+    StepBufs B{};
+    // sampler state
+    SampDev* d_samp = nullptr;
+    std::vector<SampDev> h_samp;
+    std::vector<int> greedy;
+    std::vector<std::mt19937> rng;
+    int* d_hist = nullptr;
+    int* d_hist_len = nullptr;
+    int hist_cap = 0;
+    // outputs
+    int32_t* h_codes = nullptr;
+    float* h_logits = nullptr;
+    uint32_t* h_misc = nullptr;              // [0] error word, [1..] active experts per layer
+    std::vector<float> step_logits;
+    std::vector<char> step_has_logits;
+    std::vector<int> desc_out_host;
+    int cur_n_desc = 0;
+    // graphs keyed by (n_desc, T, n_out)
+    bool graphs_enabled = true;
+    std::map<uint64_t, cudaGraphExec_t> graphs;
+    std::map<uint64_t, int> graph_launches;
+    int launches = 0, loop_launches = 0;
+    // decode-loop uniforms
+    double* d_canon_all = nullptr;
+    double* h_canon_all = nullptr;
+    size_t canon_all_cap = 0;
+    // accounting of the last step
+    uint64_t last_wbytes = 0, last_kvbytes = 0, last_other = 0;
+    std::vector<void*> dallocs, hallocs;
+    ~Ctx();
+};
+
+void set_error(const std::string& e);
+const char* last_error();
+int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out);
+int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp);
+int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes, float* out_logits);
+int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits);
+int ctx_decode_loop(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps);
+int ctx_sync(Ctx* c);
+void enqueue_step(Ctx* c, int T, int n_out);
+void account(Ctx* c, const z2b_slot_desc* descs, int n, int T);
+
+}  // namespace z2b

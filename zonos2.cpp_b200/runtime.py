@@ -1,0 +1,260 @@
+"""ctypes binding of include/z2b.h — the Python host mirror of the reference batch API.
+
+Names follow src/zonos2.h: ``Model`` (zonos2_model_load / _free), ``BatchCtx``
+(zonos2_batch_init / _free, zonos2_batch_slot_prefill, zonos2_batch_step,
+zonos2_batch_slot_logits) and ``Slot`` (zonos2_slot, with the per-frame EOS logic of
+zonos2_slot_sample, src/zonos2-graph.cpp:843-870). Sampling itself runs on the device.
+Every call raises ``Z2BError`` when the library returns an error; there is no fallback
+path — without libz2b.so and a CUDA device nothing here works.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .build import LIB
+
+NCOL = 10
+WANT_LOGITS = 1
+WANT_SAMPLE = 3
+
+
+class Z2BError(RuntimeError):
+    def __init__(self, rc, msg):
+        super().__init__(f"z2b error {rc}: {msg}")
+        self.rc = rc
+
+
+class HParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in ("n_layer", "n_embd", "head_dim", "n_head", "n_head_kv", "n_ff",
+                                                "n_expert", "n_ctx_train")] + \
+               [(n, ctypes.c_float) for n in ("rope_freq_base", "rms_eps", "qk_norm_eps", "logit_softcap")] + \
+               [(n, ctypes.c_uint32) for n in ("n_codebooks", "codebook_size", "audio_vocab", "eoa_id",
+                                                "audio_pad_id", "text_vocab", "spk_dim", "spk_lda_dim",
+                                                "router_dim")] + \
+               [("expert_used", ctypes.c_int32 * 128), ("weight_bytes", ctypes.c_uint64)]
+
+
+class Sampling(ctypes.Structure):
+    """zonos2_sampling (src/zonos2.h:197-208) with the reference defaults."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
+                ("min_p", ctypes.c_float), ("rep_penalty", ctypes.c_float), ("rep_window", ctypes.c_int32),
+                ("rep_codebooks", ctypes.c_int32), ("seed", ctypes.c_uint32), ("greedy", ctypes.c_int32)]
+
+    def __init__(self, temperature=1.15, top_k=106, top_p=0.0, min_p=0.18, rep_penalty=1.2, rep_window=50,
+                 rep_codebooks=8, seed=0, greedy=False):
+        super().__init__(temperature, top_k, top_p, min_p, rep_penalty, rep_window, rep_codebooks, seed,
+                         1 if greedy else 0)
+
+
+class SlotDesc(ctypes.Structure):
+    _fields_ = [("slot", ctypes.c_int32), ("n_past", ctypes.c_int32), ("n_new", ctypes.c_int32),
+                ("flags", ctypes.c_int32), ("cfg_twin", ctypes.c_int32), ("cfg_scale", ctypes.c_float)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libz2b.so (built in-tree by __graft_entry__.build() / build.py)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            raise Z2BError(-1, f"{LIB} is not built; run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB)
+        P, I, V = ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p
+        sig = {
+            "z2b_model_load": ([ctypes.c_char_p, I, ctypes.POINTER(P)], I),
+            "z2b_model_free": ([P], I),
+            "z2b_model_hparams": ([P, ctypes.POINTER(HParams)], I),
+            "z2b_set_expert_mask": ([P, V, I, V, V], I),
+            "z2b_ctx_create": ([P, I, I, ctypes.POINTER(P)], I),
+            "z2b_ctx_destroy": ([P], I),
+            "z2b_slot_reset": ([P, I, ctypes.POINTER(Sampling)], I),
+            "z2b_slot_prefill": ([P, I, V, I, V], I),
+            "z2b_step": ([P, V, I, V, V, V], I),
+            "z2b_step_logits": ([P, I], ctypes.POINTER(ctypes.c_float)),
+            "z2b_decode_loop": ([P, V, I, V, I], I),
+            "z2b_sync": ([P], I),
+            "z2b_ctx_stream": ([P], P),
+            "z2b_last_step_bytes": ([P, V, V, V], I),
+            "z2b_last_step_launches": ([P], I),
+            "z2b_last_error": ([], ctypes.c_char_p),
+            "z2b_test_dequant": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, I, V], I),
+            "z2b_test_gemv": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V, I, V], I),
+            "z2b_host_tiles_bytes": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
+            "z2b_host_repack": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V], I),
+            "z2b_host_unpack_tiles": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V], I),
+        }
+        for name, (args, res) in sig.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def _check(rc):
+    if rc != 0:
+        raise Z2BError(rc, lib().z2b_last_error().decode(errors="replace"))
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+class Model:
+    """A zonos2 GGUF loaded onto one GPU (zonos2_model)."""
+
+    def __init__(self, path: str, device: int = 0):
+        h = ctypes.c_void_p()
+        _check(lib().z2b_model_load(path.encode(), device, ctypes.byref(h)))
+        self.h = h
+        self.hp = HParams()
+        _check(lib().z2b_model_hparams(self.h, ctypes.byref(self.hp)))
+
+    def set_expert_mask(self, keep: dict[int, list[int]]):
+        layers = np.array(sorted(keep), np.int32)
+        offs, ids = [0], []
+        for L in layers:
+            ids += list(keep[int(L)])
+            offs.append(len(ids))
+        offs = np.array(offs, np.int32)
+        ids = np.array(ids or [0], np.int32)
+        _check(lib().z2b_set_expert_mask(self.h, _ptr(layers), len(layers), _ptr(offs), _ptr(ids)))
+
+    def close(self):
+        if self.h:
+            lib().z2b_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class Slot:
+    """zonos2_slot: graph-facing per-stream state owned by the caller."""
+    index: int
+    n_past: int = 0
+    step: int = 0
+    eos_frame: int = -1
+    countdown: int = -1
+    done: bool = False
+    next_ids: list = field(default_factory=list)
+
+
+class BatchCtx:
+    """Continuous-batching context (zonos2_batch_ctx) on one GPU."""
+
+    def __init__(self, model: Model, n_slots: int, slot_cap_frames: int):
+        self.model = model
+        h = ctypes.c_void_p()
+        _check(lib().z2b_ctx_create(model.h, n_slots, slot_cap_frames, ctypes.byref(h)))
+        self.h = h
+        hp = model.hp
+        self.ncb, self.av = hp.n_codebooks, hp.audio_vocab
+        self.n_slots = n_slots
+
+    def close(self):
+        if self.h:
+            lib().z2b_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def slot_reset(self, slot: int, sampling: Sampling | None = None):
+        _check(lib().z2b_slot_reset(self.h, slot, ctypes.byref(sampling) if sampling else None))
+
+    def slot_prefill(self, slot: int, ids) -> np.ndarray:
+        """zonos2_batch_slot_prefill: returns the last prompt row's logits [ncb, av]."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1, NCOL)
+        out = np.empty((self.ncb, self.av), np.float32)
+        _check(lib().z2b_slot_prefill(self.h, slot, _ptr(ids), ids.shape[0], _ptr(out)))
+        return out
+
+    def step(self, descs, ids, want_logits=True):
+        """One batched step. descs: list of (slot, n_past, n_new, flags[, cfg_twin, cfg_scale]).
+        Returns (codes [n, ncb] int32, logits [n, ncb, av] or None)."""
+        n = len(descs)
+        arr = (SlotDesc * n)()
+        for i, d in enumerate(descs):
+            d = tuple(d) + (-1, 1.0)[len(d) - 4:] if len(d) < 6 else tuple(d)
+            arr[i] = SlotDesc(int(d[0]), int(d[1]), int(d[2]), int(d[3]), int(d[4]), float(d[5]))
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1, NCOL)
+        codes = np.full((n, self.ncb), -1, np.int32)
+        logits = np.empty((n, self.ncb, self.av), np.float32) if want_logits else None
+        _check(lib().z2b_step(self.h, ctypes.cast(arr, ctypes.c_void_p), n, _ptr(ids), _ptr(codes), _ptr(logits)))
+        return codes, logits
+
+    def decode_loop(self, descs, first_ids, n_steps: int):
+        n = len(descs)
+        arr = (SlotDesc * n)()
+        for i, d in enumerate(descs):
+            arr[i] = SlotDesc(int(d[0]), int(d[1]), 1, WANT_SAMPLE, -1, 1.0)
+        first_ids = np.ascontiguousarray(first_ids, np.int32).reshape(-1, NCOL)
+        _check(lib().z2b_decode_loop(self.h, ctypes.cast(arr, ctypes.c_void_p), n, _ptr(first_ids), n_steps))
+
+    def sync(self):
+        _check(lib().z2b_sync(self.h))
+
+    def stream(self) -> int:
+        return lib().z2b_ctx_stream(self.h) or 0
+
+    def last_step_bytes(self):
+        w, k, o = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        _check(lib().z2b_last_step_bytes(self.h, ctypes.byref(w), ctypes.byref(k), ctypes.byref(o)))
+        return w.value, k.value, o.value
+
+    def last_step_launches(self) -> int:
+        return lib().z2b_last_step_launches(self.h)
+
+
+def slot_after_sample(hp: HParams, s: Slot, codes, max_frames: int) -> None:
+    """EOS / countdown / next_ids bookkeeping of zonos2_slot_sample (src/zonos2-graph.cpp:852-868)."""
+    ncb = hp.n_codebooks
+    frame_idx = s.step
+    max_eoa = -1
+    for cb in range(ncb):
+        if int(codes[cb]) == hp.eoa_id:
+            max_eoa = cb
+    if s.eos_frame < 0 and max_eoa >= 0:
+        s.eos_frame = max(0, frame_idx - max_eoa)
+        s.countdown = ncb + 1
+    finished = False
+    if s.countdown > 0:
+        s.countdown -= 1
+        finished = s.countdown == 0
+    s.next_ids = [int(c) for c in codes[:ncb]] + [hp.text_vocab]
+    s.step += 1
+    if finished or s.step >= max_frames:
+        s.done = True
+
+
+def test_dequant(qtype: int, rows: int, k: int, raw: np.ndarray, from_tiles: bool) -> np.ndarray:
+    out = np.empty((rows, k), np.float32)
+    raw = np.ascontiguousarray(raw)
+    rc = lib().z2b_test_dequant(qtype, rows, k, _ptr(raw), 1 if from_tiles else 0, _ptr(out))
+    if rc != 0:
+        raise Z2BError(rc, "z2b_test_dequant")
+    return out
+
+
+def test_gemv(qtype: int, rows: int, k: int, raw: np.ndarray, x: np.ndarray) -> np.ndarray:
+    x16 = np.ascontiguousarray(x, np.float16)
+    out = np.empty((x16.shape[0], rows), np.float32)
+    raw = np.ascontiguousarray(raw)
+    rc = lib().z2b_test_gemv(qtype, rows, k, _ptr(raw), x16.ctypes.data_as(ctypes.c_void_p), x16.shape[0], _ptr(out))
+    if rc != 0:
+        raise Z2BError(rc, "z2b_test_gemv")
+    return out
