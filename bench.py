@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""Benchmark of the batched MoE backbone decode step.
+
+Workload (synthetic, seeded; no dataset): the ZONOS2-scale backbone (d 2048, 28 MoE
+layers, 32 experts top-4, ff 1408, 16x128 heads / 4 KV heads, Q4_K attention and expert
+gate/up, F16 expert down per the reference quantizer's fallback for ff = 1408, Q8_0
+head/router, Q6_K embeddings) with random N(0, 0.02) weights; 16 concurrent streams per
+GPU whose contexts start uniform in [64, 2048] (workload seed 1), each decoding 256
+frames before it is replaced by a new stream with a 96-row prompt (continuous batching;
+replacements are staggered and their prompt rows are packed into the decode step).
+A step = one decode step of the 16-stream batch = 16 codec frames. Greedy sampling on
+the device, as the reference's --decode-bench (src/main.cpp:107-157).
+
+value: frames/s with every step's inputs resident in HBM (z2b_run_schedule: prompt rows
+uploaded before the timed region, decode rows fed back from the device sampler), CUDA
+events on the context's stream; e2e: the same steps through the public z2b_step call
+with host buffers (per step: H2D of the input rows, D2H of the sampled frames).
+Weights streamed per step (~6-8 GB) exceed the 126 MB L2, so no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun each rank runs an independent replica on its GPU (replicas only: the
+decode path has no collective); value = frames of all ranks / max rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "codec frames/sec/GPU, batch-16 Q4_K ragged decode; MoE expert % HBM peak"
+STREAMS = 16
+STEPS_PER_STREAM = 256
+REFILL_PROMPT = 96
+CTX_RANGE = (64, 2048)
+
+
+def load_pkg():
+    if "z2b" in sys.modules:
+        return sys.modules["z2b"]
+    spec = importlib.util.spec_from_file_location(
+        "z2b", os.path.join(ROOT, "zonos2.cpp_b200", "__init__.py"),
+        submodule_search_locations=[os.path.join(ROOT, "zonos2.cpp_b200")])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["z2b"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def model_dir():
+    d = os.environ.get("Z2B_MODEL_DIR")
+    if d:
+        return d
+    for cand in ("/dev/shm/z2b_models", "/tmp/z2b_models"):
+        base = os.path.dirname(cand)
+        try:
+            if shutil.disk_usage(base).free > 12e9:
+                return cand
+        except OSError:
+            pass
+    return "/tmp/z2b_models"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def random_rows(g, n, text_vocab=519):
+    a = g.integers(0, 1024, (n, 10))
+    a[:, 9] = g.integers(0, text_vocab + 1, n)
+    return a.astype(np.int32)
+
+
+class Workload:
+    """Continuous 16-stream schedule: per step each stream decodes one frame, or, when its
+    256 frames are done, is replaced by a new stream whose 96-row prompt is prefilled in
+    that same step (its last row's logits give the new stream's first frame)."""
+
+    def __init__(self, seed=1, streams=STREAMS):
+        self.g = np.random.default_rng(seed)
+        self.n = streams
+        self.ctx0 = self.g.integers(CTX_RANGE[0], CTX_RANGE[1] + 1, streams)
+        self.remaining = self.g.integers(1, STEPS_PER_STREAM + 1, streams)    # staggered replacements
+        self.n_past = self.ctx0.copy()
+
+    def next_step(self):
+        """Returns (descs [n,6], per-stream prompt rows or None)."""
+        descs = np.zeros((self.n, 6), np.float64)
+        prompts = [None] * self.n
+        for i in range(self.n):
+            if self.remaining[i] == 0:
+                prompts[i] = random_rows(self.g, REFILL_PROMPT)
+                descs[i] = (i, 0, REFILL_PROMPT, 3, -1, 1.0)
+                self.n_past[i] = REFILL_PROMPT
+                self.remaining[i] = STEPS_PER_STREAM - 1
+            else:
+                descs[i] = (i, self.n_past[i], 1, 3, -1, 1.0)
+                self.n_past[i] += 1
+                self.remaining[i] -= 1
+        return descs, prompts
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling every 200 ms during a timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(path, seconds, cores):
+    """The CPU restatement (oracle, ggml-emu arithmetic) on the host cores: 16 streams with
+    contexts of the benchmark's distribution (KV filled with random f16 instead of a
+    prefill), decode steps until `seconds` have elapsed."""
+    sys.path.insert(0, ROOT)
+    from oracle import oracle as O
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    om = O.Model(path, O.GGML_EMU)
+    wl = Workload(seed=1)
+    c = O.Ctx(om, STREAMS, CTX_RANGE[1] + STEPS_PER_STREAM + 8)
+    for i in range(STREAMS):
+        c.fake_fill(i, int(wl.ctx0[i]), seed=i)
+    g = np.random.default_rng(3)
+    ids = random_rows(g, STREAMS)
+    past = wl.ctx0.astype(np.int32).copy()
+    c.step(list(range(STREAMS)), past, ids)           # page in the weights
+    past += 1
+    steps, t0 = 0, time.time()
+    while time.time() - t0 < seconds:
+        lg = c.step(list(range(STREAMS)), past, ids)
+        ids = np.concatenate([lg.argmax(-1).astype(np.int32), np.full((STREAMS, 1), 519, np.int32)], 1)
+        past += 1
+        steps += 1
+    dt = time.time() - t0
+    return dict(value=STREAMS * steps / dt, unit="frames/s", cores=cores, kind="port",
+                sample=f"{steps} decode steps x {STREAMS} streams (contexts U[64,2048], KV pre-filled), "
+                       f"oracle/z2o.cpp ggml-emu arithmetic, {dt:.1f}s")
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU implementation of this path timed on the host. The
+    reference cannot be built here (its ggml submodule is not vendored), so this is the
+    CPU restatement in oracle/ on all host threads."""
+    if rank != 0:
+        return
+    z2b = load_pkg()
+    import z2b.synth as S
+    path = S.cached("zonos2", directory=model_dir())
+    cores = os.cpu_count() or 1
+    budget = float(os.environ.get("Z2B_REF_SECONDS", "60"))
+    cb = cpu_baseline(path, budget, cores)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (ggml-emu: int8 activations for quantised weights)",
+            "data": "synthetic", "config": {"workload": workload_name(), "streams": STREAMS},
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "frames/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_name():
+    return (f"config2: ZONOS2-scale Q4_K backbone, {STREAMS} streams/GPU, ctx U[{CTX_RANGE[0]},{CTX_RANGE[1]}], "
+            f"{STEPS_PER_STREAM} frames per stream, continuous refill with {REFILL_PROMPT}-row prompts")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=float(os.environ.get("Z2B_CPU_SECONDS", "20")))
+    ap.add_argument("--profile-steps", type=int, default=16)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    z2b = load_pkg()
+    import z2b.runtime as R
+    import z2b.synth as S
+    mdir = model_dir()
+    if rank == 0 or world == 1:
+        path = S.cached("zonos2", directory=mdir)
+    if dist:
+        dist.barrier()
+        path = S.cached("zonos2", directory=mdir)
+
+    model = R.Model(path, device=local if world > 1 else 0)
+    hp = model.hp
+    ctx = R.BatchCtx(model, STREAMS, CTX_RANGE[1] + STEPS_PER_STREAM + 8)
+    ctx.set_logits_readback(False)          # frames only, as the device samples
+    wl = Workload(seed=1)
+    g = np.random.default_rng(2)
+    first = []
+    for i in range(STREAMS):
+        ctx.slot_reset(i, R.Sampling(greedy=True))
+        lg = ctx.slot_prefill(i, random_rows(g, int(wl.ctx0[i])))
+        first.append(np.r_[lg.argmax(-1), hp.text_vocab])
+    first = np.stack(first).astype(np.int32)
+
+    def build_schedule(n_steps, first_rows):
+        descs = np.zeros((n_steps, STREAMS, 6))
+        src = np.full((n_steps, STREAMS), -1, np.int32)
+        rows = [] if first_rows is None else [first_rows]
+        nrow = 0 if first_rows is None else len(first_rows)
+        for s in range(n_steps):
+            d, prompts = wl.next_step()
+            descs[s] = d
+            for i in range(STREAMS):
+                if prompts[i] is not None:
+                    src[s, i] = nrow
+                    rows.append(prompts[i])
+                    nrow += len(prompts[i])
+                elif s == 0 and first_rows is not None:
+                    src[s, i] = i
+        rows = np.concatenate(rows) if rows else np.zeros((1, 10), np.int32)
+        return descs, rows, src
+
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local if world > 1 else 0))
+    frames_per_step = STREAMS
+
+    # ---- value: device-resident scheduled run
+    d, rows, src = build_schedule(args.warmup, first)
+    ctx.run_schedule(d, rows, src)
+    ctx.sync()
+    d, rows, src = build_schedule(args.steps, None)
+    clocks = ClockSampler(local if world > 1 else 0)
+    clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ctx.run_schedule(d, rows, src)
+    e1.record(stream)
+    ctx.sync()
+    torch.cuda.synchronize()
+    value_ms = e0.elapsed_time(e1)
+    launches = ctx.last_run_launches()
+
+    # ---- kernel breakdown + routed-expert bytes: event-profiled steps of the same workload
+    def host_rows(descs, prompts, prev_codes):
+        out = []
+        for i in range(STREAMS):
+            out.append(prompts[i] if prompts[i] is not None else
+                       np.r_[prev_codes[i], hp.text_vocab][None].astype(np.int32))
+        return np.concatenate(out)
+
+    # frames the device sampled in the last scheduled step feed the host-driven steps
+    cur_rows = ctx.last_codes(STREAMS)
+    exps = model_expert_bytes(path)
+    prof_bytes = {"gateup": 0, "down": 0, "step": 0}
+    ctx.profile(True)
+    prof_steps = max(1, args.profile_steps)
+    for s_ in range(prof_steps):
+        dsc, prompts = wl.next_step()
+        cur_rows, _ = ctx.step([tuple(x) for x in dsc], host_rows(dsc, prompts, cur_rows), want_logits=False)
+        act = ctx.last_step_active()
+        T = int(dsc[:, 2].sum())
+        prof_bytes["gateup"] += int(act.sum()) * (exps["gate"] + exps["up"]) + hp.n_layer * T * hp.n_embd * 2
+        prof_bytes["down"] += int(act.sum()) * exps["down"] + hp.n_layer * T * 4 * hp.n_ff * 2
+        w, kv, o = ctx.last_step_bytes()
+        prof_bytes["step"] += w + kv + o
+    prof = ctx.profile(False)
+
+    # ---- e2e: public call with host buffers, per step H2D rows + D2H frames
+    for s in range(args.warmup):
+        dsc, prompts = wl.next_step()
+        cur_rows, _ = ctx.step([tuple(x) for x in dsc], host_rows(dsc, prompts, cur_rows), want_logits=False)
+    h2d = d2h = 0
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for s in range(args.steps):
+        dsc, prompts = wl.next_step()
+        rows = host_rows(dsc, prompts, cur_rows)
+        cur_rows, _ = ctx.step([tuple(x) for x in dsc], rows, want_logits=False)
+        hb, db = ctx.last_step_io()
+        h2d += hb
+        d2h += db
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    clk = clocks.stop()
+
+    # ---- reduce over ranks
+    t_value, t_e2e = value_ms, e2e_ms
+    if dist:
+        t = torch.tensor([value_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_value, t_e2e = float(t[0]), float(t[1])
+    if rank != 0:
+        ctx.close(); model.close()
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    hbm, peak_src = peaks()
+    gu_ms, gu_n = prof["expert_gateup_gemv"]
+    achieved = prof_bytes["gateup"] / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else None
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(tf):
+        traffic = json.load(open(tf)).get("expert_gateup_gemv_dram_bytes_per_launch")
+    step_ms_prof = sum(v[0] for v in prof.values()) / prof_steps
+    line = {
+        "metric": METRIC,
+        "value": world * frames_per_step * args.steps / (t_value * 1e-3),
+        "unit": "frames/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_value / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 (mma.sync f16 x f16 -> f32; Q4_K/F16/Q8_0 weights decoded in registers)",
+        "data": "synthetic",
+        "config": {"workload": workload_name(), "global_batch": world * STREAMS, "seq_len": "ctx U[64,2048]",
+                   "parallelism": f"replicas x{world}", "model": "zonos2 synthetic (28L, E32 top-4, Q4_K, F16 down)",
+                   "l2": "weights streamed per step (GBs) exceed L2; no flush needed",
+                   "sampling": "greedy on device"},
+        "per_gpu_frames_per_s": frames_per_step * args.steps / (t_value * 1e-3),
+        "roofline": {"bound": "hbm", "kernel": "expert gate/up grouped GEMV (Q4_K)",
+                     "achieved": achieved, "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
+                     "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": prof_bytes["gateup"] / max(gu_n, 1),
+                     "avg_launch_ms": gu_ms / max(gu_n, 1), "timing": "CUDA events around each launch, "
+                     f"{prof_steps} eager steps of the timed workload"},
+        "step_roofline": {"algorithmic_bytes_per_step": prof_bytes["step"] / prof_steps,
+                          "achieved_gbs_value": prof_bytes["step"] / prof_steps / (t_value / args.steps * 1e-3) / 1e9,
+                          "frac_value": prof_bytes["step"] / prof_steps / (t_value / args.steps * 1e-3) / 1e9 / hbm},
+        "kernel_ms_per_step": {k: v[0] / prof_steps for k, v in prof.items()},
+        "profiled_step_ms": step_ms_prof,
+        "expert_down_gbs": prof_bytes["down"] / (prof["expert_down_gemv"][0] * 1e-3) / 1e9
+        if prof["expert_down_gemv"][0] > 0 else None,
+        "e2e": {"value": world * frames_per_step * args.steps / (t_e2e * 1e-3), "unit": "frames/s",
+                "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if world == 1 and args.cpu_seconds > 0:
+        line["cpu_baseline"] = cpu_baseline(path, args.cpu_seconds, os.cpu_count() or 1)
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def model_expert_bytes(path):
+    """GGUF bytes of one expert's gate / up / down matrices (first MoE layer)."""
+    from gguf import GGUFReader
+    r = GGUFReader(path)
+    t = {x.name: x for x in r.tensors}
+    out = {}
+    for k, nm in (("gate", "ffn_gate_exps"), ("up", "ffn_up_exps"), ("down", "ffn_down_exps")):
+        x = t[f"blk.0.{nm}.weight"]
+        out[k] = int(x.n_bytes) // int(x.shape[2])
+    return out
+
+
+if __name__ == "__main__":
+    main()

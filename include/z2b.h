@@ -103,15 +103,44 @@ int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* 
 int z2b_step(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* ids,
              int32_t* out_codes, float* out_logits);
 
-/* Logits of desc `index` of the last step (host copy, valid until the next step).
+/* Logits of desc `index` of the last step (host copy, valid until the next step; NULL
+ * when logits readback is off and the step was given no out_logits).
  * Replaces zonos2_batch_slot_logits (src/zonos2.h:298). */
 const float* z2b_step_logits(const z2b_ctx* ctx, int index);
+/* Logits readback to the host after every step (default on, as the reference reads all
+ * logits each step). Off: only the sampled frames cross PCIe unless a step passes
+ * out_logits. */
+int z2b_set_logits_readback(z2b_ctx* ctx, int enable);
+/* Bytes the last z2b_step copied host->device (inputs) and device->host (outputs). */
+int z2b_last_step_io(const z2b_ctx* ctx, uint64_t* h2d_bytes, uint64_t* d2h_bytes);
 
 /* Device-resident decode loop for throughput runs: n_steps decode steps over the same
  * streams, each step feeding every stream its previous sampled frame (+ text pad) and
  * advancing n_past on the device; descs[i].n_new must be 1. Returns when all steps are
  * enqueued (asynchronous on the context's stream). */
 int z2b_decode_loop(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps);
+/* Scheduled device-resident run of n_steps steps over n streams (desc i stays on one
+ * slot). descs[s*n + i] is stream i's work at step s; every desc must want logits. Rows
+ * of stream i at step s come from rows[row_src[s*n+i] ..] when row_src >= 0 (prompts,
+ * first rows), or, with n_new == 1 and row_src < 0, from the frame the device sampled
+ * for stream i at step s-1 (+ text pad; at s = 0, the previous step run on this context
+ * with the same streams), so no host round trip sits between steps.
+ * Asynchronous on the context's stream. The continuous-batching benchmark uses it to
+ * replay arrivals (prompt prefills packed into decode steps) and decodes. */
+int z2b_run_schedule(z2b_ctx* ctx, int n_steps, int n, const z2b_slot_desc* descs, const int32_t* rows,
+                     int n_rows, const int32_t* row_src);
+/* Frames sampled for the first n output rows by the last step run on the context (also
+ * after z2b_run_schedule / z2b_decode_loop): out[n][n_codebooks]. Synchronises. */
+int z2b_last_codes(z2b_ctx* ctx, int32_t* out, int n);
+/* Kernel launches issued by the last z2b_run_schedule. */
+long z2b_last_run_launches(const z2b_ctx* ctx);
+/* Per-kernel-class device time: enable = 1 starts recording CUDA events around every
+ * launch (steps then run without graphs); enable = 0 stops, synchronises and returns
+ * milliseconds and launch counts per class (pack, embed, qkv, rope, attention,
+ * attention combine, wo, router, expert gate/up, expert down, combine, head, sampler,
+ * feed). */
+int z2b_profile(z2b_ctx* ctx, int enable, double* ms_per_class, long* count_per_class, int n_classes);
+
 /* Wait for all work on the context's stream and report device errors. */
 int z2b_sync(z2b_ctx* ctx);
 /* The context's cudaStream_t (for event timing by the caller). */
@@ -122,6 +151,9 @@ void* z2b_ctx_stream(z2b_ctx* ctx);
 int z2b_last_step_bytes(const z2b_ctx* ctx, uint64_t* weight_bytes, uint64_t* kv_bytes, uint64_t* other_bytes);
 /* Kernel launches issued by the last z2b_step / per decode-loop step. */
 int z2b_last_step_launches(const z2b_ctx* ctx);
+/* Experts that received routes in each layer during the last z2b_step (n_layer values;
+ * returns n_layer). */
+int z2b_last_step_active(const z2b_ctx* ctx, int32_t* out, int cap);
 
 const char* z2b_last_error(void);
 

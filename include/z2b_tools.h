@@ -58,6 +58,21 @@ int z2b_test_dequant(uint32_t type, int64_t rows, int64_t k, const void* gguf_ro
 int z2b_test_gemv(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, const uint16_t* x_f16,
                   int n_tok, float* out);
 
+/* Device packer on host descriptors {slot, n_past, n_new, flags(bit0 = output)}[n] with
+ * T = sum(n_new): per-token slot, position, output row (-1 if none) and the token of each
+ * output row. */
+int z2b_test_pack(const int32_t* desc4, int n, int T, int32_t* tok_slot, int32_t* tok_pos, int32_t* tok_out,
+                  int32_t* out_tok);
+/* Device segment builder on given router ids sel[T][k] and weights: expert offsets
+ * seg_off[E+1], token of each route in expert order, and the position of route (t, j). */
+int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
+                   int32_t* route_tok, int32_t* route_pos);
+
+/* Router ids of every layer for the last z2b_step: writes [n_layer][T][kmax] when cap is
+ * large enough; returns the number of entries (or -1). */
+struct z2b_ctx;
+int z2b_debug_last_sel(struct z2b_ctx* ctx, int32_t* out, int cap);
+
 #ifdef __cplusplus
 }
 #endif

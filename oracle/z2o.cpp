@@ -691,16 +691,18 @@ int o_last_sel(void* ctx, int32_t* out, int cap) {
 void o_ctx_fake_fill(void* ctx, int slot, int n, uint32_t seed) {
     OCtx* c = (OCtx*)ctx;
     const OHp& hp = c->m->hp;
-    std::mt19937 g(seed);
-    std::normal_distribution<float> nd(0.0f, 1.0f);
     const size_t row = (size_t)hp.n_head_kv * hp.head_dim;
-    for (int L = 0; L < hp.n_layer; ++L)
+#pragma omp parallel for schedule(dynamic)
+    for (int L = 0; L < hp.n_layer; ++L) {
+        std::mt19937 g(seed * 1000u + (uint32_t)L);
+        std::normal_distribution<float> nd(0.0f, 1.0f);
         for (int p = 0; p < n && p < c->cap; ++p)
             for (size_t i = 0; i < row; ++i) {
                 const size_t at = ((size_t)slot * c->cap + p) * row + i;
                 c->K[L][at] = f2h(nd(g));
                 c->V[L][at] = f2h(nd(g));
             }
+    }
 }
 
 void o_dequant(uint32_t type, const void* data, int64_t n, float* out) { deq(type, (const uint8_t*)data, out, n); }

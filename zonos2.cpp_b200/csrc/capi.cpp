@@ -112,6 +112,42 @@ int z2b_decode_loop(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32
     return ctx_decode_loop(ctx->c, descs, n, first_ids, n_steps);
 }
 
+int z2b_run_schedule(z2b_ctx* ctx, int n_steps, int n, const z2b_slot_desc* descs, const int32_t* rows, int n_rows,
+                     const int32_t* row_src) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_run_schedule(ctx->c, n_steps, n, descs, rows, n_rows, row_src);
+}
+
+long z2b_last_run_launches(const z2b_ctx* ctx) { return ctx ? ctx->c->sched_launches : -1; }
+
+int z2b_profile(z2b_ctx* ctx, int enable, double* ms_per_class, long* count_per_class, int n_classes) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    Ctx* c = ctx->c;
+    cudaSetDevice(c->m->device);
+    if (enable) {
+        c->profiling = true;
+        c->prof_used = 0;
+        c->prof_class.clear();
+        c->prof_ms.assign(PC_N, 0.0);
+        c->prof_count.assign(PC_N, 0);
+        return Z2B_OK;
+    }
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) { set_error("sync failed"); return Z2B_ERR_CUDA; }
+    for (size_t i = 0; i < c->prof_class.size(); ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, c->prof_ev[2 * i], c->prof_ev[2 * i + 1]);
+        c->prof_ms[c->prof_class[i]] += ms;
+        c->prof_count[c->prof_class[i]] += 1;
+    }
+    c->profiling = false;
+    for (int i = 0; i < n_classes && i < PC_N; ++i) {
+        if (ms_per_class) ms_per_class[i] = c->prof_ms.empty() ? 0.0 : c->prof_ms[i];
+        if (count_per_class) count_per_class[i] = c->prof_count.empty() ? 0 : c->prof_count[i];
+    }
+    return Z2B_OK;
+}
+
 int z2b_sync(z2b_ctx* ctx) {
     if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
     cudaSetDevice(ctx->c->m->device);
@@ -130,6 +166,51 @@ int z2b_last_step_bytes(const z2b_ctx* ctx, uint64_t* weight_bytes, uint64_t* kv
 
 int z2b_last_step_launches(const z2b_ctx* ctx) { return ctx ? ctx->c->launches : -1; }
 
+int z2b_last_step_io(const z2b_ctx* ctx, uint64_t* h2d_bytes, uint64_t* d2h_bytes) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    if (h2d_bytes) *h2d_bytes = ctx->c->last_h2d;
+    if (d2h_bytes) *d2h_bytes = ctx->c->last_d2h;
+    return Z2B_OK;
+}
+
+int z2b_set_logits_readback(z2b_ctx* ctx, int enable) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    ctx->c->keep_logits = enable != 0;
+    return Z2B_OK;
+}
+
+int z2b_last_codes(z2b_ctx* ctx, int32_t* out, int n) {
+    if (!ctx || !out) { set_error("null argument"); return Z2B_ERR_ARG; }
+    Ctx* c = ctx->c;
+    if (n < 0 || n > c->O_max) { set_error("row count out of range"); return Z2B_ERR_ARG; }
+    cudaSetDevice(c->m->device);
+    const size_t bytes = (size_t)n * c->m->dims.n_codebooks * 4;
+    if (cudaMemcpyAsync(out, c->B.codes, bytes, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess) { set_error("cudaMemcpy failed"); return Z2B_ERR_CUDA; }
+    return Z2B_OK;
+}
+
+int z2b_last_step_active(const z2b_ctx* ctx, int32_t* out, int cap) {
+    if (!ctx) return -1;
+    const int L = ctx->c->m->dims.n_layer;
+    for (int i = 0; i < L && i < cap; ++i) out[i] = (int32_t)ctx->c->h_misc[1 + i];
+    return L;
+}
+
 const char* z2b_last_error(void) { return last_error(); }
+
+int z2b_debug_last_sel(z2b_ctx* ctx, int32_t* out, int cap) {
+    if (!ctx) return -1;
+    Ctx* c = ctx->c;
+    const int L = c->m->dims.n_layer, T = c->last_T, k = c->kmax;
+    const int need = L * T * k;
+    if (out && cap >= need) {
+        cudaSetDevice(c->m->device);
+        for (int l = 0; l < L; ++l)
+            if (cudaMemcpy(out + (size_t)l * T * k, c->B.sel_log + (size_t)l * c->T_max * k, (size_t)T * k * 4,
+                           cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    }
+    return need;
+}
 
 }  // extern "C"

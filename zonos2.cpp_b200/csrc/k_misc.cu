@@ -4,6 +4,8 @@
 #include "kernels.h"
 #include "quant.h"
 
+#include <vector>
+
 namespace z2b {
 
 namespace {
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(256) sampler_kernel(const StepBufs b, const Sa
     }
     for (int i = threadIdx.x; i < av; i += blockDim.x) {
         float v = lg[i];
-        if (lu) v = lu[i] + D.cfg_scale * (v - lu[i]);       // src/zonos2-graph.cpp:917-918
+        if (lu) v = __fadd_rn(lu[i], __fmul_rn(D.cfg_scale, __fsub_rn(v, lu[i])));   // src/zonos2-graph.cpp:917-918
         lv[i] = v;
         li[i] = i;
     }
@@ -308,7 +310,46 @@ __global__ void dequant_rows_kernel(const uint8_t* rows, uint32_t type, size_t r
     for (int j = threadIdx.x; j < K; j += blockDim.x) out[(size_t)r * K + j] = emb_elem(rows, type, row_bytes, r, j);
 }
 
+// Scheduled device loop: install step s's descriptors and input rows. Rows of streams
+// with src >= 0 come from the uploaded prompt rows; a stream with src < 0 is fed its
+// previous sampled frame (output row i of the previous step) plus the text pad.
+__global__ void sched_feed_kernel(const SlotDesc* step_descs, const int* src, int n, SlotDesc* descs, int* ids_in,
+                                  const int* codes, const int* rows, const double* canon_src, double* canon_dst,
+                                  int ncb, int text_pad) {
+    __shared__ int start[1024];
+    const int tid = threadIdx.x;
+    if (tid < n) start[tid] = step_descs[tid].n_new;
+    __syncthreads();
+    for (int off = 1; off < n; off <<= 1) {
+        int a = 0;
+        if (tid < n && tid >= off) a = start[tid - off];
+        __syncthreads();
+        if (tid < n && tid >= off) start[tid] += a;
+        __syncthreads();
+    }
+    for (int i = tid; i < n; i += blockDim.x) {
+        const SlotDesc d = step_descs[i];
+        descs[i] = d;
+        const int t0 = start[i] - d.n_new;
+        if (src[i] >= 0) {
+            for (int r = 0; r < d.n_new; ++r)
+                for (int c = 0; c < NCOL; ++c) ids_in[(t0 + r) * NCOL + c] = rows[(src[i] + r) * NCOL + c];
+        } else {
+            for (int c = 0; c < ncb; ++c) ids_in[t0 * NCOL + c] = codes[i * ncb + c];
+            ids_in[t0 * NCOL + ncb] = text_pad;
+        }
+        for (int c = 0; c < ncb; ++c) canon_dst[i * ncb + c] = canon_src[i * ncb + c];
+    }
+}
+
 }  // namespace
+
+void launch_sched_feed(const SlotDesc* step_descs, const int* src, int n, SlotDesc* descs, int* ids_in,
+                       const int* codes, const int* rows, const double* canon_src, double* canon_dst, int ncb,
+                       int text_pad, cudaStream_t s) {
+    sched_feed_kernel<<<1, 1024, 0, s>>>(step_descs, src, n, descs, ids_in, codes, rows, canon_src, canon_dst, ncb,
+                                         text_pad);
+}
 
 void launch_dequant_rows(const uint8_t* rows_dev, uint32_t type, size_t row_bytes, int rows, int K, float* out,
                          cudaStream_t s) {
@@ -343,3 +384,44 @@ void launch_sampler(const StepBufs& b, const SampDev* samp, int* hist, int* hist
 }
 
 }  // namespace z2b
+
+// Runs the device packer on host descriptors {slot, n_past, n_new, flags} (flags bit 0:
+// wants an output row) and returns the per-token slot / position / output row and the
+// token of each output row.
+extern "C" int z2b_test_pack(const int32_t* desc4, int n, int T, int32_t* tok_slot, int32_t* tok_pos,
+                             int32_t* tok_out, int32_t* out_tok) {
+    using namespace z2b;
+    if (n < 1 || n > 1024 || T < 1) return 1;
+    std::vector<SlotDesc> d(n);
+    int n_out = 0, tsum = 0;
+    for (int i = 0; i < n; ++i) {
+        d[i] = SlotDesc{desc4[4 * i], desc4[4 * i + 1], desc4[4 * i + 2], (desc4[4 * i + 3] & 1) ? (int)SD_OUTPUT : 0,
+                        -1, 1.0f, desc4[4 * i], 0};
+        n_out += (desc4[4 * i + 3] & 1) ? 1 : 0;
+        tsum += desc4[4 * i + 2];
+    }
+    if (tsum != T) return 1;
+    StepBufs b{};
+    void* base = nullptr;
+    const size_t bytes = (size_t)n * sizeof(SlotDesc) + (size_t)T * NCOL * 4 * 2 + (size_t)T * 16 + (size_t)n * 12 + 4096;
+    if (cudaMalloc(&base, bytes) != cudaSuccess) return 4;
+    cudaMemset(base, 0, bytes);
+    uint8_t* p = (uint8_t*)base;
+    auto take = [&](size_t nb) { uint8_t* r = p; p += (nb + 255) / 256 * 256; return r; };
+    b.descs = (const SlotDesc*)take(n * sizeof(SlotDesc));
+    b.n_desc = n;
+    b.ids_in = (const int*)take((size_t)T * NCOL * 4);
+    b.ids = (int*)take((size_t)T * NCOL * 4);
+    b.tok_slot = (int*)take(T * 4); b.tok_pos = (int*)take(T * 4); b.tok_desc = (int*)take(T * 4);
+    b.tok_out = (int*)take(T * 4); b.out_tok = (int*)take(n * 4); b.out_desc = (int*)take(n * 4);
+    b.desc_out = (int*)take(n * 4); b.err = (uint32_t*)take(4);
+    cudaMemcpy((void*)b.descs, d.data(), n * sizeof(SlotDesc), cudaMemcpyHostToDevice);
+    pack_kernel<<<1, 1024>>>(b, T);
+    int rc = 0;
+    if (cudaMemcpy(tok_slot, b.tok_slot, T * 4, cudaMemcpyDeviceToHost) ||
+        cudaMemcpy(tok_pos, b.tok_pos, T * 4, cudaMemcpyDeviceToHost) ||
+        cudaMemcpy(tok_out, b.tok_out, T * 4, cudaMemcpyDeviceToHost) ||
+        cudaMemcpy(out_tok, b.out_tok, (size_t)(n_out > 0 ? n_out : 1) * 4, cudaMemcpyDeviceToHost)) rc = 4;
+    cudaFree(base);
+    return rc;
+}

@@ -31,6 +31,51 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
     }
 }
 
+// Expert segments from the selected ids: routes sorted by expert, then token, then rank
+// in the token's top-k. Called by one whole block; cnt is a [MAX_EXPERTS] shared array.
+__device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
+                               int* seg_off, int* active, int* n_active, int* route_tok, float* route_w,
+                               int* route_pos) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const int R = T * k;
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int e = __ldcg(sel + (r / k) * kmax + r % k);
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int off = 0, na = 0;
+        for (int e = 0; e < E; ++e) {
+            seg_off[e] = off;
+            if (cnt[e] > 0) active[na++] = e;
+            off += cnt[e];
+        }
+        seg_off[E] = off;
+        *n_active = na;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int e = w; e < E; e += nw) {
+        if (cnt[e] == 0) continue;
+        int p = seg_off[e];
+        for (int base = 0; base < R; base += 32) {
+            const int r = base + lane;
+            const int se = r < R ? __ldcg(sel + (r / k) * kmax + r % k) : -1;
+            const unsigned m = __ballot_sync(0xffffffffu, se == e);
+            if (se == e) {
+                const int pos = p + __popc(m & ((1u << lane) - 1u));
+                const int tt = r / k, jj = r % k;
+                route_tok[pos] = tt;
+                route_w[pos] = __ldcg(selw + tt * kmax + jj);
+                route_pos[tt * kmax + jj] = pos;
+            }
+            p += __popc(m);
+        }
+    }
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(256) router_kernel(const StepBufs b, const LayerSmall ly, const Dims dm,
                                                      int first_moe, int T, int layer) {
     extern __shared__ float sh[];
@@ -115,6 +160,9 @@ __global__ void __launch_bounds__(256) router_kernel(const StepBufs b, const Lay
         b.selw[t * b.kmax] = 1.0f;
     }
 
+    if (b.sel_log && threadIdx.x == 0)
+        for (int j = 0; j < k; ++j) b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + j] = b.sel[t * b.kmax + j];
+
     // ---- last block: expert segments ----
     __threadfence();
     __syncthreads();
@@ -122,46 +170,18 @@ __global__ void __launch_bounds__(256) router_kernel(const StepBufs b, const Lay
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
-    const int R = T * k;
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        const int e = __ldcg(b.sel + (r / k) * b.kmax + r % k);
-        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-    }
-    __syncthreads();
+    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.active, b.n_active, b.route_tok, b.route_w,
+                   b.route_pos);
     if (threadIdx.x == 0) {
-        int off = 0, na = 0;
-        for (int e = 0; e < E; ++e) {
-            b.seg_off[e] = off;
-            if (cnt[e] > 0) b.active[na++] = e;
-            off += cnt[e];
-        }
-        b.seg_off[E] = off;
-        *b.n_active = na;
-        if (b.layer_active) b.layer_active[layer] = na;
+        if (b.layer_active) b.layer_active[layer] = *b.n_active;
+        *b.ticket = 0;
     }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int e = w; e < E; e += nw) {
-        if (cnt[e] == 0) continue;
-        int p = b.seg_off[e];
-        for (int base = 0; base < R; base += 32) {
-            const int r = base + lane;
-            const int se = r < R ? __ldcg(b.sel + (r / k) * b.kmax + r % k) : -1;
-            const unsigned m = __ballot_sync(0xffffffffu, se == e);
-            if (se == e) {
-                const int pos = p + __popc(m & ((1u << lane) - 1u));
-                const int tt = r / k, jj = r % k;
-                b.route_tok[pos] = tt;
-                b.route_w[pos] = __ldcg(b.selw + tt * b.kmax + jj);
-                b.route_pos[tt * b.kmax + jj] = pos;
-            }
-            p += __popc(m);
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) *b.ticket = 0;
+}
+
+__global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
+                                  int* n_active, int* route_tok, float* route_w, int* route_pos) {
+    __shared__ int cnt[MAX_EXPERTS];
+    build_segments(sel, selw, T, k, k, E, cnt, seg_off, active, n_active, route_tok, route_w, route_pos);
 }
 
 }  // namespace
@@ -178,3 +198,28 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
 }
 
 }  // namespace z2b
+
+extern "C" int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
+                              int32_t* route_tok, int32_t* route_pos) {
+    using namespace z2b;
+    if (T < 1 || k < 1 || E < 1 || E > MAX_EXPERTS) return 1;
+    int *dsel = nullptr, *dseg = nullptr, *dact = nullptr, *dna = nullptr, *dtok = nullptr, *dpos = nullptr;
+    float *dw = nullptr, *drw = nullptr;
+    int rc = 0;
+    const size_t R = (size_t)T * k;
+    if (cudaMalloc(&dsel, R * 4) || cudaMalloc(&dw, R * 4) || cudaMalloc(&dseg, (E + 1) * 4) ||
+        cudaMalloc(&dact, E * 4) || cudaMalloc(&dna, 4) || cudaMalloc(&dtok, R * 4) || cudaMalloc(&drw, R * 4) ||
+        cudaMalloc(&dpos, R * 4)) rc = 4;
+    if (!rc) {
+        cudaMemcpy(dsel, sel, R * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(dw, selw, R * 4, cudaMemcpyHostToDevice);
+        cudaMemset(dpos, 0xff, R * 4);
+        route_test_kernel<<<1, 256>>>(dsel, dw, T, k, E, dseg, dact, dna, dtok, drw, dpos);
+        if (cudaMemcpy(seg_off, dseg, (E + 1) * 4, cudaMemcpyDeviceToHost) ||
+            cudaMemcpy(route_tok, dtok, R * 4, cudaMemcpyDeviceToHost) ||
+            cudaMemcpy(route_pos, dpos, R * 4, cudaMemcpyDeviceToHost)) rc = 4;
+    }
+    cudaFree(dsel); cudaFree(dw); cudaFree(dseg); cudaFree(dact); cudaFree(dna); cudaFree(dtok); cudaFree(drw);
+    cudaFree(dpos);
+    return rc;
+}

@@ -125,6 +125,7 @@ struct StepBufs {
     int* codes;                     // [O][ncb]
     const double* canon;            // [O][ncb] host-drawn uniform(0,1) values
     int* layer_active;              // [n_layer] experts with routes, per layer (accounting)
+    int* sel_log; int sel_log_T;    // optional [n_layer][sel_log_T][kmax] record of router ids
     uint32_t* err;
 };
 
@@ -149,6 +150,9 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
                    cudaStream_t s);
 // Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the
 // next input row, advance n_past, and copy this step's host-drawn uniforms.
+void launch_sched_feed(const SlotDesc* step_descs, const int* src, int n, SlotDesc* descs, int* ids_in,
+                       const int* codes, const int* rows, const double* canon_src, double* canon_dst, int ncb,
+                       int text_pad, cudaStream_t s);
 void launch_feed(SlotDesc* descs, int n, int* ids_in, const int* codes, const int* desc_out, double* canon_dst,
                  const double* canon_src, int ncb, int text_pad, int advance, cudaStream_t s);
 void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,

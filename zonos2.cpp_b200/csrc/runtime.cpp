@@ -35,6 +35,10 @@ Ctx::~Ctx() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     if (d_canon_all) cudaFree(d_canon_all);
     if (h_canon_all) cudaFreeHost(h_canon_all);
+    if (d_sched_descs) cudaFree(d_sched_descs);
+    if (d_sched_src) cudaFree(d_sched_src);
+    if (d_sched_rows) cudaFree(d_sched_rows);
+    for (cudaEvent_t e : prof_ev) cudaEventDestroy(e);
     for (void* p : dallocs) cudaFree(p);
     for (void* p : hallocs) cudaFreeHost(p);
     if (stream) cudaStreamDestroy(stream);
@@ -106,6 +110,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     acc(4); acc(MAX_EXPERTS * 4); acc((MAX_EXPERTS + 1) * 4); acc((size_t)R * 4); acc((size_t)R * 4); acc((size_t)T * c->kmax * 4);
     acc(4); acc((size_t)R * D.n_ff * 2); acc((size_t)R * d * 4); acc((size_t)O * d * 2);
     acc((size_t)O * ncb * av * 4); acc((size_t)O * ncb * 4); acc(D.n_layer * 4); acc(4);
+    acc((size_t)D.n_layer * T * c->kmax * 4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -131,6 +136,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.hout = carve<__half>(p, (size_t)O * d); B.logits = carve<float>(p, (size_t)O * ncb * av);
     B.codes = carve<int>(p, (size_t)O * ncb); B.layer_active = carve<int>(p, D.n_layer);
     B.err = carve<uint32_t>(p, 1);
+    B.sel_log = carve<int>(p, (size_t)D.n_layer * T * c->kmax); B.sel_log_T = T;
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -195,10 +201,27 @@ int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp) {
 
 namespace {
 
+// Event pair around each launch when profiling (eager steps only).
+struct ProfScope {
+    Ctx* c; int cls; cudaEvent_t e1 = nullptr;
+    ProfScope(Ctx* c_, int cls_) : c(c_), cls(cls_) {
+        if (!c->profiling) return;
+        if (c->prof_used + 2 > c->prof_ev.size()) {
+            for (int i = 0; i < 256; ++i) { cudaEvent_t e; cudaEventCreate(&e); c->prof_ev.push_back(e); }
+        }
+        cudaEventRecord(c->prof_ev[c->prof_used], c->stream);
+        e1 = c->prof_ev[c->prof_used + 1];
+        c->prof_class.push_back(cls);
+        c->prof_used += 2;
+    }
+    ~ProfScope() { if (c->profiling) cudaEventRecord(e1, c->stream); }
+};
+
 int ctas_per_sm(int smem) { return std::max(1, std::min(4, (227 * 1024) / (smem + 1024))); }
 
 void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int T, const __half* X, int ldx,
-               float* out, int ldo, int epi, float cap) {
+               float* out, int ldo, int epi, float cap, int cls) {
+    ProfScope ps(c, cls);
     GemvParams p{};
     p.mode = GM_PROJ; p.epi = epi;
     p.type = mats[0]->type; p.K = mats[0]->K; p.chunks = mats[0]->chunks;
@@ -219,6 +242,7 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
 }
 
 void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
+    ProfScope ps(c, mode == GM_GATEUP ? PC_GATEUP : PC_DOWN);
     const Dims& D = c->m->dims;
     GemvParams p{};
     const DevMat& w0 = mode == GM_GATEUP ? ly.gate_exps : ly.down_exps;
@@ -252,8 +276,8 @@ void enqueue_step(Ctx* c, int T, int n_out) {
     B.n_desc = c->cur_n_desc;
     c->launches = 0;
     cudaMemsetAsync(B.err, 0, 4, c->stream);
-    launch_pack(B, T, n_out, c->stream); c->launches++;
-    launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->stream); c->launches++;
+    { ProfScope ps(c, PC_PACK); launch_pack(B, T, n_out, c->stream); c->launches++; }
+    { ProfScope ps(c, PC_EMBED); launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->stream); c->launches++; }
     const int hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv;
     bool first_moe = true;
     for (int L = 0; L < D.n_layer; ++L) {
@@ -261,41 +285,47 @@ void enqueue_step(Ctx* c, int T, int n_out) {
         if (ly.qkvg_fused) {
             const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
             const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
-            gemv_proj(c, mats, offs, 4, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f);
+            gemv_proj(c, mats, offs, 4, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV);
         } else {
             const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
             const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
-            for (int i = 0; i < 4; ++i) gemv_proj(c, &mats[i], &offs[i], 1, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f);
+            for (int i = 0; i < 4; ++i)
+                gemv_proj(c, &mats[i], &offs[i], 1, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV);
         }
-        launch_rope_append(B, c->kv, ly.small.attn_temp, D, L, T, c->stream); c->launches++;
-        launch_attention(B, c->kv, D, L, T, c->split_keys, c->max_split, c->stream); c->launches++;
-        launch_attn_combine(B, D, T, c->split_keys, c->max_split, c->stream); c->launches++;
+        { ProfScope ps(c, PC_ROPE); launch_rope_append(B, c->kv, ly.small.attn_temp, D, L, T, c->stream); c->launches++; }
+        { ProfScope ps(c, PC_ATTN); launch_attention(B, c->kv, D, L, T, c->split_keys, c->max_split, c->stream); c->launches++; }
+        { ProfScope ps(c, PC_ATTN_COMB); launch_attn_combine(B, D, T, c->split_keys, c->max_split, c->stream); c->launches++; }
         {
             const DevMat* mats[1] = {&ly.wo};
             const int offs[1] = {0};
-            gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f);
+            gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f, PC_WO);
         }
-        launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches++;
+        { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches++; }
         if (ly.is_moe) first_moe = false;
         gemv_moe(c, ly, GM_GATEUP);
         gemv_moe(c, ly, GM_DOWN);
         const bool last = L == D.n_layer - 1;
-        launch_moe_combine(B, ly.small, last ? nullptr : m->layers[L + 1].small.attn_norm, m->out_norm, D, T,
-                           last ? 1 : 0, c->stream);
-        c->launches++;
+        {
+            ProfScope ps(c, PC_COMBINE);
+            launch_moe_combine(B, ly.small, last ? nullptr : m->layers[L + 1].small.attn_norm, m->out_norm, D, T,
+                               last ? 1 : 0, c->stream);
+            c->launches++;
+        }
     }
     if (n_out > 0) {
         const DevMat* mats[1] = {&m->head};
         const int offs[1] = {0};
         gemv_proj(c, mats, offs, 1, n_out, B.hout, D.n_embd, B.logits, D.n_codebooks * D.audio_vocab, EPI_SOFTCAP,
-                  D.softcap);
+                  D.softcap, PC_HEAD);
+        ProfScope ps(c, PC_SAMPLER);
         launch_sampler(B, c->d_samp, c->d_hist, c->d_hist_len, c->hist_cap, D, n_out, c->stream);
         c->launches++;
     }
 }
 
 int run_step(Ctx* c, int T, int n_out) {
-    const bool use_graph = c->graphs_enabled;
+    // graphs for decode-only shapes (T == streams); steps carrying prompt rows run eagerly
+    const bool use_graph = c->graphs_enabled && !c->profiling && T == c->cur_n_desc;
     if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
     const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48);
     auto it = c->graphs.find(key);
@@ -392,28 +422,43 @@ int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int3
     if (rc) return rc;
     std::memcpy(c->h_stage + c->st_ids, ids, (size_t)T * NCOL * 4);
     draw_canon(c, descs, n, (double*)(c->h_stage + c->st_canon));
-    CK(cudaMemcpyAsync(c->d_stage, c->h_stage, c->st_bytes, cudaMemcpyHostToDevice, c->stream));
+    const int ncb = D.n_codebooks, av = D.audio_vocab;
+    // inputs: only the used part of each staging section
+    const size_t b_pt = c->h_pt.size() * 4, b_desc = (size_t)n * sizeof(SlotDesc), b_ids = (size_t)T * NCOL * 4,
+                 b_canon = (size_t)n_out * ncb * 8;
+    CK(cudaMemcpyAsync(c->d_stage + c->st_pt, c->h_stage + c->st_pt, b_pt, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_stage + c->st_descs, c->h_stage + c->st_descs, b_desc, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_stage + c->st_ids, c->h_stage + c->st_ids, b_ids, cudaMemcpyHostToDevice, c->stream));
+    if (b_canon) CK(cudaMemcpyAsync(c->d_stage + c->st_canon, c->h_stage + c->st_canon, b_canon, cudaMemcpyHostToDevice, c->stream));
+    c->last_h2d = b_pt + b_desc + b_ids + b_canon;
     rc = run_step(c, T, n_out);
     if (rc) return rc;
-    const int ncb = D.n_codebooks, av = D.audio_vocab;
+    c->last_d2h = 4 + (size_t)D.n_layer * 4;
     if (n_out > 0) {
         CK(cudaMemcpyAsync(c->h_codes, c->B.codes, (size_t)n_out * ncb * 4, cudaMemcpyDeviceToHost, c->stream));
-        CK(cudaMemcpyAsync(c->h_logits, c->B.logits, (size_t)n_out * ncb * av * 4, cudaMemcpyDeviceToHost, c->stream));
+        c->last_d2h += (size_t)n_out * ncb * 4;
+        if (out_logits || c->keep_logits) {
+            CK(cudaMemcpyAsync(c->h_logits, c->B.logits, (size_t)n_out * ncb * av * 4, cudaMemcpyDeviceToHost, c->stream));
+            c->last_d2h += (size_t)n_out * ncb * av * 4;
+        }
     }
     CK(cudaMemcpyAsync(c->h_misc, c->B.err, 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaMemcpyAsync(c->h_misc + 1, c->B.layer_active, (size_t)D.n_layer * 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    const bool have_logits = out_logits || c->keep_logits;
     const uint32_t derr = c->h_misc[0];
     if (derr) { set_error("device error flags 0x" + std::to_string(derr)); return Z2B_ERR_DEVICE; }
     for (int i = 0; i < n; ++i) {
         const int o = c->desc_out_host[i];
-        c->step_has_logits[i] = o >= 0;
+        c->step_has_logits[i] = o >= 0 && have_logits;
         if (o < 0) continue;
-        std::memcpy(&c->step_logits[(size_t)i * ncb * av], c->h_logits + (size_t)o * ncb * av, (size_t)ncb * av * 4);
+        if (have_logits)
+            std::memcpy(&c->step_logits[(size_t)i * ncb * av], c->h_logits + (size_t)o * ncb * av, (size_t)ncb * av * 4);
         if (out_codes) std::memcpy(out_codes + (size_t)i * ncb, c->h_codes + (size_t)o * ncb, (size_t)ncb * 4);
         if (out_logits) std::memcpy(out_logits + (size_t)i * ncb * av, c->h_logits + (size_t)o * ncb * av, (size_t)ncb * av * 4);
     }
     account(c, descs, n, T);
+    c->last_T = T;
     return Z2B_OK;
 }
 
@@ -490,6 +535,103 @@ int ctx_decode_loop(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* fi
         if (rc) return rc;
     }
     c->loop_launches = c->launches + 1;
+    return Z2B_OK;
+}
+
+int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, const int32_t* rows, int n_rows,
+                     const int32_t* row_src) {
+    const Dims& D = c->m->dims;
+    const int ncb = D.n_codebooks;
+    if (n_steps < 1 || n < 1 || n > c->D_max || n > c->O_max || !descs || !row_src) { set_error("bad schedule arguments"); return Z2B_ERR_ARG; }
+    std::vector<int> need(c->n_slots, 0);
+    std::vector<int> T(n_steps, 0);
+    for (int s = 0; s < n_steps; ++s) {
+        std::vector<char> seen(c->n_slots, 0);
+        for (int i = 0; i < n; ++i) {
+            const z2b_slot_desc& d = descs[(size_t)s * n + i];
+            const int src = row_src[(size_t)s * n + i];
+            if (d.slot < 0 || d.slot >= c->n_slots || seen[d.slot] || d.n_new < 1 || d.n_past < 0 ||
+                d.n_past + d.n_new > c->slot_cap || (d.flags & Z2B_WANT_LOGITS) == 0 || d.cfg_twin >= n) {
+                set_error("schedule step " + std::to_string(s) + ": invalid desc " + std::to_string(i)); return Z2B_ERR_ARG;
+            }
+            if (s > 0 && descs[(size_t)(s - 1) * n + i].slot != d.slot) { set_error("schedule must keep desc i on one slot"); return Z2B_ERR_ARG; }
+            // at s == 0 a fed-back row continues from the previous step on this context
+            if (src < 0 && d.n_new != 1) { set_error("fed-back rows need n_new == 1"); return Z2B_ERR_ARG; }
+            if (src >= 0 && (rows == nullptr || src + d.n_new > n_rows)) { set_error("schedule row index out of range"); return Z2B_ERR_ARG; }
+            seen[d.slot] = 1;
+            need[d.slot] = std::max(need[d.slot], d.n_past + d.n_new);
+            T[s] += d.n_new;
+        }
+        if (T[s] > c->T_max) { set_error("schedule step exceeds rows per step"); return Z2B_ERR_ARG; }
+    }
+    for (int sl = 0; sl < c->n_slots; ++sl) {
+        auto& pages = c->slot_pages[sl];
+        const int np = need[sl] ? (need[sl] - 1) / PAGE + 1 : 0;
+        while ((int)pages.size() < np) {
+            if (c->free_pages.empty()) { set_error("KV page pool exhausted"); return Z2B_ERR_OOM; }
+            const int pg = c->free_pages.back();
+            c->free_pages.pop_back();
+            c->h_pt[(size_t)sl * c->pages_per_slot + pages.size()] = pg;
+            pages.push_back(pg);
+        }
+    }
+    // upload schedule
+    const size_t nd = (size_t)n_steps * n;
+    auto grow = [&](void** p, size_t* cap, size_t bytes) -> bool {
+        if (*cap >= bytes) return true;
+        if (*p) cudaFree(*p);
+        *p = nullptr;
+        if (cudaMalloc(p, bytes) != cudaSuccess) { *cap = 0; return false; }
+        *cap = bytes;
+        return true;
+    };
+    if (!grow((void**)&c->d_sched_descs, &c->sched_descs_cap, nd * sizeof(SlotDesc)) ||
+        !grow((void**)&c->d_sched_src, &c->sched_src_cap, nd * 4) ||
+        !grow((void**)&c->d_sched_rows, &c->sched_rows_cap, (size_t)std::max(n_rows, 1) * NCOL * 4)) {
+        set_error("schedule buffers: cudaMalloc failed"); return Z2B_ERR_OOM;
+    }
+    std::vector<SlotDesc> sd(nd);
+    c->desc_out_host.assign(n, 0);
+    for (int i = 0; i < n; ++i) c->desc_out_host[i] = i;
+    for (size_t j = 0; j < nd; ++j) {
+        const z2b_slot_desc& d = descs[j];
+        sd[j] = SlotDesc{d.slot, d.n_past, d.n_new,
+                         SD_OUTPUT | (((d.flags & Z2B_WANT_SAMPLE) == Z2B_WANT_SAMPLE) ? SD_SAMPLE : 0),
+                         d.cfg_twin, d.cfg_scale, d.slot, 0};
+    }
+    const size_t per = (size_t)n * ncb;
+    if (c->canon_all_cap < per * n_steps) {
+        if (c->d_canon_all) cudaFree(c->d_canon_all);
+        if (c->h_canon_all) cudaFreeHost(c->h_canon_all);
+        CK(cudaMalloc(&c->d_canon_all, per * n_steps * 8));
+        CK(cudaMallocHost(&c->h_canon_all, per * n_steps * 8));
+        c->canon_all_cap = per * n_steps;
+    }
+    for (int s = 0; s < n_steps; ++s) draw_canon(c, descs + (size_t)s * n, n, c->h_canon_all + per * s);
+    std::memcpy(c->h_stage + c->st_pt, c->h_pt.data(), c->h_pt.size() * 4);
+    CK(cudaMemcpyAsync(c->d_stage, c->h_stage, c->st_bytes, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_sched_descs, sd.data(), nd * sizeof(SlotDesc), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_sched_src, row_src, nd * 4, cudaMemcpyHostToDevice, c->stream));
+    if (n_rows > 0) CK(cudaMemcpyAsync(c->d_sched_rows, rows, (size_t)n_rows * NCOL * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_canon_all, c->h_canon_all, per * n_steps * 8, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaStreamSynchronize(c->stream));          // host staging stays valid across the loop
+    c->cur_n_desc = n;
+    SlotDesc* d_descs = (SlotDesc*)(c->d_stage + c->st_descs);
+    int* d_ids = (int*)(c->d_stage + c->st_ids);
+    double* d_canon = (double*)(c->d_stage + c->st_canon);
+    long total_launches = 0;
+    for (int s = 0; s < n_steps; ++s) {
+        {
+            ProfScope ps(c, PC_FEED);
+            launch_sched_feed(c->d_sched_descs + (size_t)s * n, c->d_sched_src + (size_t)s * n, n, d_descs, d_ids,
+                              c->B.codes, c->d_sched_rows, c->d_canon_all + per * s, d_canon, ncb, D.text_vocab,
+                              c->stream);
+        }
+        const int rc = run_step(c, T[s], n);
+        if (rc) return rc;
+        total_launches += c->launches + 1;
+    }
+    c->sched_launches = total_launches;
     return Z2B_OK;
 }
 

@@ -49,6 +49,9 @@ struct Ctx {
     std::vector<char> step_has_logits;
     std::vector<int> desc_out_host;
     int cur_n_desc = 0;
+    int last_T = 0;                          // tokens of the last z2b_step
+    size_t last_h2d = 0, last_d2h = 0;       // bytes copied by the last z2b_step
+    bool keep_logits = true;                 // read logits back even without out_logits
     // graphs keyed by (n_desc, T, n_out)
     bool graphs_enabled = true;
     std::map<uint64_t, cudaGraphExec_t> graphs;
@@ -58,6 +61,21 @@ struct Ctx {
     double* d_canon_all = nullptr;
     double* h_canon_all = nullptr;
     size_t canon_all_cap = 0;
+    // per-launch profiling (eager steps only): class of each launch and its event pair
+    bool profiling = false;
+    std::vector<int> prof_class;
+    std::vector<cudaEvent_t> prof_ev;
+    size_t prof_used = 0;
+    std::vector<double> prof_ms;             // accumulated per class
+    std::vector<long> prof_count;
+    // scheduled device loop
+    int* d_sched_rows = nullptr;             // prompt rows uploaded for a schedule
+    size_t sched_rows_cap = 0;
+    SlotDesc* d_sched_descs = nullptr;
+    size_t sched_descs_cap = 0;
+    int* d_sched_src = nullptr;              // [steps][n] row offset or -1 (feed from codes)
+    size_t sched_src_cap = 0;
+    long sched_launches = 0;                 // kernel launches of the last schedule
     // accounting of the last step
     uint64_t last_wbytes = 0, last_kvbytes = 0, last_other = 0;
     std::vector<void*> dallocs, hallocs;
@@ -73,6 +91,10 @@ int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits)
 int ctx_decode_loop(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps);
 int ctx_sync(Ctx* c);
 void enqueue_step(Ctx* c, int T, int n_out);
+int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, const int32_t* rows, int n_rows,
+                     const int32_t* row_src);
+enum ProfClass { PC_PACK, PC_EMBED, PC_QKV, PC_ROPE, PC_ATTN, PC_ATTN_COMB, PC_WO, PC_ROUTER, PC_GATEUP, PC_DOWN,
+                 PC_COMBINE, PC_HEAD, PC_SAMPLER, PC_FEED, PC_N };
 void account(Ctx* c, const z2b_slot_desc* descs, int n, int T);
 
 }  // namespace z2b

@@ -83,6 +83,13 @@ def lib():
             "z2b_last_step_bytes": ([P, V, V, V], I),
             "z2b_last_step_launches": ([P], I),
             "z2b_last_error": ([], ctypes.c_char_p),
+            "z2b_last_step_active": ([P, V, I], I),
+            "z2b_last_codes": ([P, V, I], I),
+            "z2b_last_step_io": ([P, V, V], I),
+            "z2b_set_logits_readback": ([P, I], I),
+            "z2b_run_schedule": ([P, I, I, V, V, I, V], I),
+            "z2b_last_run_launches": ([P], ctypes.c_long),
+            "z2b_profile": ([P, I, V, V, I], I),
             "z2b_test_dequant": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, I, V], I),
             "z2b_test_gemv": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V, I, V], I),
             "z2b_host_tiles_bytes": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
@@ -218,6 +225,52 @@ class BatchCtx:
 
     def last_step_launches(self) -> int:
         return lib().z2b_last_step_launches(self.h)
+
+    def last_step_active(self) -> np.ndarray:
+        out = np.zeros(self.model.hp.n_layer, np.int32)
+        lib().z2b_last_step_active(self.h, _ptr(out), len(out))
+        return out
+
+    def run_schedule(self, descs: np.ndarray, rows: np.ndarray, row_src: np.ndarray):
+        """descs: int32/float [n_steps, n, 6] (slot, n_past, n_new, flags, cfg_twin, cfg_scale)."""
+        n_steps, n = descs.shape[:2]
+        arr = (SlotDesc * (n_steps * n))()
+        flat = descs.reshape(-1, 6)
+        for j in range(n_steps * n):
+            d = flat[j]
+            arr[j] = SlotDesc(int(d[0]), int(d[1]), int(d[2]), int(d[3]), int(d[4]), float(d[5]))
+        rows = np.ascontiguousarray(rows, np.int32).reshape(-1, NCOL)
+        row_src = np.ascontiguousarray(row_src, np.int32)
+        self._keep = (arr, rows, row_src)          # host copies stay alive while the run is queued
+        _check(lib().z2b_run_schedule(self.h, n_steps, n, ctypes.cast(arr, ctypes.c_void_p), _ptr(rows),
+                                      rows.shape[0], _ptr(row_src)))
+
+    def last_step_io(self):
+        h, d = ctypes.c_uint64(), ctypes.c_uint64()
+        _check(lib().z2b_last_step_io(self.h, ctypes.byref(h), ctypes.byref(d)))
+        return h.value, d.value
+
+    def set_logits_readback(self, enable: bool):
+        _check(lib().z2b_set_logits_readback(self.h, 1 if enable else 0))
+
+    def last_codes(self, n: int) -> np.ndarray:
+        out = np.zeros((n, self.ncb), np.int32)
+        _check(lib().z2b_last_codes(self.h, _ptr(out), n))
+        return out
+
+    def last_run_launches(self) -> int:
+        return int(lib().z2b_last_run_launches(self.h))
+
+    PROF_CLASSES = ["pack", "embed", "qkv_gemv", "rope_append", "attention", "attn_combine", "wo_gemv", "router",
+                    "expert_gateup_gemv", "expert_down_gemv", "moe_combine", "head_gemv", "sampler", "feed"]
+
+    def profile(self, enable: bool):
+        n = len(self.PROF_CLASSES)
+        ms = np.zeros(n, np.float64)
+        cnt = np.zeros(n, np.int64)
+        _check(lib().z2b_profile(self.h, 1 if enable else 0, _ptr(ms), _ptr(cnt), n))
+        if not enable:
+            return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(self.PROF_CLASSES)}
 
 
 def slot_after_sample(hp: HParams, s: Slot, codes, max_frames: int) -> None:
