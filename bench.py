@@ -226,6 +226,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=float(os.environ.get("Z2B_CPU_SECONDS", "20")))
     ap.add_argument("--profile-steps", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=28,
+                    help="fewer layers for small ncu captures (the headline run uses 28)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -247,11 +249,12 @@ def main():
     import z2b.runtime as R
     import z2b.synth as S
     mdir = model_dir()
+    over = {} if args.layers == 28 else dict(n_layer=args.layers, expert_used=[4] * args.layers)
     if rank == 0 or world == 1:
-        path = S.cached("zonos2", directory=mdir)
+        path = S.cached("zonos2", directory=mdir, **over)
     if dist:
         dist.barrier()
-        path = S.cached("zonos2", directory=mdir)
+        path = S.cached("zonos2", directory=mdir, **over)
 
     model = R.Model(path, device=local if world > 1 else 0)
     hp = model.hp
@@ -298,9 +301,11 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
     ctx.run_schedule(d, rows, src)
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     ctx.sync()
     torch.cuda.synchronize()
     value_ms = e0.elapsed_time(e1)
@@ -405,6 +410,8 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if args.layers != 28:
+        line["config"]["layers"] = args.layers
     if world == 1 and args.cpu_seconds > 0:
         line["cpu_baseline"] = cpu_baseline(path, args.cpu_seconds, os.cpu_count() or 1)
     print(json.dumps(line), flush=True)
