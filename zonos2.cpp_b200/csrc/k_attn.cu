@@ -17,6 +17,7 @@
 //                  key 4*(n/2) + n%2 (+2 for the second n-tile).
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace z2b {
 
@@ -34,52 +35,56 @@ template <int HD> __device__ __forceinline__ int kswz(int key) {   // K row chun
 template <int HD>
 __global__ void rope_append_kernel(const StepBufs b, const KVDev kv, const float* __restrict__ temp,
                                    const Dims dm, int layer) {
-    const int t = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    // one warp per (token, head); heads: [0, nh) q, [nh, nh+nkv) k, [nh+nkv, nh+2nkv) v
+    pdl_wait();
+    pdl_release();
+    const int t = blockIdx.x, lane = threadIdx.x & 31;
+    const int nh = dm.n_head, nkv = dm.n_head_kv;
+    const int h = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (h >= nh + 2 * nkv) return;
     const int slot = b.tok_slot[t];
     if (slot < 0) return;
-    const int pos = b.tok_pos[t], nh = dm.n_head, nkv = dm.n_head_kv;
-    const float* row = b.qkvg + (size_t)t * b.ldq;
-    const int pg = pos / PAGE, j = pos % PAGE;
-    int page = -1;
-    if (pg < kv.max_pages) page = kv.page_table[(size_t)slot * kv.max_pages + pg];
-    if (page < 0) { if (threadIdx.x == 0) atomicOr(b.err, (uint32_t)DERR_PAGE); return; }
-    __half* lbase = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
-    const float ts = powf(dm.rope_base, -2.0f / (float)HD);
-    // heads: [0, nh) q, [nh, nh+nkv) k, [nh+nkv, nh+2nkv) v
-    for (int h = w; h < nh + 2 * nkv; h += nw) {
-        const bool isq = h < nh, isk = !isq && h < nh + nkv;
-        const float* x = row + (size_t)h * HD;       // q | k | v are contiguous in qkvg
-        if (isq || isk) {
-            float ss = 0.0f;
-            for (int i = lane; i < HD; i += 32) ss += x[i] * x[i];
-            ss = warp_sum(ss);
-            const float sc = 1.0f / sqrtf(ss / (float)HD + dm.qk_eps);
-            const float tm = isq ? temp[h] : 1.0f;
-            for (int i = lane; i < HD / 2; i += 32) {
-                float x0 = x[2 * i] * sc, x1 = x[2 * i + 1] * sc;
-                if (isq) { x0 = x0 * tm; x1 = x1 * tm; }
-                float theta = (float)pos;                     // ggml rope cache: theta *= theta_scale
-                for (int k = 0; k < i; ++k) theta *= ts;
-                const float c = cosf(theta), s = sinf(theta);
-                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-                const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-                if (isq) {
-                    __half2* q = (__half2*)(b.qh + ((size_t)t * nh + h) * HD);
-                    q[i] = __floats2half2_rn(y0, y1);
-                } else {
-                    __half* kb = lbase + (size_t)(h - nh) * kv.head_elems + (size_t)j * HD;
-                    const int e = 2 * i, c16 = e / 8;
-                    __half2* dst = (__half2*)(kb + ((c16 ^ kswz<HD>(j)) * 8 + (e % 8)));
-                    *dst = __floats2half2_rn(y0, y1);
-                }
+    const int pos = b.tok_pos[t];
+    const float* x = b.qkvg + (size_t)t * b.ldq + (size_t)h * HD;    // q | k | v are contiguous
+    const bool isq = h < nh, isk = !isq && h < nh + nkv;
+    __half* lbase = nullptr;
+    const int j = pos % PAGE;
+    if (!isq) {
+        const int pg = pos / PAGE;
+        const int page = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
+        if (page < 0) { if (lane == 0) atomicOr(b.err, (uint32_t)DERR_PAGE); return; }
+        lbase = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
+    }
+    if (isq || isk) {
+        float ss = 0.0f;
+        for (int i = lane; i < HD; i += 32) ss += x[i] * x[i];
+        ss = warp_sum(ss);
+        const float sc = 1.0f / sqrtf(ss / (float)HD + dm.qk_eps);
+        const float tm = isq ? temp[h] : 1.0f;
+        const float ts = powf(dm.rope_base, -2.0f / (float)HD);
+        for (int i = lane; i < HD / 2; i += 32) {
+            float x0 = x[2 * i] * sc, x1 = x[2 * i + 1] * sc;
+            if (isq) { x0 = x0 * tm; x1 = x1 * tm; }
+            float theta = (float)pos;                     // ggml rope cache: theta *= theta_scale
+            for (int k = 0; k < i; ++k) theta *= ts;
+            const float c = cosf(theta), s = sinf(theta);
+            const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+            if (isq) {
+                __half2* q = (__half2*)(b.qh + ((size_t)t * nh + h) * HD);
+                q[i] = __floats2half2_rn(y0, y1);
+            } else {
+                __half* kb = lbase + (size_t)(h - nh) * kv.head_elems + (size_t)j * HD;
+                const int e = 2 * i, c16 = e / 8;
+                *(__half2*)(kb + ((c16 ^ kswz<HD>(j)) * 8 + (e % 8))) = __floats2half2_rn(y0, y1);
             }
-        } else {
-            const int hv = h - nh - nkv;
-            __half* vb = lbase + (size_t)(nkv + hv) * kv.head_elems + (size_t)(j / KCH) * HD * KCH;
-            const int col = j % KCH;
-            for (int i = lane; i < HD; i += 32)
-                vb[(size_t)i * KCH + (((col / 8) ^ (i & 7)) * 8) + (col % 8)] = __float2half_rn(x[i]);
         }
+    } else {
+        const int hv = h - nh - nkv;
+        __half* vb = lbase + (size_t)(nkv + hv) * kv.head_elems + (size_t)(j / KCH) * HD * KCH;
+        const int col = j % KCH;
+        for (int i = lane; i < HD; i += 32)
+            vb[(size_t)i * KCH + (((col / 8) ^ (i & 7)) * 8) + (col % 8)] = __float2half_rn(x[i]);
     }
 }
 
@@ -101,6 +106,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     uint8_t* stages = smem + 128;
     float* merge = reinterpret_cast<float*>(stages + SM::NS * SM::STAGE);
+    pdl_wait();
+    pdl_release();
     const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
     const int slot = b.tok_slot[t];
     if (slot < 0) return;
@@ -245,38 +252,70 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
         }
         b.apart[(((size_t)t * nh + hk * G + g) * max_split + sp) * (HD + 2) + e] = v;
     }
+    // The last split block of (token, kv head) to finish merges all splits of the group's
+    // heads in split order and applies the per-head sigmoid gate (src/zonos2-graph.cpp:173).
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    const int ns = (n_keys + split_keys - 1) / split_keys;
+    if (threadIdx.x == 0) {
+        int* ctr = b.attn_ticket + (size_t)t * dm.n_head_kv + hk;
+        s_last = (atomicAdd(ctr, 1) == ns - 1) ? 1 : 0;
+        if (s_last) *ctr = 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int gate_off = nh * HD + 2 * dm.n_head_kv * HD;
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+        const int g = idx / HD, e = idx % HD, h = hk * G + g;
+        const float* base = b.apart + ((size_t)t * nh + h) * max_split * (HD + 2);
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, __ldcg(base + (size_t)s2 * (HD + 2)));
+        float L = 0.0f, O = 0.0f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float* ps = base + (size_t)s2 * (HD + 2);
+            const float pm = __ldcg(ps);
+            if (pm == -INFINITY) continue;
+            const float f = expf(pm - M);
+            L += f * __ldcg(ps + 1);
+            O += f * __ldcg(ps + 2 + e);
+        }
+        const float gg = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
+        b.o[(size_t)t * nh * HD + (size_t)h * HD + e] = __float2half_rn((O / L) * gg);
+    }
     if (failed) {
         for (int c = 0; c < SM::NS; ++c) (void)mbar_try_wait(&bars[c], 0);
     }
 }
 
 // ---------------------------------------------------------------- split combine + gate
+// one block per (token, head), one thread per output dim
 template <int HD>
 __global__ void attn_combine_kernel(const StepBufs b, const Dims dm, int split_keys) {
-    const int t = blockIdx.x, nh = dm.n_head;
+    pdl_wait();
+    pdl_release();
+    const int t = blockIdx.x, h = blockIdx.y, e = threadIdx.x, nh = dm.n_head;
     const int slot = b.tok_slot[t];
-    const int gate_off = nh * HD + 2 * dm.n_head_kv * HD;
-    for (int idx = threadIdx.x; idx < nh * HD; idx += blockDim.x) {
-        const int h = idx / HD, e = idx % HD;
-        float out = 0.0f;
-        if (slot >= 0) {
-            const int ns = (b.tok_pos[t] + 1 + split_keys - 1) / split_keys;
-            const float* base = b.apart + ((size_t)t * nh + h) * b.max_split * (HD + 2);
-            float M = -INFINITY;
-            for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(size_t)s * (HD + 2)]);
-            float L = 0.0f, O = 0.0f;
-            for (int s = 0; s < ns; ++s) {
-                const float* ps = base + (size_t)s * (HD + 2);
-                if (ps[0] == -INFINITY) continue;
-                const float f = expf(ps[0] - M);
-                L += f * ps[1];
-                O += f * ps[2 + e];
-            }
-            const float g = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
-            out = (O / L) * g;
+    float out = 0.0f;
+    if (slot >= 0) {
+        const int gate_off = nh * HD + 2 * dm.n_head_kv * HD;
+        const int ns = (b.tok_pos[t] + 1 + split_keys - 1) / split_keys;
+        const float* base = b.apart + ((size_t)t * nh + h) * b.max_split * (HD + 2);
+        float M = -INFINITY;
+        for (int s = 0; s < ns; ++s) M = fmaxf(M, base[(size_t)s * (HD + 2)]);
+        float L = 0.0f, O = 0.0f;
+        for (int s = 0; s < ns; ++s) {
+            const float* ps = base + (size_t)s * (HD + 2);
+            if (ps[0] == -INFINITY) continue;
+            const float f = expf(ps[0] - M);
+            L += f * ps[1];
+            O += f * ps[2 + e];
         }
-        b.o[(size_t)t * nh * HD + idx] = __float2half_rn(out);
+        const float g = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
+        out = (O / L) * g;
     }
+    b.o[(size_t)t * nh * HD + (size_t)h * HD + e] = __float2half_rn(out);
 }
 
 template <int HD, int G>
@@ -285,7 +324,7 @@ void attn_launch_hg(const StepBufs& b, const KVDev& kv, const Dims& d, int layer
     using SM = AttnSmem<HD>;
     cudaFuncSetAttribute(attn_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
     dim3 grid(T, d.n_head_kv, max_split);
-    attn_kernel<HD, G><<<grid, 128, SM::BYTES, s>>>(b, kv, d, layer, split_keys);
+    launch_pdl(attn_kernel<HD, G>, grid, dim3(128), (size_t)SM::BYTES, s, b, kv, d, layer, split_keys);
 }
 
 template <int HD>
@@ -304,11 +343,13 @@ void attn_launch_h(const StepBufs& b, const KVDev& kv, const Dims& d, int layer,
 
 void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T,
                         cudaStream_t s) {
+    const int heads = d.n_head + 2 * d.n_head_kv;
+    dim3 grid(T, (heads + 3) / 4);
     switch (d.head_dim) {
-        case 16: rope_append_kernel<16><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
-        case 32: rope_append_kernel<32><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
-        case 64: rope_append_kernel<64><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
-        default: rope_append_kernel<128><<<T, 256, 0, s>>>(b, kv, temp, d, layer); break;
+        case 16: launch_pdl(rope_append_kernel<16>, grid, dim3(128), 0, s, b, kv, temp, d, layer); break;
+        case 32: launch_pdl(rope_append_kernel<32>, grid, dim3(128), 0, s, b, kv, temp, d, layer); break;
+        case 64: launch_pdl(rope_append_kernel<64>, grid, dim3(128), 0, s, b, kv, temp, d, layer); break;
+        default: launch_pdl(rope_append_kernel<128>, grid, dim3(128), 0, s, b, kv, temp, d, layer); break;
     }
 }
 
@@ -324,11 +365,12 @@ void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int lay
 
 void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s) {
     (void)max_split;
+    dim3 grid(T, d.n_head);
     switch (d.head_dim) {
-        case 16: attn_combine_kernel<16><<<T, 256, 0, s>>>(b, d, split_keys); break;
-        case 32: attn_combine_kernel<32><<<T, 256, 0, s>>>(b, d, split_keys); break;
-        case 64: attn_combine_kernel<64><<<T, 256, 0, s>>>(b, d, split_keys); break;
-        default: attn_combine_kernel<128><<<T, 256, 0, s>>>(b, d, split_keys); break;
+        case 16: launch_pdl(attn_combine_kernel<16>, grid, dim3(16), 0, s, b, d, split_keys); break;
+        case 32: launch_pdl(attn_combine_kernel<32>, grid, dim3(32), 0, s, b, d, split_keys); break;
+        case 64: launch_pdl(attn_combine_kernel<64>, grid, dim3(64), 0, s, b, d, split_keys); break;
+        default: launch_pdl(attn_combine_kernel<128>, grid, dim3(128), 0, s, b, d, split_keys); break;
     }
 }
 

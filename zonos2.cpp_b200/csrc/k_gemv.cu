@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "gguf.h"
 #include "kernels.h"
+#include "launch.cuh"
 #include "tile_layout.h"
 
 #include <algorithm>
@@ -36,8 +37,14 @@ template <int N> __device__ __forceinline__ uint32_t shr_signed(uint32_t x) {
 // ---- per-type decoders: prep() reads the chunk's scales, frag() builds A for k-step S ----
 template <int WT> struct Dec;
 
+// Q4_K: w = (d*sc)*q - dmin*m, decoded per pair as hfma2(q, S, -M) with q recovered
+// exactly from the magic-number extraction (1024 + q, or 1024 + 16 q for the high
+// nibbles). Rounding the centred value q*S - M once keeps the weight error relative to
+// the weight itself (rounding q*S alone and subtracting the min later doubles it).
 template <> struct Dec<GT_Q4_K> {
     static constexpr int KS = 16, KC = 256;
+    static constexpr bool kMinMma = false;
+    uint32_t amin[2] = {0u, 0u};
     __half2 S[2][2], M[2][2];                 // [sub-block 0/1][row r / r+8], M holds -min
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
@@ -72,6 +79,8 @@ template <> struct Dec<GT_Q4_K> {
 
 template <> struct Dec<GT_Q6_K> {
     static constexpr int KS = 16, KC = 256;
+    static constexpr bool kMinMma = false;
+    uint32_t amin[2] = {0u, 0u};
     __half2 S[4][2];
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
@@ -104,6 +113,8 @@ template <> struct Dec<GT_Q6_K> {
 
 template <> struct Dec<GT_Q8_0> {
     static constexpr int KS = 8, KC = 128;
+    static constexpr bool kMinMma = false;
+    uint32_t amin[2] = {0u, 0u};
     __half2 D[2];
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
@@ -124,6 +135,8 @@ template <> struct Dec<GT_Q8_0> {
 // F16 with KS k-steps per chunk (KS = 4, 2, 1)
 template <int KS_> struct DecF16 {
     static constexpr int KS = KS_, KC = 16 * KS_;
+    static constexpr bool kMinMma = false;
+    uint32_t amin[2] = {0u, 0u};
     __device__ __forceinline__ void prep(const uint8_t*, int) {}
     template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
         const uint4 w = *(const uint4*)(T + (s * 32 + lane) * 16);
@@ -199,26 +212,20 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
     const int NS = p.n_stages;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                         // [NW][NS]
     uint8_t* stages = smem + 128 * ((NW * NS * 8 + 127) / 128);                  // [NW][NS][stage_bytes]
-    float* red = reinterpret_cast<float*>(stages + (size_t)NW * NS * p.stage_bytes);   // [NW][NMAT][NTG][32][4]
+    float* red = reinterpret_cast<float*>(stages + (size_t)NW * NS * p.stage_bytes);   // [2][NW][NMAT][NTG][32][4]
     uint64_t* mybar = bars + warp * NS;
     uint8_t* mystage = stages + (size_t)warp * NS * p.stage_bytes;
 
     const int c0 = warp * p.chunks / NW, c1 = (warp + 1) * p.chunks / NW, ncw = c1 - c0;
     const uint32_t wbytes = (uint32_t)(ncw * p.tile_bytes);
 
-    int n_items;
-    if constexpr (MODE == GM_PROJ) n_items = p.total_items;
-    else n_items = (*p.n_active) * p.n_row_tiles;
-    const int it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
-    const int it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
-    if (it0 >= it1) return;
-
     if (lane == 0)
         for (int s = 0; s < NS; ++s) mbar_init(&mybar[s], 1);
     fence_mbar_init();
     __syncwarp();
 
-    int issued_upto = it0 - 1;                   // last item whose copy was issued
+    int it0 = 0, it1 = 0;
+    int issued_upto = -1;                        // last item whose copy was issued
     auto issue = [&](int item, int slot) {
         issued_upto = item;
         if (lane == 0 && ncw > 0) {
@@ -229,18 +236,38 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                 bulk_g2s(mystage + slot * p.stage_bytes + m * wbytes, it.src[m], wbytes, &mybar[slot]);
         }
     };
-    for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
+    if constexpr (MODE == GM_PROJ) {
+        // weights and the item list are static: start streaming before the predecessor ends
+        it0 = (int)((int64_t)blockIdx.x * p.total_items / gridDim.x);
+        it1 = (int)((int64_t)(blockIdx.x + 1) * p.total_items / gridDim.x);
+        issued_upto = it0 - 1;
+        for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
+        pdl_wait();
+        pdl_release();
+    } else {
+        pdl_wait();
+        pdl_release();
+        const int n_items = (*p.n_active) * p.n_row_tiles;
+        it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
+        it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
+        issued_upto = it0 - 1;
+        for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
+    }
 
     bool failed = false;
     uint32_t B[NTG][MAXKS][2];
+    uint32_t BX[NTG][MAXCPW];                    // Q4_K: activation sums of the lane's two sub-blocks
+    int b_key = -2;                              // token set the B fragments hold (expert, or 0)
+    constexpr float kAccScale = D::kMinMma ? 0.0625f : 1.0f;   // Q4_K products carry a factor 16
+    int red_par = 0;
     for (int item = it0; item < it1; ++item) {
         const int j = item - it0, slot = j % NS;
         const uint32_t parity = (uint32_t)((j / NS) & 1);
         const ItemRef it = item_ref<MODE>(p, item, c0);
         if (!failed && ncw > 0 && item <= issued_upto) failed = !mbar_wait(&mybar[slot], parity, p.err);
-        const int waited = item;
         const uint8_t* st = mystage + slot * p.stage_bytes;
         const int n_groups = (it.n_tok + 8 * NTG - 1) / (8 * NTG);
+        const int key = (MODE == GM_PROJ) ? 0 : it.expert;
         for (int g = 0; g < n_groups; ++g) {
             const int ntv = min(NTG, (it.n_tok - g * 8 * NTG + 7) / 8);
             float acc[NMAT][NTG][4];
@@ -251,21 +278,34 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
 #pragma unroll
                     for (int e = 0; e < 4; ++e) acc[m][nt][e] = 0.0f;
             if (!failed && ncw > 0) {
-                // activation fragments: token n = lane/4 of each n-tile, k = chunk*KC + q*KC/4 + 4s
+                // activation fragments: token n = lane/4 of each n-tile, k = chunk*KC + q*KC/4 + 4s;
+                // kept across items while the token set is the same
+                if (!(n_groups == 1 && key == b_key)) {
 #pragma unroll
-                for (int nt = 0; nt < NTG; ++nt) {
-                    const int n = g * 8 * NTG + nt * 8 + r8;
-                    const bool ok = nt < ntv && n < it.n_tok;
-                    const __half* xr = ok ? p.X + (size_t)x_row<MODE>(p, it, n) * p.ldx : nullptr;
+                    for (int nt = 0; nt < NTG; ++nt) {
+                        const int n = g * 8 * NTG + nt * 8 + r8;
+                        const bool ok = nt < ntv && n < it.n_tok;
+                        const __half* xr = ok ? p.X + (size_t)x_row<MODE>(p, it, n) * p.ldx : nullptr;
 #pragma unroll
-                    for (int cc = 0; cc < MAXCPW; ++cc)
+                        for (int cc = 0; cc < MAXCPW; ++cc) {
+                            float xs0 = 0.0f, xs1 = 0.0f;      // sums over the lane's two sub-blocks
 #pragma unroll
-                        for (int s = 0; s < KS; ++s) {
-                            uint2 v = make_uint2(0u, 0u);
-                            if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
-                            B[nt][cc * KS + s][0] = v.x;
-                            B[nt][cc * KS + s][1] = v.y;
+                            for (int s = 0; s < KS; ++s) {
+                                uint2 v = make_uint2(0u, 0u);
+                                if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
+                                if constexpr (D::kMinMma) {
+                                    const float2 f0 = __half22float2(u2h(v.x)), f1 = __half22float2(u2h(v.y));
+                                    const float part = (f0.x + f0.y) + (f1.x + f1.y);
+                                    if (s < KS / 2) xs0 += part; else xs1 += part;
+                                    v.x = h2u(__hmul2(u2h(v.x), hc(0x4C00)));          // x16 for the 1x pairs
+                                }
+                                B[nt][cc * KS + s][0] = v.x;
+                                B[nt][cc * KS + s][1] = v.y;
+                            }
+                            if constexpr (D::kMinMma) BX[nt][cc] = h2u(__floats2half2_rn(xs0, xs1));
                         }
+                    }
+                    b_key = (n_groups == 1) ? key : -2;
                 }
 #pragma unroll
                 for (int cc = 0; cc < MAXCPW; ++cc) {
@@ -276,6 +316,11 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                             D dec;
                             dec.prep(T, lane);
                             KLoop<D, 0, KS>::template run<NMAT>(dec, T, lane, cc * KS, B, acc, m, ntv);
+                            if constexpr (D::kMinMma) {
+#pragma unroll
+                                for (int nt = 0; nt < NTG; ++nt)
+                                    if (nt < ntv) mma1688(acc[m][nt], dec.amin[0], dec.amin[1], BX[nt][cc]);
+                            }
                         }
                     }
                 }
@@ -285,15 +330,18 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                 fence_proxy_async();
                 if (!failed && item + NS < it1) issue(item + NS, slot);
             }
-            // cross-warp reduction in a fixed order
-            float* myred = red + (size_t)warp * NMAT * NTG * 128;
+            // cross-warp reduction in a fixed order (double-buffered: one barrier per pass)
+            float* rbuf = red + (size_t)red_par * NW * NMAT * NTG * 128;
+            float* myred = rbuf + (size_t)warp * NMAT * NTG * 128;
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
 #pragma unroll
                 for (int nt = 0; nt < NTG; ++nt)
                     *(float4*)(myred + ((m * NTG + nt) * 32 + lane) * 4) =
-                        make_float4(acc[m][nt][0], acc[m][nt][1], acc[m][nt][2], acc[m][nt][3]);
+                        make_float4(acc[m][nt][0] * kAccScale, acc[m][nt][1] * kAccScale,
+                                    acc[m][nt][2] * kAccScale, acc[m][nt][3] * kAccScale);
             __syncthreads();
+            red_par ^= 1;
             for (int t = threadIdx.x; t < NTG * 128; t += blockDim.x) {
                 const int nt = t >> 7, ln = (t & 127) >> 2, e = t & 3;
                 const int rr = (ln >> 2) + 8 * (e >> 1);
@@ -302,9 +350,9 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                 float v[NMAT];
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m) {
-                    float s = 0.0f;
-                    for (int w = 0; w < NW; ++w) s += red[(((size_t)w * NMAT + m) * NTG + nt) * 128 + ln * 4 + e];
-                    v[m] = s;
+                    float sum = 0.0f;
+                    for (int w = 0; w < NW; ++w) sum += rbuf[(((size_t)w * NMAT + m) * NTG + nt) * 128 + ln * 4 + e];
+                    v[m] = sum;
                 }
                 if constexpr (MODE == GM_PROJ) {
                     const ProjSeg& sg = p.seg[it.seg];
@@ -330,9 +378,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                     }
                 }
             }
-            __syncthreads();
         }
-        (void)waited;
     }
     // After a failed wait (error already recorded) later copies may still be in flight:
     // wait for each of them, bounded, before the shared memory goes away. Every warp
@@ -353,7 +399,7 @@ void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStrea
     else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP>;
     else k = gemv_kernel<WT, KSF, GM_DOWN>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    k<<<grid, nwarps * 32, smem, s>>>(p);
+    launch_pdl(k, dim3(grid), dim3(nwarps * 32), (size_t)smem, s, p);
 }
 
 }  // namespace
@@ -370,15 +416,23 @@ void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stage
     if (nw == 0) nw = std::max(min_nw, std::min(16, m.chunks));
     const int cpw = (m.chunks + nw - 1) / nw;
     const int sb = cpw * m.tile_bytes * nmat;
-    const int red = nw * nmat * NTG * 128 * 4;
-    const int bars_max = 128 * ((nw * 4 * 8 + 127) / 128);
-    const int budget = 220 * 1024 - red - bars_max;
-    int ns = std::min(4, budget / (nw * sb));
-    if (ns < 1) ns = 1;
+    const int red = 2 * nw * nmat * NTG * 128 * 4;
+    auto total = [&](int ns) { return 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red; };
+    // deepest ring that still lets two blocks share an SM (block-level barriers of one
+    // block then overlap the other's streaming); else one block with up to 4 stages
+    const int per_sm = 233472, per_block_reserved = 1024;
+    int ns = 0;
+    for (int cand = 4; cand >= 2; --cand)
+        if (2 * (total(cand) + per_block_reserved) <= per_sm) { ns = cand; break; }
+    if (ns == 0) {
+        ns = 1;
+        for (int cand = 4; cand >= 1; --cand)
+            if (total(cand) + per_block_reserved <= per_sm) { ns = cand; break; }
+    }
     *nwarps = nw;
     *n_stages = ns;
     *stage_bytes = sb;
-    *smem = 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red;
+    *smem = total(ns);
 }
 
 void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s) {

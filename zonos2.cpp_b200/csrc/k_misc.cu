@@ -2,6 +2,7 @@
 #include "common.cuh"
 #include "gguf.h"
 #include "kernels.h"
+#include "launch.cuh"
 #include "quant.h"
 
 #include <vector>
@@ -19,6 +20,7 @@ namespace {
 __global__ void pack_kernel(const StepBufs b, int T) {
     __shared__ int s_start[1024], s_out[1024];
     const int n = b.n_desc, tid = threadIdx.x;
+    if (tid == 0) *b.err = 0;          // first kernel of a step: clear the error word
     if (tid < n) {
         s_start[tid] = b.descs[tid].n_new;
         s_out[tid] = (b.descs[tid].flags & SD_OUTPUT) ? 1 : 0;
@@ -88,6 +90,8 @@ __device__ __forceinline__ float emb_elem(const uint8_t* tbl, uint32_t type, siz
 // residual (:300), cur = rms_norm(x) * attn_norm[0] feeds layer 0 (:343).
 __global__ void embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0, const Dims dm) {
     extern __shared__ float sh[];
+    pdl_wait();
+    pdl_release();
     float* emb = sh;                      // [d]
     float* red = sh + dm.n_embd;          // [32]
     const int t = blockIdx.x, d = dm.n_embd;
@@ -131,36 +135,44 @@ __global__ void embed_kernel(const StepBufs b, const EmbedDev e, const float* __
 // x = sum_j out_route[pos(t, j)] in top-k order (src/zonos2-graph.cpp:232-238), then the
 // residual fold res = x + res (:332/:353) and the next block's input norm
 // (attn_norm of layer L+1, or output_norm after the last layer for output tokens).
-__global__ void moe_combine_kernel(const StepBufs b, int k, const float* __restrict__ next_norm,
-                                   const float* __restrict__ out_norm, const Dims dm, int last) {
+__global__ void __launch_bounds__(512) moe_combine_kernel(const StepBufs b, int k, const float* __restrict__ next_norm,
+                                                          const float* __restrict__ out_norm, const Dims dm, int last) {
     __shared__ float red[32];
-    const int t = blockIdx.x, d = dm.n_embd;
+    pdl_wait();
+    pdl_release();
+    const int t = blockIdx.x, d = dm.n_embd, d4 = d / 4;
     const bool active = b.tok_slot[t] >= 0;
     int pos[8];
-    for (int j = 0; j < k && j < 8; ++j) pos[j] = active ? b.route_pos[t * b.kmax + j] : -1;
-    float* res = b.res + (size_t)t * d;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pos[j] = (active && j < k) ? b.route_pos[t * b.kmax + j] : -1;
+    float4* res = reinterpret_cast<float4*>(b.res + (size_t)t * d);
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float x = 0.0f;
-        for (int j = 0; j < k && j < 8; ++j) {
+    for (int i = threadIdx.x; i < d4; i += blockDim.x) {
+        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
             if (pos[j] < 0) continue;
-            const float v = b.out_route[(size_t)pos[j] * d + i];
-            x = (j == 0) ? v : __fadd_rn(x, v);
+            const float4 v = reinterpret_cast<const float4*>(b.out_route + (size_t)pos[j] * d)[i];
+            if (j == 0) x = v;
+            else { x.x = __fadd_rn(x.x, v.x); x.y = __fadd_rn(x.y, v.y); x.z = __fadd_rn(x.z, v.z); x.w = __fadd_rn(x.w, v.w); }
         }
-        const float r = __fadd_rn(x, res[i]);
+        float4 r = res[i];
+        r.x = __fadd_rn(x.x, r.x); r.y = __fadd_rn(x.y, r.y); r.z = __fadd_rn(x.z, r.z); r.w = __fadd_rn(x.w, r.w);
         res[i] = r;
-        ss += r * r;
+        ss += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
     }
     const int orow = b.tok_out[t];
     if (last && orow < 0) return;              // uniform per block
     ss = block_sum(ss, red);
     const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
-    if (!last) {
-        for (int i = threadIdx.x; i < d; i += blockDim.x)
-            b.cur[(size_t)t * d + i] = __float2half_rn((res[i] * sc) * next_norm[i]);
-    } else {
-        for (int i = threadIdx.x; i < d; i += blockDim.x)
-            b.hout[(size_t)orow * d + i] = __float2half_rn((res[i] * sc) * out_norm[i]);
+    const float* w = last ? out_norm : next_norm;
+    __half* dst = last ? b.hout + (size_t)orow * d : b.cur + (size_t)t * d;
+    for (int i = threadIdx.x; i < d4; i += blockDim.x) {
+        const float4 r = res[i];
+        const float4 ww = reinterpret_cast<const float4*>(w)[i];
+        __half2* o = reinterpret_cast<__half2*>(dst) + 2 * i;
+        o[0] = __floats2half2_rn((r.x * sc) * ww.x, (r.y * sc) * ww.y);
+        o[1] = __floats2half2_rn((r.z * sc) * ww.z, (r.w * sc) * ww.w);
     }
 }
 
@@ -180,6 +192,8 @@ __global__ void __launch_bounds__(256) sampler_kernel(const StepBufs b, const Sa
     __shared__ float pv[SORT_N];
     __shared__ unsigned char drop_p[SORT_N];   // top-p rejections
     __shared__ int s_code;
+    pdl_wait();
+    pdl_release();
     const int o = blockIdx.x, cb = blockIdx.y, av = dm.audio_vocab;
     const int di = b.out_desc[o];
     const SlotDesc D = b.descs[di];
@@ -368,19 +382,19 @@ void launch_pack(const StepBufs& b, int T, int n_out, cudaStream_t s) {
 }
 
 void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s) {
-    embed_kernel<<<T, 256, (d.n_embd + 32) * sizeof(float), s>>>(b, e, attn_norm0, d);
+    launch_pdl(embed_kernel, dim3(T), dim3(256), (d.n_embd + 32) * sizeof(float), s, b, e, attn_norm0, d);
 }
 
 void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,
                         const Dims& d, int T, int last, cudaStream_t s) {
-    moe_combine_kernel<<<T, 256, 0, s>>>(b, ly.is_moe ? ly.top_k : 1, next_norm, out_norm, d, last);
+    launch_pdl(moe_combine_kernel, dim3(T), dim3(512), 0, s, b, ly.is_moe ? ly.top_k : 1, next_norm, out_norm, d, last);
 }
 
 void launch_sampler(const StepBufs& b, const SampDev* samp, int* hist, int* hist_len, int hist_cap,
                     const Dims& d, int n_out, cudaStream_t s) {
     if (n_out <= 0) return;
     dim3 grid(n_out, d.n_codebooks);
-    sampler_kernel<<<grid, 256, 0, s>>>(b, samp, hist, hist_len, hist_cap, d);
+    launch_pdl(sampler_kernel, grid, dim3(256), 0, s, b, samp, hist, hist_len, hist_cap, d);
 }
 
 }  // namespace z2b

@@ -9,6 +9,7 @@
 // token's top-k, so the permutation is a pure function of the selected ids.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace z2b {
 
@@ -18,16 +19,32 @@ __device__ __forceinline__ float gelu_erf(float x) {
     return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
 }
 
-// y[i] = sum_j W[i][j] x[j] for i < rows (W row-major f32), one warp per row.
+// y[i] = sum_j W[i][j] x[j] for i < rows (W row-major f32, x in shared memory): one warp
+// per row group, every row's loads issued together (cols a multiple of 4).
 __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const float* x, float* y,
                                              int rows, int cols) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int i = w; i < rows; i += nw) {
-        const float* wr = W + (size_t)i * cols;
-        float acc = 0.0f;
-        for (int j = lane; j < cols; j += 32) acc += wr[j] * x[j];
-        acc = warp_sum(acc);
-        if (lane == 0) y[i] = acc;
+    const int c4 = cols / 4;
+    for (int i0 = w; i0 < rows; i0 += 4 * nw) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int j = lane; j < c4; j += 32) {
+            const float4 xv = reinterpret_cast<const float4*>(x)[j];
+            float4 wv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const int row = i0 + r * nw;
+                wv[r] = row < rows ? reinterpret_cast<const float4*>(W + (size_t)row * cols)[j]
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r] += wv[r].x * xv.x + wv[r].y * xv.y + wv[r].z * xv.z + wv[r].w * xv.w;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float a = warp_sum(acc[r]);
+            const int row = i0 + r * nw;
+            if (lane == 0 && row < rows) y[row] = a;
+        }
     }
 }
 
@@ -76,40 +93,133 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(256) router_kernel(const StepBufs b, const LayerSmall ly, const Dims dm,
-                                                     int first_moe, int T, int layer) {
-    extern __shared__ float sh[];
-    const int d = dm.n_embd, rd = dm.rd, t = blockIdx.x;
-    const int E = ly.is_moe ? ly.n_expert : 1, k = ly.is_moe ? ly.top_k : 1;
-    float* xs = sh;                 // [d]
-    float* rh = xs + d;             // [rd]
-    float* rn = rh + rd;            // [rd]
-    float* h0 = rn + rd;            // [rd]
-    float* pr = h0 + rd;            // [E]
-    float* red = pr + MAX_EXPERTS;  // [32]
+// Router down projection, split over (row block of 8, K slice of d/4, group of 16
+// tokens). The weights are static, so each block dequantises its 8 x d/4 slice into
+// shared memory (w = q * d exactly in f32 for Q8_0) before waiting on the step's
+// predecessor. After the wait it stages u = res * ffn_norm for its tokens and writes
+// the partial dot products sum_k w[r][k] * u[t][k]; the token's RMS scale is applied
+// once to the summed partials in router_mlp_kernel (rh = Wd . (res * s * ffn_norm)).
+constexpr int RP_ROWS = 8, RP_TOK = 16;
+__host__ __device__ inline int router_kslices(int d) { return d % 128 == 0 ? 4 : 1; }
+
+__global__ void __launch_bounds__(256) router_proj_kernel(const StepBufs b, const LayerSmall ly, const Dims dm, int T) {
+    extern __shared__ __align__(16) float sh[];
+    const int d = dm.n_embd, rd = dm.rd, L = d / router_kslices(d), S = L + 4, H = L / 2;
+    const int rb = blockIdx.x, ks = blockIdx.y, t0 = blockIdx.z * RP_TOK, k0 = ks * L;
+    float* xs = sh;                          // [RP_TOK][S]: k < H at k, k >= H at k + 4
+    float* ws = xs + RP_TOK * S;             // [RP_ROWS][S], same split
+    float* fn = ws + RP_ROWS * S;            // [L]
+    auto at = [&](int k) { return k < H ? k : k + 4; };
+    for (int i = threadIdx.x; i < RP_ROWS * L / 4; i += blockDim.x) {
+        const int r = (4 * i) / L, kk = (4 * i) % L, row = rb * RP_ROWS + r;
+        float4 v;
+        if (ly.rdown_q) {
+            const char4 q = *reinterpret_cast<const char4*>(ly.rdown_q + (size_t)row * d + k0 + kk);
+            const float dv = ly.rdown_qd[(size_t)row * (d / 32) + (k0 + kk) / 32];
+            v = make_float4((float)q.x * dv, (float)q.y * dv, (float)q.z * dv, (float)q.w * dv);
+        } else {
+            v = *reinterpret_cast<const float4*>(ly.rdown_w + (size_t)row * d + k0 + kk);
+        }
+        *reinterpret_cast<float4*>(ws + r * S + at(kk)) = v;
+    }
+    for (int i = threadIdx.x; i < L / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(fn)[i] = reinterpret_cast<const float4*>(ly.ffn_norm + k0)[i];
+    pdl_wait();
+    pdl_release();
+    __syncthreads();                         // fn (and ws) written by other threads
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int tt = warp; tt < RP_TOK; tt += nw) {
+        const int t = t0 + tt;
+        for (int j = lane; j < L / 4; j += 32) {
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (t < T) v = *reinterpret_cast<const float4*>(b.res + (size_t)t * d + k0 + 4 * j);
+            const float4 f = reinterpret_cast<const float4*>(fn)[j];
+            *reinterpret_cast<float4*>(xs + tt * S + at(4 * j)) = make_float4(v.x * f.x, v.y * f.y, v.z * f.z, v.w * f.w);
+        }
+    }
+    __syncthreads();
+    // warp -> row, lane -> (token lane & 15, half lane >> 4)
+    const int tt = lane & 15, h = lane >> 4;
+    for (int r = warp; r < RP_ROWS; r += nw) {
+        const float* xr = xs + tt * S + h * (H + 4);
+        const float* wr = ws + r * S + h * (H + 4);
+        float acc = 0.0f;
+        for (int j = 0; j < H; j += 4) {
+            const float4 xv = *reinterpret_cast<const float4*>(xr + j);
+            const float4 wv = *reinterpret_cast<const float4*>(wr + j);
+            acc += wv.x * xv.x + wv.y * xv.y + wv.z * xv.z + wv.w * xv.w;
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+        if (h == 0 && t0 + tt < T) b.rpart[((size_t)ks * b.rpart_T + t0 + tt) * rd + rb * RP_ROWS + r] = acc;
+    }
+}
+
+// One block per token (512 threads): ffn_norm (src/zonos2-graph.cpp:347) -> cur (f16
+// for the experts); rh = s * sum of the router_proj partials + b (+ previous MoE layer's
+// state * eda_scale), which becomes the next MoE layer's state (:199-203); RMSNorm(rh) *
+// router_norm, two erf-GELU layers, expert logits (+ mask), softmax, top-k on probs +
+// balancing bias (+ mask), route weight = probs[sel] with no renormalisation
+// (:206-220). The MLP weights are static: when they fit, one bulk copy per matrix brings
+// them into shared memory before the wait on router_proj. The last block to finish
+// builds the expert segments.
+__global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const LayerSmall ly, const Dims dm,
+                                                         int first_moe, int T, int layer, int stage) {
+    extern __shared__ __align__(128) float sh[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[32];
     __shared__ int s_last;
     __shared__ int cnt[MAX_EXPERTS];
+    const int d = dm.n_embd, rd = dm.rd, t = blockIdx.x;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int E = ly.is_moe ? ly.n_expert : 1, k = ly.is_moe ? ly.top_k : 1;
+    const float* W0 = ly.m0_w;
+    const float* W2 = ly.m2_w;
+    const float* W4 = ly.m4_w;
+    float* rh = sh;                  // [rd]
+    float* rn = rh + rd;             // [rd]
+    float* h0 = rn + rd;             // [rd]
+    float* pr = h0 + rd;             // [MAX_EXPERTS]
+    float* wst = pr + MAX_EXPERTS;   // staged m0 [rd][rd], m2 [rd][rd], m4 [E][rd]
+    const bool staged = ly.is_moe && stage;
+    if (staged) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            fence_mbar_init();
+            const uint32_t b0 = (uint32_t)(rd * rd * 4), b4 = (uint32_t)(E * rd * 4);
+            mbar_expect_tx(&bar, 2 * b0 + b4);
+            bulk_g2s(wst, ly.m0_w, b0, &bar);
+            bulk_g2s(wst + rd * rd, ly.m2_w, b0, &bar);
+            bulk_g2s(wst + 2 * rd * rd, ly.m4_w, b4, &bar);
+        }
+        W0 = wst;
+        W2 = wst + rd * rd;
+        W4 = wst + 2 * rd * rd;
+    }
+    pdl_wait();
+    pdl_release();
     const bool active = b.tok_slot[t] >= 0;
 
-    // ffn_norm -> cur (f16 for the experts) and xs (f32 for the router)
-    const float* res = b.res + (size_t)t * d;
+    // ffn_norm -> cur (f16)
+    const float4* r4 = reinterpret_cast<const float4*>(b.res + (size_t)t * d);
     float ss = 0.0f;
-    for (int j = threadIdx.x; j < d; j += blockDim.x) ss += res[j] * res[j];
+    for (int j = threadIdx.x; j < d / 4; j += blockDim.x) { const float4 v = r4[j]; ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
     ss = block_sum(ss, red);
     const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
-    for (int j = threadIdx.x; j < d; j += blockDim.x) {
-        const float v = (res[j] * sc) * ly.ffn_norm[j];
-        xs[j] = v;
-        b.cur[(size_t)t * d + j] = __float2half_rn(v);
+    for (int j = threadIdx.x; j < d / 4; j += blockDim.x) {
+        const float4 r = r4[j];
+        const float4 f = reinterpret_cast<const float4*>(ly.ffn_norm)[j];
+        __half2* o = reinterpret_cast<__half2*>(b.cur + (size_t)t * d) + 2 * j;
+        o[0] = __floats2half2_rn((r.x * sc) * f.x, (r.y * sc) * f.y);
+        o[1] = __floats2half2_rn((r.z * sc) * f.z, (r.w * sc) * f.w);
     }
     for (int j = threadIdx.x; j < b.kmax; j += blockDim.x) b.route_pos[t * b.kmax + j] = -1;
-    __syncthreads();
 
+    bool ok = true;
     if (ly.is_moe) {
-        block_matvec(ly.rdown_w, xs, rh, rd, d);
-        __syncthreads();
         for (int i = threadIdx.x; i < rd; i += blockDim.x) {
-            float v = rh[i] + ly.rdown_b[i];
+            float a = 0.0f;
+            for (int ks = 0; ks < router_kslices(d); ++ks) a += b.rpart[((size_t)ks * b.rpart_T + t) * rd + i];
+            float v = a * sc + ly.rdown_b[i];
             if (ly.eda && !first_moe) v = v + b.rstate[(size_t)t * rd + i] * ly.eda[i];
             rh[i] = v;
             b.rstate[(size_t)t * rd + i] = v;
@@ -120,46 +230,71 @@ __global__ void __launch_bounds__(256) router_kernel(const StepBufs b, const Lay
         s2 = block_sum(s2, red);
         const float sc2 = 1.0f / sqrtf(s2 / (float)rd + dm.rms_eps);
         for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = (rh[i] * sc2) * ly.rnorm[i];
+        if (staged) ok = mbar_wait(&bar, 0, b.err);
         __syncthreads();
-        block_matvec(ly.m0_w, rn, h0, rd, rd);
+        if (ok) {
+            block_matvec(W0, rn, h0, rd, rd);
+            __syncthreads();
+            for (int i = threadIdx.x; i < rd; i += blockDim.x) h0[i] = gelu_erf(h0[i] + ly.m0_b[i]);
+            __syncthreads();
+            block_matvec(W2, h0, rn, rd, rd);        // rn reused as h2
+            __syncthreads();
+            for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = gelu_erf(rn[i] + ly.m2_b[i]);
+            __syncthreads();
+            block_matvec(W4, rn, pr, E, rd);
+        }
         __syncthreads();
-        for (int i = threadIdx.x; i < rd; i += blockDim.x) h0[i] = gelu_erf(h0[i] + ly.m0_b[i]);
-        __syncthreads();
-        block_matvec(ly.m2_w, h0, rn, rd, rd);        // rn reused as h2
-        __syncthreads();
-        for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = gelu_erf(rn[i] + ly.m2_b[i]);
-        __syncthreads();
-        block_matvec(ly.m4_w, rn, pr, E, rd);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            // softmax (ggml: sum in double, scale by the rounded reciprocal)
-            if (ly.rmask) for (int e = 0; e < E; ++e) pr[e] = pr[e] + ly.rmask[e];
+        if (w == 0 && ok) {
+            // softmax (ggml: sum in double, scale by the rounded reciprocal), one warp
             float mx = -INFINITY;
-            for (int e = 0; e < E; ++e) mx = fmaxf(mx, pr[e]);
-            double sum = 0.0;
-            for (int e = 0; e < E; ++e) { const float v = expf(pr[e] - mx); pr[e] = v; sum += (double)v; }
-            const float inv = (float)(1.0 / sum);
-            for (int e = 0; e < E; ++e) pr[e] = pr[e] * inv;
-            // top-k over probs + bias (+ mask), ties to the lower expert id
+            for (int e = lane; e < E; e += 32) {
+                if (ly.rmask) pr[e] = pr[e] + ly.rmask[e];
+                mx = fmaxf(mx, pr[e]);
+            }
+            mx = warp_max(mx);
+            __syncwarp();
+            if (lane == 0) {
+                double sum = 0.0;
+                for (int e = 0; e < E; ++e) { const float v = expf(pr[e] - mx); pr[e] = v; sum += (double)v; }
+                red[0] = (float)(1.0 / sum);
+            }
+            __syncwarp();
+            const float inv = red[0];
+            for (int e = lane; e < E; e += 32) pr[e] = pr[e] * inv;
+            __syncwarp();
+            // top-k over probs + bias (+ mask), ties to the lower expert id: k rounds of warp argmax
             unsigned long long taken[MAX_EXPERTS / 64] = {0};
             for (int j = 0; j < k; ++j) {
-                int best = -1; float bv = -INFINITY;
-                for (int e = 0; e < E; ++e) {
+                float bv = -INFINITY; int best = 0x7fffffff;
+                for (int e = lane; e < E; e += 32) {
                     if (taken[e >> 6] >> (e & 63) & 1ull) continue;
                     float sv = pr[e] + ly.rbias[e];
                     if (ly.rmask) sv = sv + ly.rmask[e];
-                    if (best < 0 || sv > bv) { bv = sv; best = e; }
+                    if (sv > bv || (sv == bv && e < best)) { bv = sv; best = e; }
                 }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, best, o);
+                    if (ov > bv || (ov == bv && oi < best)) { bv = ov; best = oi; }
+                }
+                if (best >= E) best = 0;              // all remaining scores -inf: keep a valid id
                 taken[best >> 6] |= 1ull << (best & 63);
-                b.sel[t * b.kmax + j] = active ? best : -1;
-                b.selw[t * b.kmax + j] = pr[best];
+                if (lane == 0) {
+                    b.sel[t * b.kmax + j] = active ? best : -1;
+                    b.selw[t * b.kmax + j] = pr[best];
+                }
             }
+        }
+        if (!ok && threadIdx.x < k) {                  // weights never arrived (error recorded)
+            b.sel[t * b.kmax + threadIdx.x] = -1;
+            b.selw[t * b.kmax + threadIdx.x] = 0.0f;
         }
     } else if (threadIdx.x == 0) {
         b.sel[t * b.kmax] = active ? 0 : -1;
         b.selw[t * b.kmax] = 1.0f;
     }
-
+    __syncthreads();
     if (b.sel_log && threadIdx.x == 0)
         for (int j = 0; j < k; ++j) b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + j] = b.sel[t * b.kmax + j];
 
@@ -186,16 +321,33 @@ __global__ void route_test_kernel(const int* sel, const float* selw, int T, int 
 
 }  // namespace
 
+size_t router_mlp_smem(const Dims& d, int E, bool* stage) {
+    const size_t base = (size_t)(3 * d.rd + MAX_EXPERTS) * sizeof(float);
+    const size_t w = (size_t)(2 * d.rd * d.rd + E * d.rd) * sizeof(float);
+    *stage = base + w <= 160 * 1024;
+    return *stage ? base + w : base;
+}
+
 void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
                    cudaStream_t s) {
-    const size_t smem = (size_t)(d.n_embd + 3 * d.rd + MAX_EXPERTS + 32) * sizeof(float);
     static bool configured = false;
     if (!configured) {
-        cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        cudaFuncSetAttribute(router_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(router_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         configured = true;
     }
-    router_kernel<<<T, 256, smem, s>>>(b, ly, d, first_moe, T, layer);
+    if (ly.is_moe) {
+        const int nks = router_kslices(d.n_embd), L = d.n_embd / nks, S = L + 4;
+        const size_t smem = (size_t)((RP_TOK + RP_ROWS) * S + L) * sizeof(float);
+        launch_pdl(router_proj_kernel, dim3(d.rd / RP_ROWS, nks, (T + RP_TOK - 1) / RP_TOK), dim3(256), smem, s,
+                   b, ly, d, T);
+    }
+    bool stage = false;
+    const size_t smem = router_mlp_smem(d, ly.is_moe ? ly.n_expert : 1, &stage);
+    launch_pdl(router_mlp_kernel, dim3(T), dim3(512), smem, s, b, ly, d, first_moe, T, layer, stage ? 1 : 0);
 }
+
+int router_launches(const LayerSmall& ly) { return ly.is_moe ? 2 : 1; }
 
 }  // namespace z2b
 

@@ -113,8 +113,10 @@ struct StepBufs {
     float* qkvg; int ldq;           // [T][ldq]
     __half* qh;                     // [T][nh][hd]
     float* apart; int max_split;    // [T][nh][max_split][hd+2]
+    int* attn_ticket;               // [T][nkv] split arrivals (zero between steps)
     __half* o;                      // [T][nh*hd]
     float* rstate;                  // [T][rd]
+    float* rpart; int rpart_T;      // [4][rpart_T][rd] router down-projection partial sums
     int* sel; float* selw; int kmax;// [T][kmax]
     int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
     int* ticket;
@@ -133,6 +135,8 @@ struct StepBufs {
 struct LayerSmall {
     const float *attn_norm, *ffn_norm, *attn_temp;
     const float *rdown_w, *rdown_b, *m0_w, *m0_b, *m2_w, *m2_b, *m4_w, *rnorm, *rbias, *eda, *rmask;
+    const int8_t* rdown_q;          // router down projection kept as Q8_0 quants [rd][d] (or null)
+    const float* rdown_qd;          // its block scales [rd][d/32] (f32 copies of the f16 d)
     int is_moe, top_k, n_expert;
 };
 
@@ -148,6 +152,7 @@ void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int lay
 void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s);
 void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
                    cudaStream_t s);
+int router_launches(const LayerSmall& ly);
 // Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the
 // next input row, advance n_past, and copy this step's host-drawn uniforms.
 void launch_sched_feed(const SlotDesc* step_descs, const int* src, int n, SlotDesc* descs, int* ids_in,

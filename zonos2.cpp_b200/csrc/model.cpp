@@ -216,7 +216,27 @@ struct Loader {
                 if (!rdw) return false;
                 if (rd == 0) rd = (int)rdw->ne[1];
                 if (rdw->ne[1] != rd || rdw->ne[0] != d) return fail(Z2B_ERR_FORMAT, "router_down shape");
-                s.rdown_w = small(rdw, (int64_t)rd * d);
+                if (rdw->type == GT_Q8_0) {
+                    // split Q8_0 blocks into int8 rows and f32 scales: w = q * d exactly
+                    const int64_t nb = (int64_t)rd * d / 32;
+                    std::vector<int8_t> qs((size_t)rd * d);
+                    std::vector<float> ds((size_t)nb);
+                    for (int64_t blk = 0; blk < nb; ++blk) {
+                        uint16_t dh; std::memcpy(&dh, rdw->data + blk * 34, 2);
+                        ds[blk] = f16_to_f32(dh);
+                        std::memcpy(&qs[blk * 32], rdw->data + blk * 34 + 2, 32);
+                    }
+                    int8_t* dq = (int8_t*)dalloc(qs.size());
+                    float* dd = (float*)dalloc(ds.size() * 4);
+                    if (!dq || !dd || !h2d(dq, qs.data(), qs.size()) || !h2d(dd, ds.data(), ds.size() * 4)) return false;
+                    s.rdown_q = dq;
+                    s.rdown_qd = dd;
+                    s.rdown_w = nullptr;
+                } else {
+                    s.rdown_w = small(rdw, (int64_t)rd * d);
+                    s.rdown_q = nullptr;
+                    s.rdown_qd = nullptr;
+                }
                 s.rdown_b = small(req(b + "router_down.bias"), rd);
                 s.m0_w = small(req(b + "router_mlp0.weight"), (int64_t)rd * rd);
                 s.m0_b = small(req(b + "router_mlp0.bias"), rd);
@@ -227,7 +247,7 @@ struct Loader {
                 s.rbias = small(req(b + "router_bias"), E);
                 const GTensor* eda = f.tensor(b + "router_eda_scale");
                 s.eda = eda ? small(eda, rd) : nullptr;
-                if (!s.rdown_w || !s.rdown_b || !s.m0_w || !s.m0_b || !s.m2_w || !s.m2_b || !s.m4_w || !s.rnorm || !s.rbias)
+                if ((!s.rdown_w && !s.rdown_q) || !s.rdown_b || !s.m0_w || !s.m0_b || !s.m2_w || !s.m2_b || !s.m4_w || !s.rnorm || !s.rbias)
                     return false;
                 if (eda && !s.eda) return false;
                 if (first) {
@@ -248,7 +268,8 @@ struct Loader {
         D.rd = rd; D.n_layer = (int)hp.n_layer; D.n_codebooks = (int)hp.n_codebooks;
         D.audio_vocab = (int)hp.audio_vocab; D.text_vocab = (int)hp.text_vocab;
         D.rms_eps = hp.rms_eps; D.qk_eps = hp.qk_norm_eps; D.rope_base = hp.rope_freq_base; D.softcap = hp.logit_softcap;
-        if (rd > 1024) return fail(Z2B_ERR_UNSUPPORTED, "router_dim too large");
+        if (rd > 1024 || rd % 8) return fail(Z2B_ERR_UNSUPPORTED, "router_dim must be a multiple of 8, at most 1024");
+        if (d % 16) return fail(Z2B_ERR_UNSUPPORTED, "n_embd must be a multiple of 16 (router K slices)");
         return true;
     }
 };

@@ -111,6 +111,8 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     acc(4); acc((size_t)R * D.n_ff * 2); acc((size_t)R * d * 4); acc((size_t)O * d * 2);
     acc((size_t)O * ncb * av * 4); acc((size_t)O * ncb * 4); acc(D.n_layer * 4); acc(4);
     acc((size_t)D.n_layer * T * c->kmax * 4);
+    acc((size_t)4 * T * std::max(D.rd, 1) * 4);
+    acc((size_t)T * nkv * 4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -128,6 +130,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.apart = carve<float>(p, (size_t)T * nh * c->max_split * (hd + 2)); B.max_split = c->max_split;
     B.o = carve<__half>(p, (size_t)T * nh * hd);
     B.rstate = carve<float>(p, (size_t)T * std::max(D.rd, 1));
+    B.rpart = carve<float>(p, (size_t)4 * T * std::max(D.rd, 1)); B.rpart_T = T;
     B.sel = carve<int>(p, (size_t)T * c->kmax); B.selw = carve<float>(p, (size_t)T * c->kmax); B.kmax = c->kmax;
     B.n_active = carve<int>(p, 1); B.active = carve<int>(p, MAX_EXPERTS); B.seg_off = carve<int>(p, MAX_EXPERTS + 1);
     B.route_tok = carve<int>(p, R); B.route_w = carve<float>(p, R); B.route_pos = carve<int>(p, (size_t)T * c->kmax);
@@ -137,6 +140,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.codes = carve<int>(p, (size_t)O * ncb); B.layer_active = carve<int>(p, D.n_layer);
     B.err = carve<uint32_t>(p, 1);
     B.sel_log = carve<int>(p, (size_t)D.n_layer * T * c->kmax); B.sel_log_T = T;
+    B.attn_ticket = carve<int>(p, (size_t)T * nkv);
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -217,7 +221,7 @@ struct ProfScope {
     ~ProfScope() { if (c->profiling) cudaEventRecord(e1, c->stream); }
 };
 
-int ctas_per_sm(int smem) { return std::max(1, std::min(4, (227 * 1024) / (smem + 1024))); }
+int ctas_per_sm(int smem) { return std::max(1, std::min(4, 233472 / (smem + 1024))); }
 
 void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int T, const __half* X, int ldx,
                float* out, int ldo, int epi, float cap, int cls) {
@@ -275,7 +279,6 @@ void enqueue_step(Ctx* c, int T, int n_out) {
     StepBufs B = c->B;
     B.n_desc = c->cur_n_desc;
     c->launches = 0;
-    cudaMemsetAsync(B.err, 0, 4, c->stream);
     { ProfScope ps(c, PC_PACK); launch_pack(B, T, n_out, c->stream); c->launches++; }
     { ProfScope ps(c, PC_EMBED); launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->stream); c->launches++; }
     const int hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv;
@@ -294,13 +297,12 @@ void enqueue_step(Ctx* c, int T, int n_out) {
         }
         { ProfScope ps(c, PC_ROPE); launch_rope_append(B, c->kv, ly.small.attn_temp, D, L, T, c->stream); c->launches++; }
         { ProfScope ps(c, PC_ATTN); launch_attention(B, c->kv, D, L, T, c->split_keys, c->max_split, c->stream); c->launches++; }
-        { ProfScope ps(c, PC_ATTN_COMB); launch_attn_combine(B, D, T, c->split_keys, c->max_split, c->stream); c->launches++; }
         {
             const DevMat* mats[1] = {&ly.wo};
             const int offs[1] = {0};
             gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f, PC_WO);
         }
-        { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches++; }
+        { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches += router_launches(ly.small); }
         if (ly.is_moe) first_moe = false;
         gemv_moe(c, ly, GM_GATEUP);
         gemv_moe(c, ly, GM_DOWN);
