@@ -106,8 +106,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     uint8_t* stages = smem + 128;
     float* merge = reinterpret_cast<float*>(stages + SM::NS * SM::STAGE);
-    pdl_wait();
-    pdl_release();
+    // The token's slot, position and descriptor were written by the step's packer and the
+    // cached keys below the slot's first new key by earlier steps: every kernel before
+    // the immediate predecessor has completed once this grid runs (each kernel waits on
+    // its own predecessor before it releases its dependent), so those chunks are copied
+    // before the wait. Q and the keys appended by this step come after it.
     const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
     const int slot = b.tok_slot[t];
     if (slot < 0) return;
@@ -115,6 +118,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     const int key0 = sp * split_keys;
     if (key0 >= n_keys) return;
     const int key1 = min(n_keys, key0 + split_keys);
+    const int fresh = b.descs[b.tok_desc[t]].n_past;          // first key written by this step
     const int nchunks = (key1 - key0 + KCH - 1) / KCH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = lane >> 2, q = lane & 3;
@@ -152,8 +156,13 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
         bulk_g2s(st, kp, SM::CHUNK_BYTES, &bars[c % SM::NS]);
         bulk_g2s(st + SM::CHUNK_BYTES, vp, SM::CHUNK_BYTES, &bars[c % SM::NS]);
     };
+    int pre = 0;                                 // chunks issued before the wait
     if (threadIdx.x == 0)
-        for (int c = 0; c < SM::NS && c < nchunks; ++c) issue(c);
+        for (; pre < SM::NS && pre < nchunks && min(key0 + (pre + 1) * KCH, key1) <= fresh; ++pre) issue(pre);
+    pdl_wait();
+    pdl_release();
+    if (threadIdx.x == 0)
+        for (int c = pre; c < SM::NS && c < nchunks; ++c) issue(c);
 
     // Q fragments: head r of the group (rows >= G are zero), dims QO*q + 4s + {0..3}
     uint32_t qa[KST][2];
@@ -266,23 +275,40 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // split weights exp(m_s - M) and 1 / sum_s exp(m_s - M) l_s per head, then every
+    // output element sums its splits with all loads in flight together
+    float* cf = merge;                           // [G][ns] split weights
+    float* cl = merge + G * ns;                  // [G][ns] split sums, then [G] 1 / L
+    for (int i = threadIdx.x; i < G * ns; i += blockDim.x) {
+        const int g = i / ns, s2 = i % ns;
+        const float* ps = b.apart + (((size_t)t * nh + hk * G + g) * max_split + s2) * (HD + 2);
+        cf[i] = __ldcg(ps);
+        cl[i] = __ldcg(ps + 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, cf[g * ns + s2]);
+        float L = 0.0f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float pm = cf[g * ns + s2];
+            const float f = (pm == -INFINITY) ? 0.0f : expf(pm - M);
+            cf[g * ns + s2] = f;
+            L += f * cl[g * ns + s2];
+        }
+        cl[G * ns + g] = L;
+    }
+    __syncthreads();
     const int gate_off = nh * HD + 2 * dm.n_head_kv * HD;
     for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
         const int g = idx / HD, e = idx % HD, h = hk * G + g;
-        const float* base = b.apart + ((size_t)t * nh + h) * max_split * (HD + 2);
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, __ldcg(base + (size_t)s2 * (HD + 2)));
-        float L = 0.0f, O = 0.0f;
-        for (int s2 = 0; s2 < ns; ++s2) {
-            const float* ps = base + (size_t)s2 * (HD + 2);
-            const float pm = __ldcg(ps);
-            if (pm == -INFINITY) continue;
-            const float f = expf(pm - M);
-            L += f * __ldcg(ps + 1);
-            O += f * __ldcg(ps + 2 + e);
-        }
+        const float* base = b.apart + ((size_t)t * nh + h) * max_split * (HD + 2) + 2 + e;
+        float O = 0.0f;
+#pragma unroll 4
+        for (int s2 = 0; s2 < ns; ++s2) O += cf[g * ns + s2] * __ldcg(base + (size_t)s2 * (HD + 2));
         const float gg = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
-        b.o[(size_t)t * nh * HD + (size_t)h * HD + e] = __float2half_rn((O / L) * gg);
+        b.o[(size_t)t * nh * HD + (size_t)h * HD + e] = __float2half_rn((O / cl[G * ns + g]) * gg);
     }
     if (failed) {
         for (int c = 0; c < SM::NS; ++c) (void)mbar_try_wait(&bars[c], 0);

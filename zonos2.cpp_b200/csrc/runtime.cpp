@@ -60,7 +60,13 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     c->kmax = 1;
     for (auto& ly : m->layers) c->kmax = std::max(c->kmax, ly.top_k);
     c->R_max = c->T_max * c->kmax;
+    // keys per attention split: 256 (one KV page), doubled until the split combine's
+    // per-head weights fit the kernel's merge area (2 G max_split + G <= 32 (hd + 2))
     c->split_keys = 256;
+    {
+        const int G = m->dims.n_head / m->dims.n_head_kv, hd = m->dims.head_dim;
+        while (2 * G * ((c->slot_cap + c->split_keys - 1) / c->split_keys) + G > 32 * (hd + 2)) c->split_keys *= 2;
+    }
     c->max_split = (c->slot_cap + c->split_keys - 1) / c->split_keys;
     const int d = D.n_embd, hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv, ncb = D.n_codebooks, av = D.audio_vocab;
 
