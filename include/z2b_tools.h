@@ -68,6 +68,20 @@ int z2b_test_pack(const int32_t* desc4, int n, int T, int32_t* tok_slot, int32_t
 int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
                    int32_t* route_tok, int32_t* route_pos);
 
+/* Largest T * k that z2b_route_segments_noalloc accepts (its fixed device scratch is
+ * 5 words per route plus 2 * 256 + 2 words, about 320 KB). */
+#define Z2B_NOALLOC_MAX_ROUTES 16384
+/* No reference counterpart. The segment builder of z2b_test_route (same arguments, same
+ * results) without any device allocation: it works in a fixed scratch array compiled
+ * into the library, for callers that may not call cudaMalloc/cudaFree (they synchronise
+ * the device, and are refused while a stream is being captured into a CUDA graph).
+ * Runs on the current device; the first call on each device looks up the scratch
+ * address, so make it before any stream capture begins. Calls that overlap in time
+ * share the scratch and race: serialise them. T * k > Z2B_NOALLOC_MAX_ROUTES returns
+ * Z2B_ERR_ARG with z2b_last_error() naming the limit. */
+int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
+                               int32_t* route_tok, int32_t* route_pos);
+
 /* Router ids of every layer for the last z2b_step: writes [n_layer][T][kmax] when cap is
  * large enough; returns the number of entries (or -1). */
 struct z2b_ctx;

@@ -10,6 +10,10 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "../../include/z2b.h"
+#include "../../include/z2b_tools.h"
+
+#include <string>
 
 namespace z2b {
 
@@ -374,4 +378,84 @@ extern "C" int z2b_test_route(const int32_t* sel, const float* selw, int T, int 
     cudaFree(dsel); cudaFree(dw); cudaFree(dseg); cudaFree(dact); cudaFree(dna); cudaFree(dtok); cudaFree(drw);
     cudaFree(dpos);
     return rc;
+}
+
+// ---------------------------------------------------------------- allocation-free variant
+// z2b_route_segments_noalloc runs the same segment builder as z2b_test_route on a fixed
+// device scratch area instead of buffers allocated per call. It is for callers that
+// must not allocate device memory: cudaMalloc and cudaFree synchronise the whole device
+// (stalling decode steps queued by other threads) and are refused while a stream of the
+// process is being captured into a CUDA graph in the global capture mode. The scratch
+// is one file-scope array, so calls that overlap in time (from several host threads)
+// race on it and must be serialised by the caller.
+namespace z2b {
+namespace {
+
+constexpr int kNoAllocRoutes = Z2B_NOALLOC_MAX_ROUTES;
+// [sel | selw | route_tok | route_w | route_pos] x kNoAllocRoutes, then seg_off
+// [MAX_EXPERTS + 1], active [MAX_EXPERTS], n_active [1] (4-byte words)
+constexpr size_t kNoAllocWords = 5 * (size_t)kNoAllocRoutes + 2 * MAX_EXPERTS + 2;
+static __device__ __align__(256) uint32_t g_route_scratch[kNoAllocWords];
+
+constexpr int kMaxDevices = 64;
+uint32_t* g_route_scratch_ptr[kMaxDevices] = {};
+
+}  // namespace
+void set_error(const std::string& e);
+}  // namespace z2b
+
+extern "C" int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int k, int E,
+                                          int32_t* seg_off, int32_t* route_tok, int32_t* route_pos) {
+    using namespace z2b;
+    if (!sel || !selw || !seg_off || !route_tok || !route_pos) { set_error("null argument"); return Z2B_ERR_ARG; }
+    if (T < 1 || k < 1 || E < 1 || E > MAX_EXPERTS) { set_error("route_segments_noalloc: bad T, k or E"); return Z2B_ERR_ARG; }
+    if ((int64_t)T * k > kNoAllocRoutes) {
+        set_error("route_segments_noalloc: T * k exceeds Z2B_NOALLOC_MAX_ROUTES (" +
+                  std::to_string(kNoAllocRoutes) + ")");
+        return Z2B_ERR_ARG;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error("route_segments_noalloc: no usable current device");
+        return Z2B_ERR_CUDA;
+    }
+    // set-up, once per device with that device current: the device address of the
+    // scratch symbol (the host-side name of a __device__ array is not a device pointer)
+    if (!g_route_scratch_ptr[dev]) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_route_scratch);
+        if (e != cudaSuccess || !ptr) {
+            set_error(std::string("route_segments_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+            return Z2B_ERR_CUDA;
+        }
+        g_route_scratch_ptr[dev] = static_cast<uint32_t*>(ptr);
+    }
+    uint32_t* base = g_route_scratch_ptr[dev];
+    int* dsel = reinterpret_cast<int*>(base);
+    float* dw = reinterpret_cast<float*>(base + kNoAllocRoutes);
+    int* dtok = reinterpret_cast<int*>(base + 2 * (size_t)kNoAllocRoutes);
+    float* drw = reinterpret_cast<float*>(base + 3 * (size_t)kNoAllocRoutes);
+    int* dpos = reinterpret_cast<int*>(base + 4 * (size_t)kNoAllocRoutes);
+    int* dseg = reinterpret_cast<int*>(base + 5 * (size_t)kNoAllocRoutes);
+    int* dact = dseg + MAX_EXPERTS + 1;
+    int* dna = dact + MAX_EXPERTS;
+    const size_t R = (size_t)T * k;
+    cudaStream_t s = 0;
+    bool ok = cudaMemcpyAsync(dsel, sel, R * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+              cudaMemcpyAsync(dw, selw, R * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+              // route_pos of routes with no expert stays -1; everything else is written
+              cudaMemsetAsync(dpos, 0xff, R * 4, s) == cudaSuccess;
+    if (ok) {
+        route_test_kernel<<<1, 256, 0, s>>>(dsel, dw, T, k, E, dseg, dact, dna, dtok, drw, dpos);
+        ok = cudaGetLastError() == cudaSuccess &&
+             cudaMemcpyAsync(seg_off, dseg, (size_t)(E + 1) * 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+             cudaMemcpyAsync(route_tok, dtok, R * 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+             cudaMemcpyAsync(route_pos, dpos, R * 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+             cudaStreamSynchronize(s) == cudaSuccess;
+    }
+    if (!ok) {
+        set_error(std::string("route_segments_noalloc: ") + cudaGetErrorString(cudaGetLastError()));
+        return Z2B_ERR_CUDA;
+    }
+    return Z2B_OK;
 }
