@@ -155,6 +155,12 @@ int z2b_last_step_launches(const z2b_ctx* ctx);
  * returns n_layer). */
 int z2b_last_step_active(const z2b_ctx* ctx, int32_t* out, int cap);
 
+/* Average device time of one expert GEMV launch (which: 0 = gate/up + SwiGLU, 1 = down)
+ * over `reps` plain launches that cycle through the MoE layers' weights, on the routing
+ * left by the last step; also its algorithmic bytes (routed experts' weights +
+ * activations). For the roofline; no reference counterpart. */
+int z2b_time_expert_gemv(z2b_ctx* ctx, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch);
+
 const char* z2b_last_error(void);
 
 #ifdef __cplusplus

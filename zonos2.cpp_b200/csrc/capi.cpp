@@ -197,6 +197,12 @@ int z2b_last_step_active(const z2b_ctx* ctx, int32_t* out, int cap) {
     return L;
 }
 
+int z2b_time_expert_gemv(z2b_ctx* ctx, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch) {
+    if (!ctx || !ms_per_launch || !bytes_per_launch || which < 0 || which > 1) { set_error("bad argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_time_expert_gemv(ctx->c, which, reps, ms_per_launch, bytes_per_launch);
+}
+
 const char* z2b_last_error(void) { return last_error(); }
 
 int z2b_debug_last_sel(z2b_ctx* ctx, int32_t* out, int cap) {

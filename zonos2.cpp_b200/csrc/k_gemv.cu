@@ -46,22 +46,31 @@ template <> struct Dec<GT_Q4_K> {
     static constexpr bool kMinMma = false;
     uint32_t amin[2] = {0u, 0u};
     __half2 S[2][2], M[2][2];                 // [sub-block 0/1][row r / r+8], M holds -min
+    // Scales without the conversion pipe: the 6-bit fields become exact halves through
+    // the 0x6400 exponent (1024 + v, minus 1024), and d * sc (exact in f32, 17 bits) is
+    // rounded once by the half multiply, the same value __float2half_rn(d * sc) gives.
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
+        const __half2 k1024 = hc(0x6400);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const uint4 hd = *(const uint4*)(T + (r + 8 * h) * 16);
-            const float d = __half2float(__ushort_as_half((uint16_t)(hd.x & 0xffff)));
-            const float dm = __half2float(__ushort_as_half((uint16_t)(hd.x >> 16)));
+            const __half2 dd = u2h(prmt(hd.x, 0u, 0x1010u));          // (d, d)
+            const __half2 nm = u2h(prmt(hd.x, 0u, 0x3232u) ^ 0x80008000u);   // (-dmin, -dmin)
             uint32_t f;
             if (q == 0) f = hd.y;
             else if (q == 1) f = __funnelshift_r(hd.y, hd.z, 24);
             else if (q == 2) f = __funnelshift_r(hd.z, hd.w, 16);
             else f = hd.w >> 8;
-            S[0][h] = __float2half2_rn(d * (float)(f & 63));
-            S[1][h] = __float2half2_rn(d * (float)((f >> 6) & 63));
-            M[0][h] = __float2half2_rn(-(dm * (float)((f >> 12) & 63)));
-            M[1][h] = __float2half2_rn(-(dm * (float)((f >> 18) & 63)));
+            // (sc0, sc1) and (m0, m1) as 1024 + v halves
+            const uint32_t sc = lop3_and_or(f, 0x3Fu, lop3_and_or(f << 10, 0x003F0000u, 0x64006400u));
+            const uint32_t mn = lop3_and_or(f >> 12, 0x3Fu, lop3_and_or(f >> 2, 0x003F0000u, 0x64006400u));
+            const __half2 s01 = __hmul2(__hsub2(u2h(sc), k1024), dd);
+            const __half2 m01 = __hmul2(__hsub2(u2h(mn), k1024), nm);
+            S[0][h] = u2h(prmt(h2u(s01), 0u, 0x1010u));
+            S[1][h] = u2h(prmt(h2u(s01), 0u, 0x3232u));
+            M[0][h] = u2h(prmt(h2u(m01), 0u, 0x1010u));
+            M[1][h] = u2h(prmt(h2u(m01), 0u, 0x3232u));
         }
     }
     template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
@@ -82,14 +91,22 @@ template <> struct Dec<GT_Q6_K> {
     static constexpr bool kMinMma = false;
     uint32_t amin[2] = {0u, 0u};
     __half2 S[4][2];
+    // int8 scales as exact halves (1152 + sc - 1152 via the 0x6400 exponent: the byte is
+    // biased by 128), times d rounded once by the half multiply (d * sc is exact in f32).
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
+        const __half2 k1152 = hc(0x6480);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint32_t sc = *(const uint32_t*)(T + (r + 8 * h) * 16 + 4 * q);
-            const float d = __half2float(*(const __half*)(T + 256 + 2 * (r + 8 * h)));
-#pragma unroll
-            for (int j = 0; j < 4; ++j) S[j][h] = __float2half2_rn(d * (float)(int8_t)(sc >> (8 * j)));
+            const uint32_t sc = *(const uint32_t*)(T + (r + 8 * h) * 16 + 4 * q) ^ 0x80808080u;   // sc + 128
+            const uint16_t dbits = *(const uint16_t*)(T + 256 + 2 * (r + 8 * h));
+            const __half2 dd = u2h((uint32_t)dbits * 0x10001u);
+            const __half2 s01 = __hmul2(__hsub2(u2h(prmt(sc, 0x64646464u, 0x4140u)), k1152), dd);   // bytes 0, 1
+            const __half2 s23 = __hmul2(__hsub2(u2h(prmt(sc, 0x64646464u, 0x4342u)), k1152), dd);   // bytes 2, 3
+            S[0][h] = u2h(prmt(h2u(s01), 0u, 0x1010u));
+            S[1][h] = u2h(prmt(h2u(s01), 0u, 0x3232u));
+            S[2][h] = u2h(prmt(h2u(s23), 0u, 0x1010u));
+            S[3][h] = u2h(prmt(h2u(s23), 0u, 0x3232u));
         }
     }
     template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
@@ -404,8 +421,10 @@ void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStrea
 
 }  // namespace
 
-void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem) {
+void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
+                   int* cps) {
     (void)ntg;
+    *cps = 1;
     const int max_cpw = std::max(1, MAXKS / m.steps);       // chunks a warp can hold in registers
     const int min_nw = (m.chunks + max_cpw - 1) / max_cpw;
     // smallest warp count >= min(8, chunks) that splits the chunks evenly, else the

@@ -44,6 +44,7 @@ struct GemvParams {
     const int* n_active;            // device: number of experts with routes
     const int* active;              // device: active expert ids (ascending)
     const int* seg_off;             // device: [E+1] route offsets in expert order
+    const int* tile_off;            // device: [n_active+1] prefix of 8-token tiles per active expert
     const int* route_tok;           // device: token of each route (expert order)
     const float* route_w;           // device: route probability (GM_DOWN)
     // activations
@@ -55,11 +56,12 @@ struct GemvParams {
     float cap;                      // EPI_SOFTCAP
     uint32_t* err;
     // launch geometry (host-filled)
-    int n_stages, stage_bytes;
+    int n_stages, stage_bytes, cps;  // ring depth per warp, bytes per stage, chunks per stage
 };
 
 // Chooses warps/stages for a weight matrix and fills the launch geometry.
-void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem);
+void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
+                   int* cps);
 void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s);
 
 // ---- decode-step kernels -----------------------------------------------------------
@@ -119,6 +121,7 @@ struct StepBufs {
     float* rpart; int rpart_T;      // [4][rpart_T][rd] router down-projection partial sums
     int* sel; float* selw; int kmax;// [T][kmax]
     int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
+    int* tile_off;                  // [MAX_EXPERTS + 1] prefix of 8-token tiles over active experts
     int* ticket;
     __half* y;                      // [R][ff]
     float* out_route;               // [R][d]

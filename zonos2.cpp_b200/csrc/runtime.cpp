@@ -119,6 +119,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     acc((size_t)D.n_layer * T * c->kmax * 4);
     acc((size_t)4 * T * std::max(D.rd, 1) * 4);
     acc((size_t)T * nkv * 4);
+    acc((MAX_EXPERTS + 1) * 4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -147,6 +148,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.err = carve<uint32_t>(p, 1);
     B.sel_log = carve<int>(p, (size_t)D.n_layer * T * c->kmax); B.sel_log_T = T;
     B.attn_ticket = carve<int>(p, (size_t)T * nkv);
+    B.tile_off = carve<int>(p, MAX_EXPERTS + 1);
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -245,7 +247,7 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
     p.total_items = items;
     p.X = X; p.ldx = ldx; p.T = T; p.out = out; p.ldo = ldo; p.cap = cap; p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem);
+    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
     const int grid = std::min(items, c->m->n_sm * ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
@@ -262,7 +264,7 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
     p.w0 = w0.tiles;
     p.w1 = mode == GM_GATEUP ? ly.up_exps.tiles : nullptr;
     p.expert_stride = w0.expert_stride;
-    p.n_active = c->B.n_active; p.active = c->B.active; p.seg_off = c->B.seg_off;
+    p.n_active = c->B.n_active; p.active = c->B.active; p.seg_off = c->B.seg_off; p.tile_off = c->B.tile_off;
     p.route_tok = c->B.route_tok; p.route_w = c->B.route_w;
     if (mode == GM_GATEUP) {
         p.X = c->B.cur; p.ldx = D.n_embd; p.yout = c->B.y; p.ldy = D.n_ff; p.out_rows = D.n_ff;
@@ -271,13 +273,15 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
     }
     p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem);
+    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
     const int grid = c->m->n_sm * ctas_per_sm(smem);
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
 }
 
 }  // namespace
+
+void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode); }
 
 void enqueue_step(Ctx* c, int T, int n_out) {
     Model* m = c->m;
@@ -647,6 +651,51 @@ int ctx_sync(Ctx* c) {
     CK(cudaMemcpyAsync(c->h_misc, c->B.err, 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     if (c->h_misc[0]) { set_error("device error flags 0x" + std::to_string(c->h_misc[0])); return Z2B_ERR_DEVICE; }
+    return Z2B_OK;
+}
+
+}  // namespace z2b
+
+namespace z2b {
+
+// Re-launches one expert GEMV class (0 = gate/up, 1 = down) `reps` times, cycling over
+// the MoE layers so every launch streams a different layer's weights, on the routing
+// state the last step left in the step buffers (its final MoE layer). Back-to-back
+// launches with CUDA events on the context's stream around the whole loop; returns the average
+// duration per launch and the algorithmic bytes per launch (routed experts' weights +
+// activations in + results out).
+int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch) {
+    Model* m = c->m;
+    std::vector<int> moe;
+    for (int L = 0; L < (int)m->layers.size(); ++L)
+        if (m->layers[L].is_moe) moe.push_back(L);
+    if (moe.empty() || reps < 1 || c->last_T < 1) { set_error("time_expert_gemv: needs a MoE model and a previous step"); return Z2B_ERR_ARG; }
+    int n_active = 0, routes = 0;
+    CK(cudaMemcpyAsync(&n_active, c->B.n_active, 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    const LayerDev& l0 = m->layers[moe.back()];
+    CK(cudaMemcpy(&routes, c->B.seg_off + l0.n_expert, 4, cudaMemcpyDeviceToHost));
+    const Dims& D = m->dims;
+    const DevMat& w = which == 0 ? l0.gate_exps : l0.down_exps;
+    const uint64_t per_expert = (uint64_t)w.n_row_tiles * w.chunks * w.tile_bytes * (which == 0 ? 2 : 1);
+    const uint64_t act = which == 0 ? (uint64_t)routes * D.n_embd * 2 + (uint64_t)routes * D.n_ff * 2
+                                    : (uint64_t)routes * D.n_ff * 2 + (uint64_t)routes * D.n_embd * 4;
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    const bool prof = c->profiling;
+    c->profiling = false;
+    CK(cudaEventRecord(e0, c->stream));
+    for (int r = 0; r < reps; ++r) gemv_moe_public(c, m->layers[moe[r % moe.size()]], which == 0 ? GM_GATEUP : GM_DOWN);
+    CK(cudaEventRecord(e1, c->stream));
+    CK(cudaEventSynchronize(e1));
+    c->profiling = prof;
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_per_launch = ms / reps;
+    *bytes_per_launch = (uint64_t)n_active * per_expert + act;
     return Z2B_OK;
 }
 

@@ -90,6 +90,7 @@ def lib():
             "z2b_run_schedule": ([P, I, I, V, V, I, V], I),
             "z2b_last_run_launches": ([P], ctypes.c_long),
             "z2b_profile": ([P, I, V, V, I], I),
+            "z2b_time_expert_gemv": ([P, I, I, V, V], I),
             "z2b_test_dequant": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, I, V], I),
             "z2b_test_gemv": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V, I, V], I),
             "z2b_host_tiles_bytes": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
@@ -217,6 +218,13 @@ class BatchCtx:
 
     def stream(self) -> int:
         return lib().z2b_ctx_stream(self.h) or 0
+
+    def time_expert_gemv(self, which: int, reps: int):
+        """(ms per launch, algorithmic bytes per launch) of the expert gate/up (0) or down (1)
+        GEMV, timed over `reps` back-to-back launches on the last step's routing."""
+        ms, nb = ctypes.c_double(), ctypes.c_uint64()
+        _check(lib().z2b_time_expert_gemv(self.h, int(which), int(reps), ctypes.byref(ms), ctypes.byref(nb)))
+        return ms.value, nb.value
 
     def last_step_bytes(self):
         w, k, o = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
