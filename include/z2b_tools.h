@@ -55,6 +55,11 @@ int z2b_host_unpack_tiles(uint32_t type, int64_t rows, int64_t k, const void* ti
  * for n_tok f16 activation rows with the projection-mode tile GEMV.
  * Return 0, 4 (CUDA error), 6 (device error flag) or 7 (unsupported). */
 int z2b_test_dequant(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, int from_tiles, float* out);
+/* Runs the kernels' bounded mbarrier wait (at most `polls` <= 4096 polls) on a phase that
+ * never completes: *outcome = 2 when the wait gave up (1 if it completed), *err_word =
+ * the device error word it left (DERR_WAIT_TIMEOUT = 1), *elapsed_ns = how long the
+ * wait took. No fault, no trap. */
+int z2b_test_wait_timeout(uint32_t polls, uint32_t* err_word, uint32_t* outcome, uint64_t* elapsed_ns);
 int z2b_test_gemv(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, const uint16_t* x_f16,
                   int n_tok, float* out);
 

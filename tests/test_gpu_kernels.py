@@ -98,3 +98,17 @@ def test_route_permutation_bitexact(E, k, T):
     counts = np.bincount(sel.ravel(), minlength=E)
     assert np.array_equal(seg, np.concatenate([[0], np.cumsum(counts)]).astype(np.int32))
     assert np.array_equal(tok, exp_tok) and np.array_equal(pos, exp_pos)
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """The kernels' mbarrier wait on a phase nothing completes: it stops after its poll
+    limit, sets DERR_WAIT_TIMEOUT and returns; the context keeps working afterwards."""
+    L = R.lib()
+    L.z2b_test_wait_timeout.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    err, out, ns = ctypes.c_uint32(7), ctypes.c_uint32(7), ctypes.c_uint64(0)
+    assert L.z2b_test_wait_timeout(64, ctypes.byref(err), ctypes.byref(out), ctypes.byref(ns)) == 0
+    assert out.value == 2 and err.value == 1
+    print(f"bounded wait: 64 polls gave up after {ns.value / 1e3:.1f} us")
+    assert ns.value < 5e9
+    # the device is still usable: a kernel test right after succeeds
+    test_pack_prefix_sum_bitexact()

@@ -15,8 +15,10 @@ enum DevErr : uint32_t {
     DERR_PAGE = 4u,           // a KV position had no page mapped
 };
 
-// Bound on mbarrier polls. try_wait already suspends for a hardware-defined interval,
-// so this is seconds of wall time: far beyond any copy that can complete.
+// Bound on mbarrier polls. try_wait itself suspends for a short hardware-defined
+// interval, so this is seconds of wall time: far beyond any copy that can complete.
+// (An explicit suspend-time hint makes a waiting warp sleep past the phase completion,
+// which costs microseconds per stage, so the polls carry none.)
 constexpr uint32_t kMaxWaitPolls = 1u << 22;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -56,8 +58,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait; returns false (and records the error) if the phase never completed.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-    for (uint32_t i = 0; i < kMaxWaitPolls; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          uint32_t max_polls = kMaxWaitPolls) {
+    for (uint32_t i = 0; i < max_polls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     if (err) atomicOr(err, (uint32_t)DERR_WAIT_TIMEOUT);
     return false;

@@ -25,7 +25,6 @@ namespace z2b {
 
 namespace {
 
-constexpr int NTG = 2;       // n-tiles (8 tokens each) per pass over a staged item
 constexpr int MAXKS = 16;    // k-steps per warp per item (register budget for B)
 
 __device__ __forceinline__ __half2 hc(uint16_t bits) { return __half2half2(__ushort_as_half(bits)); }
@@ -43,8 +42,6 @@ template <int WT> struct Dec;
 // the weight itself (rounding q*S alone and subtracting the min later doubles it).
 template <> struct Dec<GT_Q4_K> {
     static constexpr int KS = 16, KC = 256;
-    static constexpr bool kMinMma = false;
-    uint32_t amin[2] = {0u, 0u};
     __half2 S[2][2], M[2][2];                 // [sub-block 0/1][row r / r+8], M holds -min
     // Scales without the conversion pipe: the 6-bit fields become exact halves through
     // the 0x6400 exponent (1024 + v, minus 1024), and d * sc (exact in f32, 17 bits) is
@@ -88,8 +85,6 @@ template <> struct Dec<GT_Q4_K> {
 
 template <> struct Dec<GT_Q6_K> {
     static constexpr int KS = 16, KC = 256;
-    static constexpr bool kMinMma = false;
-    uint32_t amin[2] = {0u, 0u};
     __half2 S[4][2];
     // int8 scales as exact halves (1152 + sc - 1152 via the 0x6400 exponent: the byte is
     // biased by 128), times d rounded once by the half multiply (d * sc is exact in f32).
@@ -130,8 +125,6 @@ template <> struct Dec<GT_Q6_K> {
 
 template <> struct Dec<GT_Q8_0> {
     static constexpr int KS = 8, KC = 128;
-    static constexpr bool kMinMma = false;
-    uint32_t amin[2] = {0u, 0u};
     __half2 D[2];
     __device__ __forceinline__ void prep(const uint8_t* T, int lane) {
         const int r = lane >> 2, q = lane & 3;
@@ -152,8 +145,6 @@ template <> struct Dec<GT_Q8_0> {
 // F16 with KS k-steps per chunk (KS = 4, 2, 1)
 template <int KS_> struct DecF16 {
     static constexpr int KS = KS_, KC = 16 * KS_;
-    static constexpr bool kMinMma = false;
-    uint32_t amin[2] = {0u, 0u};
     __device__ __forceinline__ void prep(const uint8_t*, int) {}
     template <int s> __device__ __forceinline__ void frag(const uint8_t* T, int lane, uint32_t a[4]) const {
         const uint4 w = *(const uint4*)(T + (s * 32 + lane) * 16);
@@ -164,8 +155,8 @@ template <int KS_> struct DecF16 {
 template <int WT, int KSF> struct DecSel { using T = Dec<WT>; };
 template <int KSF> struct DecSel<GT_F16, KSF> { using T = DecF16<KSF>; };
 
-// unrolled k-step loop
-template <class D, int s, int KS> struct KLoop {
+// unrolled k-step loop: decode one k-step of the tile, multiply with the token tiles
+template <class D, int NTG, int s, int KS> struct KLoop {
     template <int NMAT>
     __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, int kbase,
                                                const uint32_t (&B)[NTG][MAXKS][2], float (&acc)[NMAT][NTG][4],
@@ -175,33 +166,53 @@ template <class D, int s, int KS> struct KLoop {
 #pragma unroll
         for (int nt = 0; nt < NTG; ++nt)
             if (nt < ntv) mma16816(acc[m][nt], a[0], a[1], a[2], a[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
-        KLoop<D, s + 1, KS>::template run<NMAT>(dec, T, lane, kbase, B, acc, m, ntv);
+        KLoop<D, NTG, s + 1, KS>::template run<NMAT>(dec, T, lane, kbase, B, acc, m, ntv);
     }
 };
-template <class D, int KS> struct KLoop<D, KS, KS> {
+template <class D, int NTG, int KS> struct KLoop<D, NTG, KS, KS> {
     template <int NMAT>
     __device__ __forceinline__ static void run(const D&, const uint8_t*, int, int, const uint32_t (&)[NTG][MAXKS][2],
                                                float (&)[NMAT][NTG][4], int, int) {}
 };
 
+// Item = (segment or active expert s, row tile rt); a CTA walks a contiguous run of
+// items, so positions advance by increment (no division per item).
+struct ItemPos { int s, rt; };
 struct ItemRef { int expert; int seg; int rt; const uint8_t* src[2]; int n_tok; int tok0; };
 
 template <int MODE>
-__device__ __forceinline__ ItemRef item_ref(const GemvParams& p, int item, int c0) {
-    ItemRef r{};
+__device__ __forceinline__ ItemPos item_seek(const GemvParams& p, int item) {
+    ItemPos q{0, 0};
     if constexpr (MODE == GM_PROJ) {
-        int s = 0, base = 0;
-        while (s + 1 < p.n_seg && item >= base + p.seg[s].n_row_tiles) { base += p.seg[s].n_row_tiles; ++s; }
-        r.seg = s; r.rt = item - base; r.expert = -1;
-        r.src[0] = p.seg[s].tiles + ((size_t)r.rt * p.chunks + c0) * p.tile_bytes;
+        int base = 0;
+        while (q.s + 1 < p.n_seg && item >= base + p.seg[q.s].n_row_tiles) { base += p.seg[q.s].n_row_tiles; ++q.s; }
+        q.rt = item - base;
+    } else {
+        q.s = item / p.n_row_tiles;
+        q.rt = item - q.s * p.n_row_tiles;
+    }
+    return q;
+}
+
+template <int MODE>
+__device__ __forceinline__ void item_next(const GemvParams& p, ItemPos& q) {
+    const int nrt = (MODE == GM_PROJ) ? p.seg[q.s].n_row_tiles : p.n_row_tiles;
+    if (++q.rt == nrt) { q.rt = 0; ++q.s; }
+}
+
+template <int MODE>
+__device__ __forceinline__ ItemRef item_ref(const GemvParams& p, ItemPos q, int c0) {
+    ItemRef r{};
+    r.rt = q.rt;
+    if constexpr (MODE == GM_PROJ) {
+        r.seg = q.s; r.expert = -1;
+        r.src[0] = p.seg[q.s].tiles + ((size_t)q.rt * p.chunks + c0) * p.tile_bytes;
         r.src[1] = nullptr;
         r.n_tok = p.T; r.tok0 = 0;
     } else {
-        const int a = item / p.n_row_tiles;
-        r.rt = item % p.n_row_tiles;
-        r.expert = p.active[a];
+        r.expert = p.active[q.s];
         r.seg = 0;
-        const size_t off = (size_t)r.expert * p.expert_stride + ((size_t)r.rt * p.chunks + c0) * p.tile_bytes;
+        const size_t off = (size_t)r.expert * p.expert_stride + ((size_t)q.rt * p.chunks + c0) * p.tile_bytes;
         r.src[0] = p.w0 + off;
         r.src[1] = (MODE == GM_GATEUP) ? p.w1 + off : nullptr;
         r.tok0 = p.seg_off[r.expert];
@@ -217,8 +228,11 @@ __device__ __forceinline__ int x_row(const GemvParams& p, const ItemRef& it, int
     else return it.tok0 + n;
 }
 
-template <int WT, int KSF, int MODE>
-__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
+// Token tiles per pass: 2 (up to 16 tokens) for the projections and gate/up, 1 for the
+// down pass, whose lighter registers let three blocks share an SM (measured: gate/up
+// keeps its two-stage ring at two blocks per SM; down gains from the third block).
+template <int WT, int KSF, int MODE, int NTG, int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     using D = typename DecSel<WT, KSF>::T;
     constexpr int KS = D::KS, KC = D::KC;
     constexpr int NMAT = (MODE == GM_GATEUP) ? 2 : 1;
@@ -243,10 +257,13 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
 
     int it0 = 0, it1 = 0;
     int issued_upto = -1;                        // last item whose copy was issued
+    ItemPos ipos{0, 0};                          // position of the next item to issue
     auto issue = [&](int item, int slot) {
         issued_upto = item;
+        const ItemPos q = ipos;
+        item_next<MODE>(p, ipos);
         if (lane == 0 && ncw > 0) {
-            const ItemRef it = item_ref<MODE>(p, item, c0);
+            const ItemRef it = item_ref<MODE>(p, q, c0);
             mbar_expect_tx(&mybar[slot], wbytes * NMAT);
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
@@ -258,6 +275,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
         it0 = (int)((int64_t)blockIdx.x * p.total_items / gridDim.x);
         it1 = (int)((int64_t)(blockIdx.x + 1) * p.total_items / gridDim.x);
         issued_upto = it0 - 1;
+        ipos = item_seek<MODE>(p, it0);
         for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
         pdl_wait();
         pdl_release();
@@ -268,19 +286,20 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
         it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
         it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
         issued_upto = it0 - 1;
+        ipos = item_seek<MODE>(p, it0);
         for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
     }
 
     bool failed = false;
     uint32_t B[NTG][MAXKS][2];
-    uint32_t BX[NTG][MAXCPW];                    // Q4_K: activation sums of the lane's two sub-blocks
     int b_key = -2;                              // token set the B fragments hold (expert, or 0)
-    constexpr float kAccScale = D::kMinMma ? 0.0625f : 1.0f;   // Q4_K products carry a factor 16
     int red_par = 0;
+    ItemPos cpos = item_seek<MODE>(p, it0);
+    int slot = 0;
+    uint32_t parity = 0;
     for (int item = it0; item < it1; ++item) {
-        const int j = item - it0, slot = j % NS;
-        const uint32_t parity = (uint32_t)((j / NS) & 1);
-        const ItemRef it = item_ref<MODE>(p, item, c0);
+        const ItemRef it = item_ref<MODE>(p, cpos, c0);
+        item_next<MODE>(p, cpos);
         if (!failed && ncw > 0 && item <= issued_upto) failed = !mbar_wait(&mybar[slot], parity, p.err);
         const uint8_t* st = mystage + slot * p.stage_bytes;
         const int n_groups = (it.n_tok + 8 * NTG - 1) / (8 * NTG);
@@ -305,21 +324,13 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                         const __half* xr = ok ? p.X + (size_t)x_row<MODE>(p, it, n) * p.ldx : nullptr;
 #pragma unroll
                         for (int cc = 0; cc < MAXCPW; ++cc) {
-                            float xs0 = 0.0f, xs1 = 0.0f;      // sums over the lane's two sub-blocks
 #pragma unroll
                             for (int s = 0; s < KS; ++s) {
                                 uint2 v = make_uint2(0u, 0u);
                                 if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
-                                if constexpr (D::kMinMma) {
-                                    const float2 f0 = __half22float2(u2h(v.x)), f1 = __half22float2(u2h(v.y));
-                                    const float part = (f0.x + f0.y) + (f1.x + f1.y);
-                                    if (s < KS / 2) xs0 += part; else xs1 += part;
-                                    v.x = h2u(__hmul2(u2h(v.x), hc(0x4C00)));          // x16 for the 1x pairs
-                                }
                                 B[nt][cc * KS + s][0] = v.x;
                                 B[nt][cc * KS + s][1] = v.y;
                             }
-                            if constexpr (D::kMinMma) BX[nt][cc] = h2u(__floats2half2_rn(xs0, xs1));
                         }
                     }
                     b_key = (n_groups == 1) ? key : -2;
@@ -332,12 +343,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                             const uint8_t* T = st + m * wbytes + cc * p.tile_bytes;
                             D dec;
                             dec.prep(T, lane);
-                            KLoop<D, 0, KS>::template run<NMAT>(dec, T, lane, cc * KS, B, acc, m, ntv);
-                            if constexpr (D::kMinMma) {
-#pragma unroll
-                                for (int nt = 0; nt < NTG; ++nt)
-                                    if (nt < ntv) mma1688(acc[m][nt], dec.amin[0], dec.amin[1], BX[nt][cc]);
-                            }
+                            KLoop<D, NTG, 0, KS>::template run<NMAT>(dec, T, lane, cc * KS, B, acc, m, ntv);
                         }
                     }
                 }
@@ -355,8 +361,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
 #pragma unroll
                 for (int nt = 0; nt < NTG; ++nt)
                     *(float4*)(myred + ((m * NTG + nt) * 32 + lane) * 4) =
-                        make_float4(acc[m][nt][0] * kAccScale, acc[m][nt][1] * kAccScale,
-                                    acc[m][nt][2] * kAccScale, acc[m][nt][3] * kAccScale);
+                        make_float4(acc[m][nt][0], acc[m][nt][1], acc[m][nt][2], acc[m][nt][3]);
             __syncthreads();
             red_par ^= 1;
             for (int t = threadIdx.x; t < NTG * 128; t += blockDim.x) {
@@ -396,6 +401,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
                 }
             }
         }
+        if (++slot == NS) { slot = 0; parity ^= 1u; }
     }
     // After a failed wait (error already recorded) later copies may still be in flight:
     // wait for each of them, bounded, before the shared memory goes away. Every warp
@@ -412,9 +418,9 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
 template <int WT, int KSF>
 void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s) {
     void (*k)(const GemvParams);
-    if (p.mode == GM_PROJ) k = gemv_kernel<WT, KSF, GM_PROJ>;
-    else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP>;
-    else k = gemv_kernel<WT, KSF, GM_DOWN>;
+    if (p.mode == GM_PROJ) k = gemv_kernel<WT, KSF, GM_PROJ, 2, 512, 1>;
+    else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP, 2, 256, 2>;
+    else k = gemv_kernel<WT, KSF, GM_DOWN, 1, 256, 3>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     launch_pdl(k, dim3(grid), dim3(nwarps * 32), (size_t)smem, s, p);
 }
@@ -423,26 +429,32 @@ void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStrea
 
 void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
                    int* cps) {
-    (void)ntg;
     *cps = 1;
     const int max_cpw = std::max(1, MAXKS / m.steps);       // chunks a warp can hold in registers
     const int min_nw = (m.chunks + max_cpw - 1) / max_cpw;
-    // smallest warp count >= min(8, chunks) that splits the chunks evenly, else the
-    // register-bound minimum
     int nw = 0;
-    for (int cand = std::max(min_nw, std::min(8, m.chunks)); cand <= 16; ++cand)
-        if (m.chunks % cand == 0) { nw = cand; break; }
-    if (nw == 0) nw = std::max(min_nw, std::min(16, m.chunks));
+    if (ntg == 1) {
+        // expert passes: 8 warps (256 threads, three blocks per SM), K split as evenly as it goes
+        nw = std::max(min_nw, std::min(8, m.chunks));
+    } else {
+        // smallest warp count >= min(8, chunks) that splits the chunks evenly, else the
+        // register-bound minimum
+        for (int cand = std::max(min_nw, std::min(8, m.chunks)); cand <= 16; ++cand)
+            if (m.chunks % cand == 0) { nw = cand; break; }
+        if (nw == 0) nw = std::max(min_nw, std::min(16, m.chunks));
+    }
     const int cpw = (m.chunks + nw - 1) / nw;
     const int sb = cpw * m.tile_bytes * nmat;
-    const int red = 2 * nw * nmat * NTG * 128 * 4;
+    const int red = 2 * nw * nmat * ntg * 128 * 4;
     auto total = [&](int ns) { return 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red; };
-    // deepest ring that still lets two blocks share an SM (block-level barriers of one
-    // block then overlap the other's streaming); else one block with up to 4 stages
+    // deepest ring (up to 4 stages) at the target blocks per SM: three for the expert down
+    // pass, two for gate/up (two matrices per stage) and the projections (one block's
+    // barriers overlap the other's streaming)
     const int per_sm = 233472, per_block_reserved = 1024;
+    const int want = (ntg == 1 && nmat == 1) ? 3 : 2;
     int ns = 0;
-    for (int cand = 4; cand >= 2; --cand)
-        if (2 * (total(cand) + per_block_reserved) <= per_sm) { ns = cand; break; }
+    for (int cand = 4; cand >= 1 && ns == 0; --cand)
+        if (want * (total(cand) + per_block_reserved) <= per_sm) ns = cand;
     if (ns == 0) {
         ns = 1;
         for (int cand = 4; cand >= 1; --cand)

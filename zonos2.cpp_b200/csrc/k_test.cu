@@ -182,3 +182,42 @@ done:
     if (derr) cudaFree(derr);
     return rc;
 }
+
+// The bounded wait the kernels use, on an mbarrier phase that nothing completes: the
+// wait gives up after `polls` polls, records DERR_WAIT_TIMEOUT in the error word and the
+// kernel returns normally, so the context stays usable.
+namespace z2b {
+namespace {
+__global__ void wait_timeout_kernel(uint32_t polls, uint32_t* err, uint32_t* done, unsigned long long* ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        z2b::mbar_init(&bar, 1);                // one arrival expected, none will come
+        z2b::fence_mbar_init();
+    }
+    __syncthreads();
+    unsigned long long t0, t1;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    const bool ok = z2b::mbar_wait(&bar, 0, err, polls);
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+    if (threadIdx.x == 0) { *done = ok ? 1u : 2u; *ns = t1 - t0; }
+}
+}  // namespace
+}  // namespace z2b
+
+extern "C" int z2b_test_wait_timeout(uint32_t polls, uint32_t* err_word, uint32_t* outcome, uint64_t* elapsed_ns) {
+    if (!err_word || !outcome || !elapsed_ns || polls == 0 || polls > 4096) return 1;
+    uint32_t* d = nullptr;
+    if (cudaMalloc(&d, 16) != cudaSuccess) return 4;
+    int rc = 0;
+    uint32_t h[4] = {0, 0, 0, 0};
+    if (cudaMemset(d, 0, 16) != cudaSuccess) rc = 4;
+    if (!rc) {
+        z2b::wait_timeout_kernel<<<1, 32>>>(polls, d, d + 1, reinterpret_cast<unsigned long long*>(d + 2));
+        if (cudaGetLastError() != cudaSuccess || cudaMemcpy(h, d, 16, cudaMemcpyDeviceToHost) != cudaSuccess) rc = 4;
+    }
+    cudaFree(d);
+    *err_word = h[0];
+    *outcome = h[1];
+    std::memcpy(elapsed_ns, h + 2, 8);
+    return rc;
+}

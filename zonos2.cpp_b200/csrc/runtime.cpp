@@ -54,7 +54,9 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     c->n_slots = n_slots;
     c->slot_cap = (slot_cap_frames + PAGE - 1) / PAGE * PAGE;
     c->pages_per_slot = c->slot_cap / PAGE;
-    c->T_max = std::max(n_slots, 512);
+    // rows per step: every slot decoding plus 2048 prompt rows admitted in the same step
+    // (four 512-row prompts), at most 8192
+    c->T_max = std::min(8192, std::max(512, n_slots + 2048));
     c->O_max = n_slots;
     c->D_max = std::min(1024, c->T_max);
     c->kmax = 1;
@@ -273,8 +275,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
     }
     p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
-    const int grid = c->m->n_sm * ctas_per_sm(smem);
+    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, mode == GM_GATEUP ? 2 : 1, &nw, &p.n_stages, &p.stage_bytes, &smem,
+                  &p.cps);
+    // blocks per SM the kernel is built for: two for gate/up, three for down
+    const int grid = c->m->n_sm * std::min(mode == GM_GATEUP ? 2 : 3, ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
 }
