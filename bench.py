@@ -378,10 +378,13 @@ def main():
     hbm, peak_src = peaks()
     gu_ms, gu_n = prof["expert_gateup_gemv"]
     achieved = gu_iso_bytes / (gu_iso_ms * 1e-3) / 1e9
+    # DRAM bytes per launch: ncu's measured traffic / algorithmic ratio for this kernel
+    # (profiles/roofline_traffic.json), applied to this run's launch
     traffic = None
     tf = os.path.join(ROOT, "profiles", "roofline_traffic.json")
     if os.path.exists(tf):
-        traffic = json.load(open(tf)).get("expert_gateup_gemv_dram_bytes_per_launch")
+        ratio = json.load(open(tf)).get("traffic_over_algorithmic")
+        traffic = ratio * gu_iso_bytes if ratio else None
     step_ms_prof = sum(v[0] for v in prof.values()) / prof_steps
     line = {
         "metric": METRIC,
