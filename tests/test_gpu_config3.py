@@ -86,7 +86,10 @@ def test_config3_mixed_step_parity(model_dir, preset):
 
 def test_config3_batch64_invariance(model_dir):
     """60 decode streams + 4 new prompts per step at 8 layers (Q6_K): every decode
-    stream's logits in the mixed batch equal, bit for bit, the same stream decoded alone."""
+    stream's logits in the mixed batch match the same stream decoded alone. Prompt rows
+    push some experts past GEMM_MIN_TOKENS routes, and those experts run on the tensor-
+    core GEMM (a different summation order than the GEMV the lone stream uses), so the
+    match is to tolerance here; decode-only batches stay bit-exact (test_gpu_parity)."""
     path = _model(model_dir, "zonos2_q6k", 8)
     m = R.Model(path)
     try:
@@ -98,6 +101,28 @@ def test_config3_batch64_invariance(model_dir):
         for k in (3, 41):
             solo = _mixed_run(m, 1, [dec_lens[k]], [[], []], 2, seed=700 + k)
             for s in range(2):
-                assert np.array_equal(solo[s]["logits"][0].view(np.uint32), run[s]["logits"][k].view(np.uint32))
+                assert cos(solo[s]["logits"][0], run[s]["logits"][k]) >= 0.99999
+                assert max_abs_rel(solo[s]["logits"][0], run[s]["logits"][k]) <= 1e-3
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("preset", ["zonos2", "zonos2_q6k", "zonos2_q8"])
+def test_long_prompt_tensor_core_path_parity(model_dir, preset):
+    """A 512-row prompt in one step routes about 64 tokens to each of the 32 experts, so
+    about half of them take the tcgen05 grouped GEMM (>= GEMM_MIN_TOKENS routes) while the
+    rest stay on the tile GEMV: the prompt's last-row logits against the oracle."""
+    path = _model(model_dir, preset, 4)
+    m = R.Model(path)
+    try:
+        ctx = R.BatchCtx(m, 1, 600)
+        p = prompt(512, 4242)
+        ctx.slot_reset(0, R.Sampling(greedy=True))
+        lg = ctx.slot_prefill(0, p)
+        ctx.close()
+    finally:
+        m.close()
+    oc = O.Ctx(O.Model(path, O.EXACT), 1, 600)
+    ref = oc.prefill(0, p)
+    assert cos(lg, ref) >= 0.9999, cos(lg, ref)
+    assert max_abs_rel(lg, ref) <= 1e-2

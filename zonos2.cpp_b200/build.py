@@ -26,7 +26,7 @@ SYNTH_LIB = os.path.join(PKG, "libz2b_synth.so")
 
 HOST_COMMON = ["gguf.cpp", "quant.cpp"]
 Z2B_HOST = ["repack.cpp", "model.cpp", "runtime.cpp", "capi.cpp"]
-Z2B_CUDA = ["k_gemv.cu", "k_attn.cu", "k_router.cu", "k_misc.cu", "k_test.cu"]
+Z2B_CUDA = ["k_gemv.cu", "k_gemm.cu", "k_attn.cu", "k_router.cu", "k_misc.cu", "k_test.cu"]
 
 
 def _headers():

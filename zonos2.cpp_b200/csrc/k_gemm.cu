@@ -1,0 +1,277 @@
+// k_gemm.cu — grouped expert GEMM on the 5th-generation tensor cores (tcgen05), for the
+// experts that receive many routed tokens in a step (prompt rows, large batches).
+//
+// Replaces ggml_mul_mat_id (src/zonos2-graph.cpp:223-231) for those experts; the tile
+// GEMV in k_gemv.cu keeps the experts with few tokens. Tile = (expert, 128 weight rows,
+// 64 routed tokens). Per 256-wide K group the four warps dequantise the block's eight
+// 16-row weight tiles (the same in-register decoders as the GEMV, so the weight values
+// are identical) into shared memory in the UMMA K-major interleaved layout, gather the
+// tokens' activation rows next to them, and one thread issues tcgen05.mma (M 128, N 64,
+// K 16, f16 x f16 -> f32) into tensor-memory accumulators; a tcgen05.commit on an
+// mbarrier tells the block when the operands may be overwritten. The epilogue reads the
+// accumulators with tcgen05.ld: SwiGLU to f16 y (gate/up), or x route weight (down).
+//
+// Shared-memory operand layout (K-major, no swizzle): 8x8 core matrices of 16-byte rows;
+// element (m, k) of a block at (k / 8) * LBO + (m / 8) * 128 + (m % 8) * 16 + (k % 8) * 2
+// with LBO = 128 * rows / 8 (2048 B for 128 weight rows, 1024 B for 64 tokens).
+#include "common.cuh"
+#include "gguf.h"
+#include "kernels.h"
+#include "launch.cuh"
+#include "tile_layout.h"
+#include "k_decode.cuh"
+
+namespace z2b {
+
+namespace {
+
+constexpr int GT_M = 128;                        // weight rows per tile
+constexpr int GT_N = 64;                         // routed tokens per tile
+constexpr int GT_K = 256;                        // k per dequantised group
+constexpr int A_BYTES = GT_M * GT_K * 2;         // 64 KB per matrix
+constexpr int B_BYTES = GT_N * GT_K * 2;         // 32 KB
+constexpr uint32_t A_LBO = GT_M / 8 * 128, B_LBO = GT_N / 8 * 128, CORE_SBO = 128;
+// instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, N, M
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(GT_N >> 3) << 17) | ((uint32_t)(GT_M >> 4) << 24);
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(CORE_SBO >> 4) << 32) |
+           (1ull << 46);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+        :: "r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Decode k-steps s..KS-1 of one 16-row tile chunk into the A block (rows row0.., k
+// offset kofs within the group): lane (r, q) holds rows r, r+8 at k = q*KC/4 + 4s.
+template <class D, int s, int KS> struct DqLoop {
+    __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, uint8_t* A, int row0, int kofs) {
+        uint32_t a[4];
+        dec.template frag<s>(T, lane, a);
+        const int r = lane >> 2, q = lane & 3;
+        const int k = kofs + q * (D::KC / 4) + 4 * s;
+        uint8_t* p0 = A + (k >> 3) * A_LBO + ((row0 + r) >> 3) * 128 + ((row0 + r) & 7) * 16 + (k & 7) * 2;
+        uint8_t* p1 = A + (k >> 3) * A_LBO + ((row0 + r + 8) >> 3) * 128 + ((row0 + r + 8) & 7) * 16 + (k & 7) * 2;
+        *reinterpret_cast<uint2*>(p0) = make_uint2(a[0], a[2]);
+        *reinterpret_cast<uint2*>(p1) = make_uint2(a[1], a[3]);
+        DqLoop<D, s + 1, KS>::run(dec, T, lane, A, row0, kofs);
+    }
+};
+template <class D, int KS> struct DqLoop<D, KS, KS> {
+    __device__ __forceinline__ static void run(const D&, const uint8_t*, int, uint8_t*, int, int) {}
+};
+
+template <int WT, int KSF, int MODE>
+__global__ void __launch_bounds__(128, 1) moe_gemm_kernel(const GemvParams p) {
+    using D = typename DecSel<WT, KSF>::T;
+    constexpr int KC = D::KC, KS = D::KS;
+    constexpr int CPG = GT_K / KC;                   // tile chunks per K group
+    constexpr int NMAT = (MODE == GM_GATEUP) ? 2 : 1;
+    constexpr uint32_t NCOLS = NMAT == 2 ? 128u : 64u;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* Bs = smem + NMAT * A_BYTES;
+    __shared__ __align__(8) uint64_t mma_bar;
+    __shared__ uint32_t tmem_base;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(&tmem_base)), "r"(NCOLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&mma_bar, 1);
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = tmem_base;
+    pdl_wait();
+    pdl_release();
+
+    // big experts: active[n_small .. n_active)
+    const int e_lo = *p.n_small, e_hi = *p.n_active;
+    const int n_rb = (p.out_rows + GT_M - 1) / GT_M;   // 128-row blocks per expert
+    const int n_groups = (p.chunks + CPG - 1) / CPG;
+    int n_tiles = 0;
+    for (int a = e_lo; a < e_hi; ++a) {
+        const int e = p.active[a];
+        n_tiles += (p.seg_off[e + 1] - p.seg_off[e] + GT_N - 1) / GT_N * n_rb;
+    }
+    uint32_t phase = 0;
+    bool failed = false;
+    for (int t = blockIdx.x; t < n_tiles && !failed; t += gridDim.x) {
+        // locate (expert, token block, row block) of tile t
+        int a = e_lo, base = 0, e = 0, ne = 0;
+        for (; a < e_hi; ++a) {
+            e = p.active[a];
+            ne = p.seg_off[e + 1] - p.seg_off[e];
+            const int nt = (ne + GT_N - 1) / GT_N * n_rb;
+            if (t < base + nt) break;
+            base += nt;
+        }
+        const int tb = (t - base) / n_rb, rb = (t - base) % n_rb;
+        const int tok0 = p.seg_off[e] + tb * GT_N;
+        const int nv = min(GT_N, ne - tb * GT_N);
+
+        for (int g = 0; g < n_groups; ++g) {
+            if (g > 0) {                                 // previous group's MMAs done with smem
+                failed = __syncthreads_or(mbar_wait(&mma_bar, phase, p.err) ? 0 : 1) != 0;
+                phase ^= 1u;
+                if (failed) break;
+            }
+            const int c0 = g * CPG, nc = min(CPG, p.chunks - c0);
+            // A: warp w decodes row tiles 2w, 2w+1 of the block (both matrices)
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                uint8_t* A = smem + m * A_BYTES;
+                const uint8_t* wbase = (m == 0 ? p.w0 : p.w1) + (size_t)e * p.expert_stride;
+                for (int j = 2 * warp; j < 2 * warp + 2; ++j) {
+                    const int rt = rb * (GT_M / 16) + j;
+                    for (int cc = 0; cc < CPG; ++cc) {
+                        if (rt < p.n_row_tiles && cc < nc) {
+                            const uint8_t* T = wbase + ((size_t)rt * p.chunks + c0 + cc) * p.tile_bytes;
+                            D dec;
+                            dec.prep(T, lane);
+                            DqLoop<D, 0, KS>::run(dec, T, lane, A, 16 * j, cc * KC);
+                        } else {
+                            // rows past the matrix or k past K: zeros
+                            const int r = lane >> 2, q = lane & 3;
+                            for (int s = 0; s < KS; ++s) {
+                                const int k = cc * KC + q * (KC / 4) + 4 * s;
+                                for (int h = 0; h < 2; ++h) {
+                                    const int row = 16 * j + r + 8 * h;
+                                    *reinterpret_cast<uint2*>(A + (k >> 3) * A_LBO + (row >> 3) * 128 + (row & 7) * 16 +
+                                                              (k & 7) * 2) = make_uint2(0u, 0u);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            // B: the tile's token rows, 16 bytes per (token, 8-wide k chunk)
+            const int kg = c0 * KC;
+            for (int i = tid; i < GT_N * (GT_K / 8); i += blockDim.x) {
+                const int n = i % GT_N, kc = i / GT_N;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (n < nv && kc * 8 < nc * KC) {
+                    int row = tok0 + n;
+                    if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
+                    v = *reinterpret_cast<const uint4*>(p.X + (size_t)row * p.ldx + kg + kc * 8);
+                }
+                *reinterpret_cast<uint4*>(Bs + kc * B_LBO + (n >> 3) * 128 + (n & 7) * 16) = v;
+            }
+            fence_proxy_async();                         // generic-proxy writes -> tensor core reads
+            tc_fence_before();
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const int kblocks = nc * KC / 16;
+                for (int kb = 0; kb < kblocks; ++kb) {
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        const uint64_t da = umma_desc(smem_u32(smem + m * A_BYTES) + 2 * kb * A_LBO, A_LBO);
+                        const uint64_t db = umma_desc(smem_u32(Bs) + 2 * kb * B_LBO, B_LBO);
+                        umma_f16(tm + m * GT_N, da, db, (g > 0 || kb > 0) ? 1u : 0u);
+                    }
+                }
+                umma_commit(&mma_bar);
+            }
+            __syncwarp();
+        }
+        if (!failed) {
+            failed = __syncthreads_or(mbar_wait(&mma_bar, phase, p.err) ? 0 : 1) != 0;
+            phase ^= 1u;
+        }
+        tc_fence_after();
+        if (!failed) {
+            // epilogue: warp w owns TMEM lanes (rows) 32w..32w+31, 16 token columns at a time
+            const int row = rb * GT_M + 32 * warp + lane;
+            const uint32_t lane_addr = tm + ((uint32_t)(32 * warp) << 16);
+#pragma unroll 1
+            for (int c = 0; c < GT_N; c += 16) {
+                float v0[16], v1[16];
+                tmem_ld16(lane_addr + c, v0);
+                if constexpr (NMAT == 2) tmem_ld16(lane_addr + GT_N + c, v1);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int n = c + i;
+                    if (n >= nv || row >= p.out_rows) continue;
+                    if constexpr (MODE == GM_GATEUP) {
+                        const float gt = v0[i], up = v1[i];
+                        const float si = gt / (1.0f + expf(-gt));
+                        p.yout[(size_t)(tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
+                    } else {
+                        p.out[(size_t)(tok0 + n) * p.ldo + row] = v0[i] * p.route_w[tok0 + n];
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();                                 // accumulators read before the next tile
+        tc_fence_after();
+    }
+    // after a failed wait, give the issued MMAs time to retire before TMEM is released
+    if (failed) (void)mbar_wait(&mma_bar, phase, nullptr);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tm), "r"(NCOLS) : "memory");
+}
+
+template <int WT, int KSF>
+void gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
+    void (*k)(const GemvParams) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
+                                                      : moe_gemm_kernel<WT, KSF, GM_DOWN>;
+    const int smem = (p.mode == GM_GATEUP ? 2 : 1) * A_BYTES + B_BYTES;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    launch_pdl(k, dim3(grid), dim3(128), (size_t)smem, s, p);
+}
+
+}  // namespace
+
+bool moe_gemm_supported(const DevMat& m) {
+    switch (m.type) {
+        case GT_Q4_K: case GT_Q6_K: return true;              // 256-wide chunks
+        case GT_Q8_0: return true;                            // 128-wide chunks, two per group
+        case GT_F16: return m.steps == 4;                     // 64-wide chunks, four per group
+        default: return false;
+    }
+}
+
+void launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s) {
+    switch (p.type) {
+        case GT_Q4_K: gemm_typed<GT_Q4_K, 16>(p, grid, s); break;
+        case GT_Q6_K: gemm_typed<GT_Q6_K, 16>(p, grid, s); break;
+        case GT_Q8_0: gemm_typed<GT_Q8_0, 8>(p, grid, s); break;
+        case GT_F16: gemm_typed<GT_F16, 4>(p, grid, s); break;
+        default: break;
+    }
+}
+
+}  // namespace z2b

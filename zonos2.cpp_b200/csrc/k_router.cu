@@ -56,9 +56,11 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 // in the token's top-k. Called by one whole block; cnt is a [MAX_EXPERTS] shared array.
 // tile_off (optional): [n_active + 1] prefix over active experts of ceil(routes / 8), the
 // 8-token column tiles each expert's GEMV items cover.
+// n_small (optional): experts with fewer than GEMM_MIN_TOKENS routes are listed first in
+// active[0, n_small) (the tile GEMV's list); the rest follow (the tensor-core GEMM's list).
 __device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
                                int* seg_off, int* active, int* n_active, int* route_tok, float* route_w,
-                               int* route_pos, int* tile_off) {
+                               int* route_pos, int* tile_off, int* n_small) {
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     const int R = T * k;
@@ -71,14 +73,19 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
         int off = 0, na = 0, tiles = 0;
         for (int e = 0; e < E; ++e) {
             seg_off[e] = off;
-            if (cnt[e] > 0) {
+            off += cnt[e];
+        }
+        seg_off[E] = off;
+        for (int big = 0; big < 2; ++big) {
+            for (int e = 0; e < E; ++e) {
+                if (cnt[e] == 0 || (n_small && (cnt[e] >= GEMM_MIN_TOKENS) != (big == 1))) continue;
                 if (tile_off) tile_off[na] = tiles;
                 tiles += (cnt[e] + 7) / 8;
                 active[na++] = e;
             }
-            off += cnt[e];
+            if (n_small && big == 0) *n_small = na;
+            if (!n_small) break;
         }
-        seg_off[E] = off;
         if (tile_off) tile_off[na] = tiles;
         *n_active = na;
     }
@@ -317,7 +324,7 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     if (!s_last) return;
     __threadfence();
     build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.active, b.n_active, b.route_tok, b.route_w,
-                   b.route_pos, b.tile_off);
+                   b.route_pos, b.tile_off, b.n_small);
     if (threadIdx.x == 0) {
         if (b.layer_active) b.layer_active[layer] = *b.n_active;
         *b.ticket = 0;
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
 __global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
                                   int* n_active, int* route_tok, float* route_w, int* route_pos) {
     __shared__ int cnt[MAX_EXPERTS];
-    build_segments(sel, selw, T, k, k, E, cnt, seg_off, active, n_active, route_tok, route_w, route_pos, nullptr);
+    build_segments(sel, selw, T, k, k, E, cnt, seg_off, active, n_active, route_tok, route_w, route_pos, nullptr, nullptr);
 }
 
 }  // namespace

@@ -9,6 +9,7 @@
 namespace z2b {
 
 constexpr int MAX_EXPERTS = 256;
+constexpr int GEMM_MIN_TOKENS = 64;  // routes from which an expert takes the tensor-core GEMM
 constexpr int NCOL = 10;            // input columns per row: 9 audio codebooks + text
 constexpr int PAGE = 256;           // KV page length (tokens)
 
@@ -45,6 +46,7 @@ struct GemvParams {
     const int* active;              // device: active expert ids (ascending)
     const int* seg_off;             // device: [E+1] route offsets in expert order
     const int* tile_off;            // device: [n_active+1] prefix of 8-token tiles per active expert
+    const int* n_small;             // device: GEMV experts active[0, n_small); GEMM experts after them
     const int* route_tok;           // device: token of each route (expert order)
     const float* route_w;           // device: route probability (GM_DOWN)
     // activations
@@ -63,6 +65,9 @@ struct GemvParams {
 void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
                    int* cps);
 void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s);
+// tcgen05 grouped GEMM over the experts active[n_small, n_active) (k_gemm.cu)
+bool moe_gemm_supported(const DevMat& m);
+void launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s);
 
 // ---- decode-step kernels -----------------------------------------------------------
 struct Dims {
@@ -122,6 +127,7 @@ struct StepBufs {
     int* sel; float* selw; int kmax;// [T][kmax]
     int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
     int* tile_off;                  // [MAX_EXPERTS + 1] prefix of 8-token tiles over active experts
+    int* n_small;                   // experts in active[] with < GEMM_MIN_TOKENS routes (listed first)
     int* ticket;
     __half* y;                      // [R][ff]
     float* out_route;               // [R][d]

@@ -122,6 +122,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     acc((size_t)4 * T * std::max(D.rd, 1) * 4);
     acc((size_t)T * nkv * 4);
     acc((MAX_EXPERTS + 1) * 4);
+    acc(4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -151,6 +152,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.sel_log = carve<int>(p, (size_t)D.n_layer * T * c->kmax); B.sel_log_T = T;
     B.attn_ticket = carve<int>(p, (size_t)T * nkv);
     B.tile_off = carve<int>(p, MAX_EXPERTS + 1);
+    B.n_small = carve<int>(p, 1);
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -255,7 +257,10 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
     c->launches++;
 }
 
-void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
+// Expert pass (gate/up + SwiGLU, or down x route weight) over the routes of the step:
+// the tile GEMV takes the experts with few routes; when the step has at least
+// GEMM_MIN_TOKENS tokens, experts with that many routes go to the tcgen05 GEMM.
+void gemv_moe(Ctx* c, const LayerDev& ly, int mode, int T) {
     ProfScope ps(c, mode == GM_GATEUP ? PC_GATEUP : PC_DOWN);
     const Dims& D = c->m->dims;
     GemvParams p{};
@@ -266,7 +271,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
     p.w0 = w0.tiles;
     p.w1 = mode == GM_GATEUP ? ly.up_exps.tiles : nullptr;
     p.expert_stride = w0.expert_stride;
-    p.n_active = c->B.n_active; p.active = c->B.active; p.seg_off = c->B.seg_off; p.tile_off = c->B.tile_off;
+    const bool split = T >= GEMM_MIN_TOKENS && moe_gemm_supported(w0);
+    p.n_active = split ? c->B.n_small : c->B.n_active;
+    p.n_small = c->B.n_small;
+    p.active = c->B.active; p.seg_off = c->B.seg_off; p.tile_off = c->B.tile_off;
     p.route_tok = c->B.route_tok; p.route_w = c->B.route_w;
     if (mode == GM_GATEUP) {
         p.X = c->B.cur; p.ldx = D.n_embd; p.yout = c->B.y; p.ldy = D.n_ff; p.out_rows = D.n_ff;
@@ -281,11 +289,16 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode) {
     const int grid = c->m->n_sm * std::min(mode == GM_GATEUP ? 2 : 3, ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
+    if (split) {
+        p.n_active = c->B.n_active;
+        launch_moe_gemm(p, c->m->n_sm, c->stream);
+        c->launches++;
+    }
 }
 
 }  // namespace
 
-void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode); }
+void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode, c->last_T); }
 
 void enqueue_step(Ctx* c, int T, int n_out) {
     Model* m = c->m;
@@ -318,8 +331,8 @@ void enqueue_step(Ctx* c, int T, int n_out) {
         }
         { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches += router_launches(ly.small); }
         if (ly.is_moe) first_moe = false;
-        gemv_moe(c, ly, GM_GATEUP);
-        gemv_moe(c, ly, GM_DOWN);
+        gemv_moe(c, ly, GM_GATEUP, T);
+        gemv_moe(c, ly, GM_DOWN, T);
         const bool last = L == D.n_layer - 1;
         {
             ProfScope ps(c, PC_COMBINE);
