@@ -213,6 +213,43 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def expert_sweep(args):
+    """Config 4: the MoE expert FFN of one ZONOS2 layer (E 32, d 2048, ff 1408, Q4_K gate/up,
+    F16 down) on x ~ N(0, 1) with top-4 routing from router logits N(0, 1) plus a Zipf(1.1)
+    per-expert bias, at T in {16, 64, 256, 1024, 4096}. Weight GB/s over the routed experts'
+    bytes (the GEMV regime's roofline) and TFLOP/s (2 T k 3 d ff, the GEMM regime's)."""
+    load_pkg()
+    import z2b.runtime as R
+    import z2b.synth as S
+    path = S.cached("zonos2", directory=model_dir(), n_layer=1, expert_used=[4])
+    m = R.Model(path)
+    ctx = R.BatchCtx(m, 16, 64)                      # rows per step: 16 + 4096
+    hbm, peak_src = peaks()
+    tflops_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    E, k, d, ff = m.hp.n_expert, 4, m.hp.n_embd, m.hp.n_ff
+    for T in (16, 64, 256, 1024, 4096):
+        g = np.random.default_rng(T)
+        x = g.standard_normal((T, d)).astype(np.float32)
+        bias = np.log(1.0 / np.arange(1, E + 1) ** 1.1)[g.permutation(E)]
+        logits = g.standard_normal((T, E)) + bias
+        p = np.exp(logits - logits.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        sel = np.argsort(-p, 1, kind="stable")[:, :k].astype(np.int32)
+        w = np.take_along_axis(p, sel, 1).astype(np.float32)
+        _, ms, nbytes, n_gemm = ctx.expert_op(0, x, sel, w, reps=max(args.steps // 8, 10), want_out=False)
+        flops = 2.0 * T * k * 3 * d * ff
+        act = T * d * 2 + T * k * (ff * 2 * 2 + d * 4)
+        line = {"metric": "expert FFN op (config 4)", "T": T, "ms": ms,
+                "weight_gbs": nbytes / (ms * 1e-3) / 1e9, "hbm_frac": (nbytes + act) / (ms * 1e-3) / 1e9 / hbm,
+                "tflops": flops / (ms * 1e-3) / 1e12, "tensor_frac": flops / (ms * 1e-3) / 1e12 / tflops_peak,
+                "routed_expert_bytes": nbytes, "experts_on_tcgen05_gemm": n_gemm,
+                "peaks": {"hbm_gbs": hbm, "bf16_tflops": tflops_peak, "source": peak_src}}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    m.close()
+
+
 def workload_name():
     return (f"config2: ZONOS2-scale Q4_K backbone, {STREAMS} streams/GPU, ctx U[{CTX_RANGE[0]},{CTX_RANGE[1]}], "
             f"{STEPS_PER_STREAM} frames per stream, continuous refill with {REFILL_PROMPT}-row prompts")
@@ -228,8 +265,12 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=16)
     ap.add_argument("--layers", type=int, default=28,
                     help="fewer layers for small ncu captures (the headline run uses 28)")
+    ap.add_argument("--expert-sweep", action="store_true",
+                    help="config 4: the isolated expert op over T in {16, 64, 256, 1024, 4096}, one JSON line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.expert_sweep:
+        return expert_sweep(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

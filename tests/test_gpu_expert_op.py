@@ -1,0 +1,66 @@
+"""The isolated MoE expert op (config 4 of the benchmark set: E 32, d 2048, ff 1408, Q4_K
+gate/up, F16 down, top-4 routing skewed by a Zipf(1.1) bias) through z2b_expert_op,
+against a float32 numpy restatement over gguf-py's dequantised weights. T = 16 runs on
+the tile GEMV only; T = 320 sends the most-loaded experts to the tcgen05 GEMM."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import z2b.runtime as R
+import z2b.synth as S
+
+pytestmark = pytest.mark.gpu
+
+
+def routing(T, E, k, seed):
+    """Router logits N(0, 1) + Zipf(s = 1.1) per-expert bias, softmax, top-k; route
+    weight = the selected probability (no renormalisation, as the model)."""
+    g = np.random.default_rng(seed)
+    bias = np.log(1.0 / np.arange(1, E + 1) ** 1.1)
+    logits = g.standard_normal((T, E)) + bias[g.permutation(E)]
+    p = np.exp(logits - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    sel = np.argsort(-p, 1, kind="stable")[:, :k].astype(np.int32)
+    return sel, np.take_along_axis(p, sel, 1).astype(np.float32)
+
+
+def reference(path, x, sel, w):
+    from gguf import GGUFReader
+    from gguf.quants import dequantize
+    rd = GGUFReader(path)
+    t = {tt.name: tt for tt in rd.tensors}
+    W = {n: dequantize(t[f"blk.0.ffn_{n}_exps.weight"].data, t[f"blk.0.ffn_{n}_exps.weight"].tensor_type).astype(np.float32)
+         for n in ("gate", "up", "down")}
+    out = np.zeros_like(x)
+    for e in np.unique(sel):
+        rows, cols = np.nonzero(sel == e)
+        xe = x[rows]
+        gt = xe @ W["gate"][e].T
+        y = (gt / (1.0 + np.exp(-gt))) * (xe @ W["up"][e].T)
+        out[rows] += w[rows, cols][:, None] * (y @ W["down"][e].T)
+    return out
+
+
+@pytest.mark.parametrize("T", [16, 320])
+def test_expert_op_vs_float32(model_dir, T):
+    path = S.cached("zonos2", directory=model_dir, n_layer=1, expert_used=[4])
+    m = R.Model(path)
+    try:
+        ctx = R.BatchCtx(m, 16, 64)
+        x = np.random.default_rng(T).standard_normal((T, m.hp.n_embd)).astype(np.float32)
+        sel, w = routing(T, m.hp.n_expert, 4, seed=T + 1)
+        out, _, nbytes, n_gemm = ctx.expert_op(0, x, sel, w)
+        ctx.close()
+    finally:
+        m.close()
+    if T >= 64:
+        assert n_gemm > 0                      # the skewed experts took the tensor-core path
+    else:
+        assert n_gemm == 0
+    ref = reference(path, x, sel, w)
+    for t in range(T):
+        a, b = out[t].astype(np.float64), ref[t].astype(np.float64)
+        c = a @ b / (np.linalg.norm(a) * np.linalg.norm(b))
+        assert c >= 0.9999, (t, c)
+    assert np.abs(out - ref).max() / np.abs(ref).max() <= 1e-2

@@ -203,6 +203,16 @@ int z2b_time_expert_gemv(z2b_ctx* ctx, int which, int reps, double* ms_per_launc
     return ctx_time_expert_gemv(ctx->c, which, reps, ms_per_launch, bytes_per_launch);
 }
 
+int z2b_expert_op(z2b_ctx* ctx, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k,
+                  float* out, int reps, double* ms, uint64_t* weight_bytes, int32_t* n_gemm_experts) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    int ng = 0;
+    const int rc = ctx_expert_op(ctx->c, layer, x, T, sel, selw, k, out, reps, ms, weight_bytes, &ng);
+    if (n_gemm_experts) *n_gemm_experts = ng;
+    return rc;
+}
+
 const char* z2b_last_error(void) { return last_error(); }
 
 int z2b_debug_last_sel(z2b_ctx* ctx, int32_t* out, int cap) {

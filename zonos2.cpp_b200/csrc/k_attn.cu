@@ -94,8 +94,10 @@ struct AttnSmem {
     static constexpr int CHUNK_BYTES = KCH * HD * 2;          // one K or V slice
     static constexpr int NS = HD >= 128 ? 3 : 4;
     static constexpr int STAGE = 2 * CHUNK_BYTES;
-    static constexpr int MERGE = 4 * 8 * (HD + 2) * 4;        // [warp][head][m, l, o]
-    static constexpr int BYTES = 128 + NS * STAGE + MERGE;
+    static constexpr int MERGE = 4 * 8 * (HD + 2) * 4;        // [warp][head][m, l, o], over the stages
+    static_assert(MERGE <= NS * STAGE, "the merge area reuses the drained stages");
+    // two blocks per SM for HD = 128 (2 x 96 KB)
+    static constexpr int BYTES = 128 + NS * STAGE;
 };
 
 template <int HD, int G>
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     uint8_t* stages = smem + 128;
-    float* merge = reinterpret_cast<float*>(stages + SM::NS * SM::STAGE);
+    float* merge = reinterpret_cast<float*>(stages);          // used once every copy has landed
     // The token's slot, position and descriptor were written by the step's packer and the
     // cached keys below the slot's first new key by earlier steps: every kernel before
     // the immediate predecessor has completed once this grid runs (each kernel waits on
@@ -181,10 +183,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
 #pragma unroll
     for (int i = 0; i < KST; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
     bool failed = false;
+    int c_fail = 0;                              // first chunk whose wait gave up
 
     for (int c = 0; c < nchunks; ++c) {
         const int slotc = c % SM::NS;
-        if (!failed) failed = !mbar_wait(&bars[slotc], (uint32_t)((c / SM::NS) & 1), b.err);
+        if (!failed && !mbar_wait(&bars[slotc], (uint32_t)((c / SM::NS) & 1), b.err)) { failed = true; c_fail = c; }
         const uint8_t* Ks = stages + slotc * SM::STAGE;
         const uint8_t* Vs = Ks + SM::CHUNK_BYTES;
         const int kb = 16 * warp;                 // this warp's keys within the chunk
@@ -230,9 +233,16 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
                 mma16816(acc[mt], v0.x, v1.x, v0.y, v1.y, pb0, pb1);
             }
         }
-        __syncthreads();                         // stage consumed by all warps
+        // stage consumed by all warps; a failed wait anywhere stops the refills everywhere
+        if (__syncthreads_or(failed ? 1 : 0) && !failed) { failed = true; c_fail = c; }
         if (threadIdx.x == 0 && !failed && c + SM::NS < nchunks) { fence_proxy_async(); issue(c + SM::NS); }
     }
+    // After a failed wait (error recorded, results invalid) copies may still be landing
+    // in the stages: wait for them, bounded, before the stages become the merge area.
+    if (failed && threadIdx.x == 0)
+        for (int c = c_fail; c < nchunks && c < c_fail + SM::NS; ++c)
+            (void)mbar_wait(&bars[c % SM::NS], (uint32_t)((c / SM::NS) & 1), nullptr, 1u << 12);
+    __syncthreads();
     // per-warp state -> shared, merged over warps in a fixed order
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
@@ -309,9 +319,6 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
         for (int s2 = 0; s2 < ns; ++s2) O += cf[g * ns + s2] * __ldcg(base + (size_t)s2 * (HD + 2));
         const float gg = 1.0f / (1.0f + expf(-b.qkvg[(size_t)t * b.ldq + gate_off + h]));
         b.o[(size_t)t * nh * HD + (size_t)h * HD + e] = __float2half_rn((O / cl[G * ns + g]) * gg);
-    }
-    if (failed) {
-        for (int c = 0; c < SM::NS; ++c) (void)mbar_try_wait(&bars[c], 0);
     }
 }
 

@@ -38,11 +38,10 @@ template <> struct Dec<GT_Q4_K> {
             const uint4 hd = *(const uint4*)(T + (r + 8 * h) * 16);
             const __half2 dd = u2h(prmt(hd.x, 0u, 0x1010u));          // (d, d)
             const __half2 nm = u2h(prmt(hd.x, 0u, 0x3232u) ^ 0x80008000u);   // (-dmin, -dmin)
-            uint32_t f;
-            if (q == 0) f = hd.y;
-            else if (q == 1) f = __funnelshift_r(hd.y, hd.z, 24);
-            else if (q == 2) f = __funnelshift_r(hd.z, hd.w, 16);
-            else f = hd.w >> 8;
+            // quad q's 24 bits start at bit 24q of (y, z, w): selects, no divergent branch
+            const uint32_t lo = q < 2 ? hd.y : (q == 2 ? hd.z : hd.w);
+            const uint32_t hi = q < 2 ? hd.z : (q == 2 ? hd.w : 0u);
+            const uint32_t f = __funnelshift_r(lo, hi, (32 - 8 * q) & 31);
             // (sc0, sc1) and (m0, m1) as 1024 + v halves
             const uint32_t sc = lop3_and_or(f, 0x3Fu, lop3_and_or(f << 10, 0x003F0000u, 0x64006400u));
             const uint32_t mn = lop3_and_or(f >> 12, 0x3Fu, lop3_and_or(f >> 2, 0x003F0000u, 0x64006400u));

@@ -26,24 +26,25 @@ namespace z2b {
 
 namespace {
 
-// unrolled k-step loop: decode one k-step of the tile, multiply with the token tiles
+// unrolled k-step loop: decode one k-step of the tile, multiply with the first NTV token
+// tiles (NTV is a compile-time count, so no branch guards the mma)
 template <class D, int NTG, int s, int KS> struct KLoop {
-    template <int NMAT>
+    template <int NMAT, int NTV>
     __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, int kbase,
                                                const uint32_t (&B)[NTG][MAXKS][2], float (&acc)[NMAT][NTG][4],
-                                               int m, int ntv) {
+                                               int m) {
         uint32_t a[4];
         dec.template frag<s>(T, lane, a);
 #pragma unroll
-        for (int nt = 0; nt < NTG; ++nt)
-            if (nt < ntv) mma16816(acc[m][nt], a[0], a[1], a[2], a[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
-        KLoop<D, NTG, s + 1, KS>::template run<NMAT>(dec, T, lane, kbase, B, acc, m, ntv);
+        for (int nt = 0; nt < NTV; ++nt)
+            mma16816(acc[m][nt], a[0], a[1], a[2], a[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
+        KLoop<D, NTG, s + 1, KS>::template run<NMAT, NTV>(dec, T, lane, kbase, B, acc, m);
     }
 };
 template <class D, int NTG, int KS> struct KLoop<D, NTG, KS, KS> {
-    template <int NMAT>
+    template <int NMAT, int NTV>
     __device__ __forceinline__ static void run(const D&, const uint8_t*, int, int, const uint32_t (&)[NTG][MAXKS][2],
-                                               float (&)[NMAT][NTG][4], int, int) {}
+                                               float (&)[NMAT][NTG][4], int) {}
 };
 
 // Item = (segment or active expert s, row tile rt); a CTA walks a contiguous run of
@@ -214,7 +215,8 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                             const uint8_t* T = st + m * wbytes + cc * p.tile_bytes;
                             D dec;
                             dec.prep(T, lane);
-                            KLoop<D, NTG, 0, KS>::template run<NMAT>(dec, T, lane, cc * KS, B, acc, m, ntv);
+                            if (ntv == NTG) KLoop<D, NTG, 0, KS>::template run<NMAT, NTG>(dec, T, lane, cc * KS, B, acc, m);
+                            else KLoop<D, NTG, 0, KS>::template run<NMAT, 1>(dec, T, lane, cc * KS, B, acc, m);
                         }
                     }
                 }

@@ -5,6 +5,7 @@
 #include "launch.cuh"
 #include "quant.h"
 
+#include <algorithm>
 #include <vector>
 
 namespace z2b {
@@ -379,6 +380,18 @@ void launch_feed(SlotDesc* descs, int n, int* ids_in, const int* codes, const in
 void launch_pack(const StepBufs& b, int T, int n_out, cudaStream_t s) {
     (void)n_out;
     pack_kernel<<<1, 1024, 0, s>>>(b, T);
+}
+
+__global__ void to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+    pdl_wait();
+    pdl_release();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __float2half_rn(x[i]);
+}
+
+void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
+    const int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+    launch_pdl(to_f16_kernel, dim3(grid), dim3(256), 0, s, x, y, n);
 }
 
 void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s) {

@@ -331,6 +331,16 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     }
 }
 
+__global__ void segments_kernel(const StepBufs b, int T, int k, int E) {
+    __shared__ int cnt[MAX_EXPERTS];
+    pdl_wait();
+    pdl_release();
+    for (int j = threadIdx.x; j < T * b.kmax; j += blockDim.x) b.route_pos[j] = -1;
+    __syncthreads();
+    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.active, b.n_active, b.route_tok, b.route_w,
+                   b.route_pos, b.tile_off, b.n_small);
+}
+
 __global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
                                   int* n_active, int* route_tok, float* route_w, int* route_pos) {
     __shared__ int cnt[MAX_EXPERTS];
@@ -366,6 +376,10 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
 }
 
 int router_launches(const LayerSmall& ly) { return ly.is_moe ? 2 : 1; }
+
+void launch_segments(const StepBufs& b, int T, int k, int E, cudaStream_t s) {
+    launch_pdl(segments_kernel, dim3(1), dim3(1024), 0, s, b, T, k, E);
+}
 
 }  // namespace z2b
 

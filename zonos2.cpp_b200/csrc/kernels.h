@@ -162,6 +162,10 @@ void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys
 void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
                    cudaStream_t s);
 int router_launches(const LayerSmall& ly);
+// Expert segments from given router ids b.sel/b.selw (one block; the router's own last step).
+void launch_segments(const StepBufs& b, int T, int k, int E, cudaStream_t s);
+// f32 rows -> f16 rows (n values).
+void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 // Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the
 // next input row, advance n_past, and copy this step's host-drawn uniforms.
 void launch_sched_feed(const SlotDesc* step_descs, const int* src, int n, SlotDesc* descs, int* ids_in,

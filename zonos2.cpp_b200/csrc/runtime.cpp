@@ -54,9 +54,9 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     c->n_slots = n_slots;
     c->slot_cap = (slot_cap_frames + PAGE - 1) / PAGE * PAGE;
     c->pages_per_slot = c->slot_cap / PAGE;
-    // rows per step: every slot decoding plus 2048 prompt rows admitted in the same step
-    // (four 512-row prompts), at most 8192
-    c->T_max = std::min(8192, std::max(512, n_slots + 2048));
+    // rows per step: every slot decoding plus 4096 prompt rows admitted in the same step
+    // (eight 512-row prompts, or one 4096-token expert-op batch), at most 8192
+    c->T_max = std::min(8192, std::max(512, n_slots + 4096));
     c->O_max = n_slots;
     c->D_max = std::min(1024, c->T_max);
     c->kmax = 1;
@@ -713,6 +713,87 @@ int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uin
     cudaEventDestroy(e1);
     *ms_per_launch = ms / reps;
     *bytes_per_launch = (uint64_t)n_active * per_expert + act;
+    return Z2B_OK;
+}
+
+}  // namespace z2b
+
+namespace z2b {
+
+// One MoE layer's expert FFN on given activations and routing (the isolated expert op):
+// x -> f16, segments from the given ids, then the decode step's own expert passes
+// (tile GEMV for experts with few routes, tcgen05 GEMM for the rest). out[t] = sum over
+// the token's routes of selw * down(SwiGLU(gate, up)).
+int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k, float* out,
+                  int reps, double* ms, uint64_t* weight_bytes, int* n_gemm) {
+    Model* m = c->m;
+    const Dims& D = m->dims;
+    if (layer < 0 || layer >= (int)m->layers.size() || !m->layers[layer].is_moe) { set_error("expert_op: not a MoE layer"); return Z2B_ERR_ARG; }
+    const LayerDev& ly = m->layers[layer];
+    if (T < 1 || T > c->T_max || k < 1 || k > c->kmax || !x || !sel || !selw) { set_error("expert_op: bad T, k or pointers"); return Z2B_ERR_ARG; }
+    for (int i = 0; i < T * k; ++i)
+        if (sel[i] < 0 || sel[i] >= ly.n_expert) { set_error("expert_op: expert id out of range"); return Z2B_ERR_ARG; }
+    StepBufs B = c->B;
+    const size_t d = (size_t)D.n_embd;
+    std::vector<int32_t> hs((size_t)T * c->kmax, -1);
+    std::vector<float> hw((size_t)T * c->kmax, 0.0f);
+    for (int t = 0; t < T; ++t)
+        for (int j = 0; j < k; ++j) { hs[(size_t)t * c->kmax + j] = sel[t * k + j]; hw[(size_t)t * c->kmax + j] = selw[t * k + j]; }
+    CK(cudaMemcpyAsync(B.res, x, (size_t)T * d * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(B.sel, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(B.selw, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    launch_to_f16(B.res, B.cur, (size_t)T * d, c->stream);
+    launch_segments(B, T, k, ly.n_expert, c->stream);
+    const bool prof = c->profiling;
+    c->profiling = false;
+    gemv_moe(c, ly, GM_GATEUP, T);
+    gemv_moe(c, ly, GM_DOWN, T);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    if (reps > 0 && ms) {
+        cudaEvent_t e0, e1;
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        CK(cudaEventRecord(e0, c->stream));
+        for (int r = 0; r < reps; ++r) {
+            gemv_moe(c, ly, GM_GATEUP, T);
+            gemv_moe(c, ly, GM_DOWN, T);
+        }
+        CK(cudaEventRecord(e1, c->stream));
+        CK(cudaEventSynchronize(e1));
+        float t_ms = 0.0f;
+        CK(cudaEventElapsedTime(&t_ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms = t_ms / reps;
+    }
+    c->profiling = prof;
+    int na = 0, ns = 0;
+    CK(cudaMemcpy(&na, B.n_active, 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(&ns, B.n_small, 4, cudaMemcpyDeviceToHost));
+    uint32_t err = 0;
+    CK(cudaMemcpy(&err, B.err, 4, cudaMemcpyDeviceToHost));
+    if (err) { set_error("expert_op: device error word " + std::to_string(err)); return Z2B_ERR_DEVICE; }
+    const auto bytes = [](const DevMat& w) { return (uint64_t)w.n_row_tiles * w.chunks * w.tile_bytes; };
+    if (weight_bytes) *weight_bytes = (uint64_t)na * (bytes(ly.gate_exps) + bytes(ly.up_exps) + bytes(ly.down_exps));
+    if (n_gemm) *n_gemm = (T >= GEMM_MIN_TOKENS) ? na - ns : 0;
+    if (out) {
+        const int R = T * k;
+        std::vector<float> orr((size_t)R * d);
+        std::vector<int32_t> pos((size_t)T * c->kmax);
+        CK(cudaMemcpy(orr.data(), B.out_route, orr.size() * 4, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(pos.data(), B.route_pos, pos.size() * 4, cudaMemcpyDeviceToHost));
+        for (int t = 0; t < T; ++t) {
+            float* o = out + (size_t)t * d;
+            std::fill(o, o + d, 0.0f);
+            for (int j = 0; j < k; ++j) {
+                const int pr = pos[(size_t)t * c->kmax + j];
+                if (pr < 0 || pr >= R) { set_error("expert_op: route without a position"); return Z2B_ERR_DEVICE; }
+                const float* src = orr.data() + (size_t)pr * d;
+                for (size_t i = 0; i < d; ++i) o[i] += src[i];
+            }
+        }
+    }
     return Z2B_OK;
 }
 

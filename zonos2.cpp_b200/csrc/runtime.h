@@ -98,5 +98,7 @@ enum ProfClass { PC_PACK, PC_EMBED, PC_QKV, PC_ROPE, PC_ATTN, PC_ATTN_COMB, PC_W
 void account(Ctx* c, const z2b_slot_desc* descs, int n, int T);
 void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode);
 int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch);
+int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k, float* out,
+                  int reps, double* ms, uint64_t* weight_bytes, int* n_gemm);
 
 }  // namespace z2b

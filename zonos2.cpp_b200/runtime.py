@@ -91,6 +91,7 @@ def lib():
             "z2b_last_run_launches": ([P], ctypes.c_long),
             "z2b_profile": ([P, I, V, V, I], I),
             "z2b_time_expert_gemv": ([P, I, I, V, V], I),
+            "z2b_expert_op": ([P, I, V, I, V, V, I, V, I, V, V, V], I),
             "z2b_test_dequant": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, I, V], I),
             "z2b_test_gemv": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V, I, V], I),
             "z2b_host_tiles_bytes": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
@@ -225,6 +226,19 @@ class BatchCtx:
         ms, nb = ctypes.c_double(), ctypes.c_uint64()
         _check(lib().z2b_time_expert_gemv(self.h, int(which), int(reps), ctypes.byref(ms), ctypes.byref(nb)))
         return ms.value, nb.value
+
+    def expert_op(self, layer: int, x, sel, selw, reps: int = 0, want_out: bool = True):
+        """The isolated expert op of a MoE layer: returns (out [T][d] or None, ms per
+        repetition or None, routed weight bytes, experts on the tensor-core GEMM)."""
+        x = np.ascontiguousarray(x, np.float32)
+        sel = np.ascontiguousarray(sel, np.int32)
+        selw = np.ascontiguousarray(selw, np.float32)
+        T, k = sel.shape
+        out = np.empty((T, x.shape[1]), np.float32) if want_out else None
+        ms, nb, ng = ctypes.c_double(0.0), ctypes.c_uint64(0), ctypes.c_int32(0)
+        _check(lib().z2b_expert_op(self.h, int(layer), _ptr(x), T, _ptr(sel), _ptr(selw), k, _ptr(out), int(reps),
+                                   ctypes.byref(ms), ctypes.byref(nb), ctypes.byref(ng)))
+        return out, (ms.value if reps > 0 else None), nb.value, ng.value
 
     def last_step_bytes(self):
         w, k, o = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
