@@ -399,7 +399,9 @@ def main():
     e2e_ms = f0.elapsed_time(f1)
     clk = clocks.stop()
     # dominant kernel alone: the expert gate/up GEMV, back-to-back over the 28 layers'
-    # weights on the last step's routing (CUDA events on the context's stream)
+    # weights on the routing of a decode-only step (CUDA events on the context's stream)
+    dec = [(i, int(wl.n_past[i]), 1, R.WANT_SAMPLE) for i in range(STREAMS)]
+    ctx.step(dec, np.c_[cur_rows, np.full(STREAMS, hp.text_vocab)].astype(np.int32), want_logits=False)
     reps = 4 * hp.n_layer
     gu_iso_ms, gu_iso_bytes = ctx.time_expert_gemv(0, reps)
     dn_iso_ms, dn_iso_bytes = ctx.time_expert_gemv(1, reps)

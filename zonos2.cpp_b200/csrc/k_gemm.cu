@@ -21,6 +21,8 @@
 #include "tile_layout.h"
 #include "k_decode.cuh"
 
+#include <algorithm>
+
 namespace z2b {
 
 namespace {
@@ -28,6 +30,7 @@ namespace {
 constexpr int GT_M = 128;                        // weight rows per tile
 constexpr int GT_N = 64;                         // routed tokens per tile
 constexpr int GT_K = 256;                        // k per dequantised group
+constexpr int GT_WARPS_ROWS = GT_M / 16;         // 16-row weight tiles per 128-row block
 constexpr int A_BYTES = GT_M * GT_K * 2;         // 64 KB per matrix
 constexpr int B_BYTES = GT_N * GT_K * 2;         // 32 KB
 constexpr uint32_t A_LBO = GT_M / 8 * 128, B_LBO = GT_N / 8 * 128, CORE_SBO = 128;
@@ -85,28 +88,50 @@ template <class D, int KS> struct DqLoop<D, KS, KS> {
     __device__ __forceinline__ static void run(const D&, const uint8_t*, int, uint8_t*, int, int) {}
 };
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+constexpr int GM_WARPS = 8;                      // one 16-row weight tile per warp
+constexpr int RAW_NS = 3;                        // raw weight stages per warp (K groups ahead)
+
+// Per tile: the (K group g, matrix m) stages stream in order s = g * NMAT + m. Each warp
+// bulk-copies its own 16-row tile's chunks of stage s into a ring RAW_NS stages ahead;
+// the activation rows of group g are gathered with cp.async into one of two B buffers a
+// group ahead; the single A buffer is rewritten once the MMAs of the previous stage have
+// released it (tcgen05.commit -> mma_bar), then one thread issues the stage's MMAs.
 template <int WT, int KSF, int MODE>
-__global__ void __launch_bounds__(128, 1) moe_gemm_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
     using D = typename DecSel<WT, KSF>::T;
     constexpr int KC = D::KC, KS = D::KS;
     constexpr int CPG = GT_K / KC;                   // tile chunks per K group
     constexpr int NMAT = (MODE == GM_GATEUP) ? 2 : 1;
     constexpr uint32_t NCOLS = NMAT == 2 ? 128u : 64u;
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* Bs = smem + NMAT * A_BYTES;
+    uint8_t* A = smem;                               // [A_BYTES]
+    uint8_t* Bb = smem + A_BYTES;                    // [2][B_BYTES]
+    uint8_t* raw = Bb + 2 * B_BYTES;                 // [GM_WARPS][RAW_NS][CPG * tile_bytes]
     __shared__ __align__(8) uint64_t mma_bar;
+    __shared__ __align__(8) uint64_t raw_bar[GM_WARPS][RAW_NS];
     __shared__ uint32_t tmem_base;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t stage_bytes = (uint32_t)(CPG * p.tile_bytes);
+    const int ns = p.n_stages;                       // raw ring depth per warp (1..RAW_NS)
+    uint8_t* myraw = raw + (size_t)warp * ns * stage_bytes;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(&tmem_base)), "r"(NCOLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 0) {
-        mbar_init(&mma_bar, 1);
-        fence_mbar_init();
-    }
+    if (tid == 0) mbar_init(&mma_bar, 1);
+    if (lane == 0)
+        for (int i = 0; i < RAW_NS; ++i) mbar_init(&raw_bar[warp][i], 1);
+    fence_mbar_init();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -114,107 +139,141 @@ __global__ void __launch_bounds__(128, 1) moe_gemm_kernel(const GemvParams p) {
     pdl_wait();
     pdl_release();
 
-    // big experts: active[n_small .. n_active)
+    // experts with GEMM routes: active[n_small .. n_active), routes [seg_mid[e], seg_off[e + 1])
     const int e_lo = *p.n_small, e_hi = *p.n_active;
     const int n_rb = (p.out_rows + GT_M - 1) / GT_M;   // 128-row blocks per expert
     const int n_groups = (p.chunks + CPG - 1) / CPG;
+    const int n_st = n_groups * NMAT;
     int n_tiles = 0;
     for (int a = e_lo; a < e_hi; ++a) {
         const int e = p.active[a];
-        n_tiles += (p.seg_off[e + 1] - p.seg_off[e] + GT_N - 1) / GT_N * n_rb;
+        n_tiles += (p.seg_off[e + 1] - p.seg_mid[e] + GT_N - 1) / GT_N * n_rb;
     }
-    uint32_t phase = 0;
+    uint32_t mma_phase = 0;
+    int mma_pending = 0;                             // commits not yet waited for
+    uint32_t raw_phase[RAW_NS];
+#pragma unroll
+    for (int i = 0; i < RAW_NS; ++i) raw_phase[i] = 0;
     bool failed = false;
+    auto wait_mma = [&]() {
+        if (mma_pending) {
+            failed = __syncthreads_or(mbar_wait(&mma_bar, mma_phase, p.err) ? 0 : 1) != 0 || failed;
+            mma_phase ^= 1u;
+            mma_pending = 0;
+        }
+    };
+
     for (int t = blockIdx.x; t < n_tiles && !failed; t += gridDim.x) {
-        // locate (expert, token block, row block) of tile t
         int a = e_lo, base = 0, e = 0, ne = 0;
         for (; a < e_hi; ++a) {
             e = p.active[a];
-            ne = p.seg_off[e + 1] - p.seg_off[e];
+            ne = p.seg_off[e + 1] - p.seg_mid[e];
             const int nt = (ne + GT_N - 1) / GT_N * n_rb;
             if (t < base + nt) break;
             base += nt;
         }
         const int tb = (t - base) / n_rb, rb = (t - base) % n_rb;
-        const int tok0 = p.seg_off[e] + tb * GT_N;
+        const int tok0 = p.seg_mid[e] + tb * GT_N;
         const int nv = min(GT_N, ne - tb * GT_N);
+        const int rt = rb * GT_WARPS_ROWS + warp;        // this warp's row tile
+        const bool rt_ok = rt < p.n_row_tiles;
 
-        for (int g = 0; g < n_groups; ++g) {
-            if (g > 0) {                                 // previous group's MMAs done with smem
-                failed = __syncthreads_or(mbar_wait(&mma_bar, phase, p.err) ? 0 : 1) != 0;
-                phase ^= 1u;
-                if (failed) break;
+        // raw stage s -> this warp's ring slot s % RAW_NS
+        auto issue_raw = [&](int s) {
+            if (lane == 0 && rt_ok) {
+                const int g = s / NMAT, m = s % NMAT, c0 = g * CPG, nc = min(CPG, p.chunks - c0);
+                uint64_t* bar = &raw_bar[warp][s % ns];
+                const uint8_t* src = (m == 0 ? p.w0 : p.w1) + (size_t)e * p.expert_stride +
+                                     ((size_t)rt * p.chunks + c0) * p.tile_bytes;
+                mbar_expect_tx(bar, (uint32_t)(nc * p.tile_bytes));
+                bulk_g2s(myraw + (size_t)(s % ns) * stage_bytes, src, (uint32_t)(nc * p.tile_bytes), bar);
             }
-            const int c0 = g * CPG, nc = min(CPG, p.chunks - c0);
-            // A: warp w decodes row tiles 2w, 2w+1 of the block (both matrices)
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                uint8_t* A = smem + m * A_BYTES;
-                const uint8_t* wbase = (m == 0 ? p.w0 : p.w1) + (size_t)e * p.expert_stride;
-                for (int j = 2 * warp; j < 2 * warp + 2; ++j) {
-                    const int rt = rb * (GT_M / 16) + j;
-                    for (int cc = 0; cc < CPG; ++cc) {
-                        if (rt < p.n_row_tiles && cc < nc) {
-                            const uint8_t* T = wbase + ((size_t)rt * p.chunks + c0 + cc) * p.tile_bytes;
-                            D dec;
-                            dec.prep(T, lane);
-                            DqLoop<D, 0, KS>::run(dec, T, lane, A, 16 * j, cc * KC);
-                        } else {
-                            // rows past the matrix or k past K: zeros
-                            const int r = lane >> 2, q = lane & 3;
-                            for (int s = 0; s < KS; ++s) {
-                                const int k = cc * KC + q * (KC / 4) + 4 * s;
-                                for (int h = 0; h < 2; ++h) {
-                                    const int row = 16 * j + r + 8 * h;
-                                    *reinterpret_cast<uint2*>(A + (k >> 3) * A_LBO + (row >> 3) * 128 + (row & 7) * 16 +
-                                                              (k & 7) * 2) = make_uint2(0u, 0u);
-                                }
-                            }
+        };
+        // B group g -> buffer g & 1 (token rows, 16 bytes per (token, 8-wide k chunk))
+        auto issue_b = [&](int g) {
+            uint8_t* Bs = Bb + (g & 1) * B_BYTES;
+            const int kg = g * CPG * KC, klim = min(GT_K, p.K - kg);
+            for (int i = tid; i < GT_N * (GT_K / 8); i += blockDim.x) {
+                const int n = i % GT_N, kc = i / GT_N;
+                const bool ok = n < nv && kc * 8 < klim;
+                int row = tok0 + (ok ? n : 0);
+                if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
+                cp_async16(Bs + kc * B_LBO + (n >> 3) * 128 + (n & 7) * 16,
+                           p.X + (size_t)row * p.ldx + kg + (ok ? kc * 8 : 0), ok);
+            }
+            cp_async_commit();
+        };
+
+        for (int s = 0; s < ns && s < n_st; ++s) issue_raw(s);
+        issue_b(0);
+        for (int s = 0; s < n_st && !failed; ++s) {
+            const int g = s / NMAT, m = s % NMAT, c0 = g * CPG, nc = min(CPG, p.chunks - c0);
+            // raw weights of this stage have landed (warp-local); the A buffer (and at a new
+            // group, the other B buffer) is free once the previous stage's MMAs completed.
+            // One block-wide vote per stage keeps every thread on the same path.
+            const int slot = s % ns;
+            bool f = false;
+            if (rt_ok) {
+                f = !mbar_wait(&raw_bar[warp][slot], raw_phase[slot], p.err);
+                raw_phase[slot] ^= 1u;
+            }
+            if (mma_pending) {
+                f = !mbar_wait(&mma_bar, mma_phase, p.err) || f;
+                mma_phase ^= 1u;
+                mma_pending = 0;
+            }
+            failed = __syncthreads_or(f ? 1 : 0) != 0;
+            if (failed) break;
+            if (m == 0 && g + 1 < n_groups) issue_b(g + 1);
+            // dequantise this warp's row tile into A
+            const uint8_t* T0 = myraw + (size_t)slot * stage_bytes;
+            for (int cc = 0; cc < CPG; ++cc) {
+                if (rt_ok && cc < nc) {
+                    const uint8_t* T = T0 + cc * p.tile_bytes;
+                    D dec;
+                    dec.prep(T, lane);
+                    DqLoop<D, 0, KS>::run(dec, T, lane, A, 16 * warp, cc * KC);
+                } else {
+                    const int r = lane >> 2, q = lane & 3;
+                    for (int s2 = 0; s2 < KS; ++s2) {
+                        const int k = cc * KC + q * (KC / 4) + 4 * s2;
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = 16 * warp + r + 8 * h;
+                            *reinterpret_cast<uint2*>(A + (k >> 3) * A_LBO + (row >> 3) * 128 + (row & 7) * 16 +
+                                                      (k & 7) * 2) = make_uint2(0u, 0u);
                         }
                     }
                 }
             }
-            // B: the tile's token rows, 16 bytes per (token, 8-wide k chunk)
-            const int kg = c0 * KC;
-            for (int i = tid; i < GT_N * (GT_K / 8); i += blockDim.x) {
-                const int n = i % GT_N, kc = i / GT_N;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (n < nv && kc * 8 < nc * KC) {
-                    int row = tok0 + n;
-                    if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
-                    v = *reinterpret_cast<const uint4*>(p.X + (size_t)row * p.ldx + kg + kc * 8);
-                }
-                *reinterpret_cast<uint4*>(Bs + kc * B_LBO + (n >> 3) * 128 + (n & 7) * 16) = v;
-            }
-            fence_proxy_async();                         // generic-proxy writes -> tensor core reads
+            __syncwarp();
+            if (s + ns < n_st) { fence_proxy_async(); issue_raw(s + ns); }
+            // activation rows of group g complete (the newest group may still be in flight)
+            if (m == 0) { if (g + 1 < n_groups) cp_async_wait_1(); else cp_async_wait_0(); }
+            fence_proxy_async();                     // generic-proxy writes -> tensor core reads
             tc_fence_before();
             __syncthreads();
             if (tid == 0) {
                 tc_fence_after();
+                const uint8_t* Bs = Bb + (g & 1) * B_BYTES;
                 const int kblocks = nc * KC / 16;
                 for (int kb = 0; kb < kblocks; ++kb) {
-#pragma unroll
-                    for (int m = 0; m < NMAT; ++m) {
-                        const uint64_t da = umma_desc(smem_u32(smem + m * A_BYTES) + 2 * kb * A_LBO, A_LBO);
-                        const uint64_t db = umma_desc(smem_u32(Bs) + 2 * kb * B_LBO, B_LBO);
-                        umma_f16(tm + m * GT_N, da, db, (g > 0 || kb > 0) ? 1u : 0u);
-                    }
+                    const uint64_t da = umma_desc(smem_u32(A) + 2 * kb * A_LBO, A_LBO);
+                    const uint64_t db = umma_desc(smem_u32(Bs) + 2 * kb * B_LBO, B_LBO);
+                    umma_f16(tm + m * GT_N, da, db, (g > 0 || kb > 0) ? 1u : 0u);
                 }
                 umma_commit(&mma_bar);
             }
-            __syncwarp();
+            mma_pending = 1;
         }
-        if (!failed) {
-            failed = __syncthreads_or(mbar_wait(&mma_bar, phase, p.err) ? 0 : 1) != 0;
-            phase ^= 1u;
-        }
+        wait_mma();
+        cp_async_wait_0();
         tc_fence_after();
         if (!failed) {
-            // epilogue: warp w owns TMEM lanes (rows) 32w..32w+31, 16 token columns at a time
-            const int row = rb * GT_M + 32 * warp + lane;
-            const uint32_t lane_addr = tm + ((uint32_t)(32 * warp) << 16);
+            // epilogue: warp w reads TMEM lanes 32 (w % 4).., token columns 32 (w / 4) ..
+            const int row = rb * GT_M + 32 * (warp & 3) + lane;
+            const uint32_t lane_addr = tm + ((uint32_t)(32 * (warp & 3)) << 16);
 #pragma unroll 1
-            for (int c = 0; c < GT_N; c += 16) {
+            for (int c = 32 * (warp >> 2); c < 32 * (warp >> 2) + 32; c += 16) {
                 float v0[16], v1[16];
                 tmem_ld16(lane_addr + c, v0);
                 if constexpr (NMAT == 2) tmem_ld16(lane_addr + GT_N + c, v1);
@@ -236,8 +295,13 @@ __global__ void __launch_bounds__(128, 1) moe_gemm_kernel(const GemvParams p) {
         __syncthreads();                                 // accumulators read before the next tile
         tc_fence_after();
     }
-    // after a failed wait, give the issued MMAs time to retire before TMEM is released
-    if (failed) (void)mbar_wait(&mma_bar, phase, nullptr);
+    // after a failure: copies and MMAs still in flight finish (bounded) before release
+    if (failed) {
+        if (lane == 0)
+            for (int i = 0; i < ns; ++i) (void)mbar_wait(&raw_bar[warp][i], raw_phase[i], nullptr, 1u << 12);
+        (void)mbar_wait(&mma_bar, mma_phase, nullptr, 1u << 12);
+        cp_async_wait_0();
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
@@ -248,9 +312,15 @@ template <int WT, int KSF>
 void gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
     void (*k)(const GemvParams) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
                                                       : moe_gemm_kernel<WT, KSF, GM_DOWN>;
-    const int smem = (p.mode == GM_GATEUP ? 2 : 1) * A_BYTES + B_BYTES;
+    constexpr int CPG = GT_K / DecSel<WT, KSF>::T::KC;
+    // deepest raw ring (up to RAW_NS stages) that fits next to A and the two B buffers
+    const int per_stage = GM_WARPS * CPG * p.tile_bytes;
+    const int budget = 227 * 1024 - 1024 - A_BYTES - 2 * B_BYTES;
+    GemvParams q = p;
+    q.n_stages = std::max(1, std::min(RAW_NS, budget / per_stage));
+    const int smem = A_BYTES + 2 * B_BYTES + q.n_stages * per_stage;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    launch_pdl(k, dim3(grid), dim3(128), (size_t)smem, s, p);
+    launch_pdl(k, dim3(grid), dim3(32 * GM_WARPS), (size_t)smem, s, q);
 }
 
 }  // namespace

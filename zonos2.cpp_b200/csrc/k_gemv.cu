@@ -88,7 +88,7 @@ __device__ __forceinline__ ItemRef item_ref(const GemvParams& p, ItemPos q, int 
         r.src[0] = p.w0 + off;
         r.src[1] = (MODE == GM_GATEUP) ? p.w1 + off : nullptr;
         r.tok0 = p.seg_off[r.expert];
-        r.n_tok = p.seg_off[r.expert + 1] - r.tok0;
+        r.n_tok = (p.seg_mid ? p.seg_mid[r.expert] : p.seg_off[r.expert + 1]) - r.tok0;
     }
     return r;
 }

@@ -52,60 +52,87 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
     }
 }
 
-// Expert segments from the selected ids: routes sorted by expert, then token, then rank
-// in the token's top-k. Called by one whole block; cnt is a [MAX_EXPERTS] shared array.
-// tile_off (optional): [n_active + 1] prefix over active experts of ceil(routes / 8), the
-// 8-token column tiles each expert's GEMV items cover.
-// n_small (optional): experts with fewer than GEMM_MIN_TOKENS routes are listed first in
-// active[0, n_small) (the tile GEMV's list); the rest follow (the tensor-core GEMM's list).
+// Expert segments from the selected ids. Called by one whole block; cnt is a
+// [MAX_EXPERTS] shared array. Routes are grouped by expert; within an expert, the routes
+// for the tile GEMV come first (from seg_off[e]) and the routes for the tensor-core GEMM
+// follow (from seg_mid[e]), each part ordered by token, then rank in the token's top-k.
+// Which part a route joins depends on bulk_mode:
+//   0: none take the GEMM;
+//   1: all routes of an expert with >= GEMM_MIN_TOKENS routes (the isolated expert op);
+//   2: the routes of prompt rows, i.e. tokens whose descriptor feeds more than one row
+//      (the decode step). A token's path then depends on the token alone, so packing
+//      other streams into the step never changes its result.
+// active[0, n_small) lists the experts with GEMV routes, active[n_small, n_active) those
+// with GEMM routes (an expert can be in both). tile_off (optional): prefix over the GEMV
+// list of ceil(routes / 8).
 __device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
-                               int* seg_off, int* active, int* n_active, int* route_tok, float* route_w,
-                               int* route_pos, int* tile_off, int* n_small) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+                               int* seg_off, int* seg_mid, int* active, int* n_active, int* route_tok,
+                               float* route_w, int* route_pos, int* tile_off, int* n_small, int bulk_mode,
+                               const int* tok_desc, const SlotDesc* descs) {
+    __shared__ int cntb[MAX_EXPERTS];
+    auto tok_bulk = [&](int t) -> bool {
+        return bulk_mode == 2 && descs[tok_desc[t]].n_new > 1;
+    };
+    for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cntb[e] = 0; }
     __syncthreads();
     const int R = T * k;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         const int e = __ldcg(sel + (r / k) * kmax + r % k);
-        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+        if (e >= 0 && e < E) {
+            atomicAdd(&cnt[e], 1);
+            if (tok_bulk(r / k)) atomicAdd(&cntb[e], 1);
+        }
     }
+    __syncthreads();
+    if (bulk_mode == 1)
+        for (int e = threadIdx.x; e < E; e += blockDim.x) cntb[e] = cnt[e] >= GEMM_MIN_TOKENS ? cnt[e] : 0;
     __syncthreads();
     if (threadIdx.x == 0) {
         int off = 0, na = 0, tiles = 0;
         for (int e = 0; e < E; ++e) {
             seg_off[e] = off;
+            if (seg_mid) seg_mid[e] = off + cnt[e] - cntb[e];
             off += cnt[e];
         }
         seg_off[E] = off;
-        for (int big = 0; big < 2; ++big) {
-            for (int e = 0; e < E; ++e) {
-                if (cnt[e] == 0 || (n_small && (cnt[e] >= GEMM_MIN_TOKENS) != (big == 1))) continue;
-                if (tile_off) tile_off[na] = tiles;
-                tiles += (cnt[e] + 7) / 8;
-                active[na++] = e;
-            }
-            if (n_small && big == 0) *n_small = na;
-            if (!n_small) break;
+        for (int e = 0; e < E; ++e) {
+            const int nsm = cnt[e] - cntb[e];
+            if (nsm == 0) continue;
+            if (tile_off) tile_off[na] = tiles;
+            tiles += (nsm + 7) / 8;
+            active[na++] = e;
         }
         if (tile_off) tile_off[na] = tiles;
+        if (n_small) *n_small = na;
+        for (int e = 0; e < E; ++e)
+            if (cntb[e] > 0) active[na++] = e;
         *n_active = na;
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int e = w; e < E; e += nw) {
         if (cnt[e] == 0) continue;
-        int p = seg_off[e];
-        for (int base = 0; base < R; base += 32) {
-            const int r = base + lane;
-            const int se = r < R ? __ldcg(sel + (r / k) * kmax + r % k) : -1;
-            const unsigned m = __ballot_sync(0xffffffffu, se == e);
-            if (se == e) {
-                const int pos = p + __popc(m & ((1u << lane) - 1u));
-                const int tt = r / k, jj = r % k;
-                route_tok[pos] = tt;
-                route_w[pos] = __ldcg(selw + tt * kmax + jj);
-                route_pos[tt * kmax + jj] = pos;
+        for (int part = 0; part < 2; ++part) {
+            // part 0: GEMV routes from seg_off[e]; part 1: GEMM routes from the middle
+            int p = part == 0 ? seg_off[e] : seg_off[e] + cnt[e] - cntb[e];
+            if (part == 1 && cntb[e] == 0) break;
+            for (int base = 0; base < R; base += 32) {
+                const int r = base + lane;
+                int se = r < R ? __ldcg(sel + (r / k) * kmax + r % k) : -1;
+                if (se == e && bulk_mode != 0) {
+                    const bool b = bulk_mode == 1 ? cntb[e] > 0 : tok_bulk(r / k);
+                    if (b != (part == 1)) se = -1;
+                }
+                const unsigned m = __ballot_sync(0xffffffffu, se == e);
+                if (se == e) {
+                    const int pos = p + __popc(m & ((1u << lane) - 1u));
+                    const int tt = r / k, jj = r % k;
+                    route_tok[pos] = tt;
+                    route_w[pos] = __ldcg(selw + tt * kmax + jj);
+                    route_pos[tt * kmax + jj] = pos;
+                }
+                p += __popc(m);
             }
-            p += __popc(m);
         }
     }
     __syncthreads();
@@ -323,28 +350,29 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.active, b.n_active, b.route_tok, b.route_w,
-                   b.route_pos, b.tile_off, b.n_small);
+    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.seg_mid, b.active, b.n_active, b.route_tok,
+                   b.route_w, b.route_pos, b.tile_off, b.n_small, ly.gemm_ok ? 2 : 0, b.tok_desc, b.descs);
     if (threadIdx.x == 0) {
         if (b.layer_active) b.layer_active[layer] = *b.n_active;
         *b.ticket = 0;
     }
 }
 
-__global__ void segments_kernel(const StepBufs b, int T, int k, int E) {
+__global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_mode) {
     __shared__ int cnt[MAX_EXPERTS];
     pdl_wait();
     pdl_release();
     for (int j = threadIdx.x; j < T * b.kmax; j += blockDim.x) b.route_pos[j] = -1;
     __syncthreads();
-    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.active, b.n_active, b.route_tok, b.route_w,
-                   b.route_pos, b.tile_off, b.n_small);
+    build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.seg_mid, b.active, b.n_active, b.route_tok,
+                   b.route_w, b.route_pos, b.tile_off, b.n_small, bulk_mode, nullptr, nullptr);
 }
 
 __global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
                                   int* n_active, int* route_tok, float* route_w, int* route_pos) {
     __shared__ int cnt[MAX_EXPERTS];
-    build_segments(sel, selw, T, k, k, E, cnt, seg_off, active, n_active, route_tok, route_w, route_pos, nullptr, nullptr);
+    build_segments(sel, selw, T, k, k, E, cnt, seg_off, nullptr, active, n_active, route_tok, route_w, route_pos,
+                   nullptr, nullptr, 0, nullptr, nullptr);
 }
 
 }  // namespace
@@ -377,8 +405,8 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
 
 int router_launches(const LayerSmall& ly) { return ly.is_moe ? 2 : 1; }
 
-void launch_segments(const StepBufs& b, int T, int k, int E, cudaStream_t s) {
-    launch_pdl(segments_kernel, dim3(1), dim3(1024), 0, s, b, T, k, E);
+void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s) {
+    launch_pdl(segments_kernel, dim3(1), dim3(1024), 0, s, b, T, k, E, bulk_mode);
 }
 
 }  // namespace z2b

@@ -9,7 +9,8 @@
 namespace z2b {
 
 constexpr int MAX_EXPERTS = 256;
-constexpr int GEMM_MIN_TOKENS = 64;  // routes from which an expert takes the tensor-core GEMM
+constexpr int GEMM_MIN_TOKENS = 17;  // isolated expert op: routes from which an expert takes the
+                                     // tensor-core GEMM (the GEMV holds at most 16 tokens per pass)
 constexpr int NCOL = 10;            // input columns per row: 9 audio codebooks + text
 constexpr int PAGE = 256;           // KV page length (tokens)
 
@@ -47,6 +48,7 @@ struct GemvParams {
     const int* seg_off;             // device: [E+1] route offsets in expert order
     const int* tile_off;            // device: [n_active+1] prefix of 8-token tiles per active expert
     const int* n_small;             // device: GEMV experts active[0, n_small); GEMM experts after them
+    const int* seg_mid;             // device: [E] GEMV routes [seg_off, seg_mid), GEMM routes [seg_mid, seg_off+1)
     const int* route_tok;           // device: token of each route (expert order)
     const float* route_w;           // device: route probability (GM_DOWN)
     // activations
@@ -127,7 +129,8 @@ struct StepBufs {
     int* sel; float* selw; int kmax;// [T][kmax]
     int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
     int* tile_off;                  // [MAX_EXPERTS + 1] prefix of 8-token tiles over active experts
-    int* n_small;                   // experts in active[] with < GEMM_MIN_TOKENS routes (listed first)
+    int* n_small;                   // active[0, n_small): experts with GEMV routes; then GEMM experts
+    int* seg_mid;                   // [MAX_EXPERTS] first GEMM route of each expert
     int* ticket;
     __half* y;                      // [R][ff]
     float* out_route;               // [R][d]
@@ -147,6 +150,7 @@ struct LayerSmall {
     const int8_t* rdown_q;          // router down projection kept as Q8_0 quants [rd][d] (or null)
     const float* rdown_qd;          // its block scales [rd][d/32] (f32 copies of the f16 d)
     int is_moe, top_k, n_expert;
+    int gemm_ok;                    // gate/up and down both run on the tcgen05 GEMM (prompt routes)
 };
 
 // Embedding tables in GGUF block format (rows dequantised in the kernel).
@@ -163,7 +167,7 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
                    cudaStream_t s);
 int router_launches(const LayerSmall& ly);
 // Expert segments from given router ids b.sel/b.selw (one block; the router's own last step).
-void launch_segments(const StepBufs& b, int T, int k, int E, cudaStream_t s);
+void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s);
 // f32 rows -> f16 rows (n values).
 void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 // Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the

@@ -250,6 +250,10 @@ struct Loader {
                 if ((!s.rdown_w && !s.rdown_q) || !s.rdown_b || !s.m0_w || !s.m0_b || !s.m2_w || !s.m2_b || !s.m4_w || !s.rnorm || !s.rbias)
                     return false;
                 if (eda && !s.eda) return false;
+                // prompt-row routes run on the tcgen05 GEMM when every expert matrix type has
+                // its dequantiser there and the gate/up type matches
+                s.gemm_ok = moe_gemm_supported(ly.gate_exps) && moe_gemm_supported(ly.up_exps) &&
+                            moe_gemm_supported(ly.down_exps) && ly.gate_exps.type == ly.up_exps.type ? 1 : 0;
                 if (first) {
                     m->router_bytes_per_layer = rdw->nbytes + f.tensor(b + "router_mlp0.weight")->nbytes +
                                                 f.tensor(b + "router_mlp2.weight")->nbytes +

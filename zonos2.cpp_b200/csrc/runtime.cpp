@@ -123,6 +123,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     acc((size_t)T * nkv * 4);
     acc((MAX_EXPERTS + 1) * 4);
     acc(4);
+    acc(MAX_EXPERTS * 4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -153,6 +154,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     B.attn_ticket = carve<int>(p, (size_t)T * nkv);
     B.tile_off = carve<int>(p, MAX_EXPERTS + 1);
     B.n_small = carve<int>(p, 1);
+    B.seg_mid = carve<int>(p, MAX_EXPERTS);
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -258,9 +260,10 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
 }
 
 // Expert pass (gate/up + SwiGLU, or down x route weight) over the routes of the step:
-// the tile GEMV takes the experts with few routes; when the step has at least
-// GEMM_MIN_TOKENS tokens, experts with that many routes go to the tcgen05 GEMM.
-void gemv_moe(Ctx* c, const LayerDev& ly, int mode, int T) {
+// the tile GEMV takes each expert's routes [seg_off, seg_mid); when the step can have
+// routes for the tcgen05 GEMM (bulk: prompt rows, or a large expert-op batch) the GEMM
+// takes [seg_mid, seg_off + 1).
+void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
     ProfScope ps(c, mode == GM_GATEUP ? PC_GATEUP : PC_DOWN);
     const Dims& D = c->m->dims;
     GemvParams p{};
@@ -271,10 +274,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, int T) {
     p.w0 = w0.tiles;
     p.w1 = mode == GM_GATEUP ? ly.up_exps.tiles : nullptr;
     p.expert_stride = w0.expert_stride;
-    const bool split = T >= GEMM_MIN_TOKENS && moe_gemm_supported(w0);
-    p.n_active = split ? c->B.n_small : c->B.n_active;
+    const bool split = bulk && ly.small.gemm_ok;
+    p.n_active = c->B.n_small;
     p.n_small = c->B.n_small;
-    p.active = c->B.active; p.seg_off = c->B.seg_off; p.tile_off = c->B.tile_off;
+    p.active = c->B.active; p.seg_off = c->B.seg_off; p.seg_mid = c->B.seg_mid; p.tile_off = c->B.tile_off;
     p.route_tok = c->B.route_tok; p.route_w = c->B.route_w;
     if (mode == GM_GATEUP) {
         p.X = c->B.cur; p.ldx = D.n_embd; p.yout = c->B.y; p.ldy = D.n_ff; p.out_rows = D.n_ff;
@@ -298,7 +301,7 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, int T) {
 
 }  // namespace
 
-void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode, c->last_T); }
+void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode, false); }
 
 void enqueue_step(Ctx* c, int T, int n_out) {
     Model* m = c->m;
@@ -331,8 +334,9 @@ void enqueue_step(Ctx* c, int T, int n_out) {
         }
         { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches += router_launches(ly.small); }
         if (ly.is_moe) first_moe = false;
-        gemv_moe(c, ly, GM_GATEUP, T);
-        gemv_moe(c, ly, GM_DOWN, T);
+        const bool bulk = T > c->cur_n_desc;                 // the step carries prompt rows
+        gemv_moe(c, ly, GM_GATEUP, bulk);
+        gemv_moe(c, ly, GM_DOWN, bulk);
         const bool last = L == D.n_layer - 1;
         {
             ProfScope ps(c, PC_COMBINE);
@@ -743,11 +747,12 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
     CK(cudaMemcpyAsync(B.sel, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(B.selw, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice, c->stream));
     launch_to_f16(B.res, B.cur, (size_t)T * d, c->stream);
-    launch_segments(B, T, k, ly.n_expert, c->stream);
+    const bool bulk = T >= GEMM_MIN_TOKENS && ly.small.gemm_ok;
+    launch_segments(B, T, k, ly.n_expert, bulk ? 1 : 0, c->stream);
     const bool prof = c->profiling;
     c->profiling = false;
-    gemv_moe(c, ly, GM_GATEUP, T);
-    gemv_moe(c, ly, GM_DOWN, T);
+    gemv_moe(c, ly, GM_GATEUP, bulk);
+    gemv_moe(c, ly, GM_DOWN, bulk);
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaGetLastError());
     if (reps > 0 && ms) {
@@ -756,8 +761,8 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
         CK(cudaEventCreate(&e1));
         CK(cudaEventRecord(e0, c->stream));
         for (int r = 0; r < reps; ++r) {
-            gemv_moe(c, ly, GM_GATEUP, T);
-            gemv_moe(c, ly, GM_DOWN, T);
+            gemv_moe(c, ly, GM_GATEUP, bulk);
+            gemv_moe(c, ly, GM_DOWN, bulk);
         }
         CK(cudaEventRecord(e1, c->stream));
         CK(cudaEventSynchronize(e1));
@@ -776,7 +781,7 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
     if (err) { set_error("expert_op: device error word " + std::to_string(err)); return Z2B_ERR_DEVICE; }
     const auto bytes = [](const DevMat& w) { return (uint64_t)w.n_row_tiles * w.chunks * w.tile_bytes; };
     if (weight_bytes) *weight_bytes = (uint64_t)na * (bytes(ly.gate_exps) + bytes(ly.up_exps) + bytes(ly.down_exps));
-    if (n_gemm) *n_gemm = (T >= GEMM_MIN_TOKENS) ? na - ns : 0;
+    if (n_gemm) *n_gemm = bulk ? na - ns : 0;
     if (out) {
         const int R = T * k;
         std::vector<float> orr((size_t)R * d);
