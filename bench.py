@@ -284,7 +284,8 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
 
     z2b = load_pkg()
     import z2b.runtime as R

@@ -92,16 +92,17 @@ __global__ void rope_append_kernel(const StepBufs b, const KVDev kv, const float
 template <int HD>
 struct AttnSmem {
     static constexpr int CHUNK_BYTES = KCH * HD * 2;          // one K or V slice
-    static constexpr int NS = HD >= 128 ? 3 : 4;
+    static constexpr int NS = HD >= 128 ? 2 : 4;
     static constexpr int STAGE = 2 * CHUNK_BYTES;
     static constexpr int MERGE = 4 * 8 * (HD + 2) * 4;        // [warp][head][m, l, o], over the stages
     static_assert(MERGE <= NS * STAGE, "the merge area reuses the drained stages");
-    // two blocks per SM for HD = 128 (2 x 96 KB)
+    // three blocks per SM for HD = 128 (3 x 64 KB): every split block of a 16-stream
+    // decode step is resident at once
     static constexpr int BYTES = 128 + NS * STAGE;
 };
 
 template <int HD, int G>
-__global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev kv, const Dims dm,
+__global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KVDev kv, const Dims dm,
                                                    int layer, int split_keys) {
     using SM = AttnSmem<HD>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -109,31 +110,38 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
     uint8_t* stages = smem + 128;
     float* merge = reinterpret_cast<float*>(stages);          // used once every copy has landed
     // The token's slot, position and descriptor were written by the step's packer and the
-    // cached keys below the slot's first new key by earlier steps: every kernel before
-    // the immediate predecessor has completed once this grid runs (each kernel waits on
-    // its own predecessor before it releases its dependent), so those chunks are copied
-    // before the wait. Q and the keys appended by this step come after it.
+    // cached keys below the slot's first new key by earlier steps: with programmatic
+    // dependent launch, every kernel before the immediate predecessor has completed once
+    // this grid runs (each kernel waits on its own predecessor before it releases its
+    // dependent), so those chunks are copied before the wait. Q and the keys appended by
+    // this step come after it. The token's slot and position load together.
     const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
-    const int slot = b.tok_slot[t];
+    const int slot = b.tok_slot[t], pos = b.tok_pos[t];
     if (slot < 0) return;
-    const int pos = b.tok_pos[t], n_keys = pos + 1;
+    const int n_keys = pos + 1;
     const int key0 = sp * split_keys;
     if (key0 >= n_keys) return;
     const int key1 = min(n_keys, key0 + split_keys);
-    const int fresh = b.descs[b.tok_desc[t]].n_past;          // first key written by this step
     const int nchunks = (key1 - key0 + KCH - 1) / KCH;
+    // the first chunk's page, loaded while the barriers are set up
+    const int pg0 = key0 / PAGE;
+    const int page0 = threadIdx.x == 0 && pg0 < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg0] : -1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = lane >> 2, q = lane & 3;
     const int nh = dm.n_head;
     constexpr int KST = HD / 16;                 // k-steps over head_dim, also m-tiles of O^T
     constexpr int QO = HD / 4;                   // dims owned by a lane quad
 
-    // page pointers for every chunk are looked up by the issuing thread
+    // page pointers are looked up by the issuing thread, once per page
+    int cpg = pg0, cpage = page0;
     auto chunk_src = [&](int c, const __half** kp, const __half** vp) -> bool {
         const int key = key0 + c * KCH, pg = key / PAGE;
-        const int page = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
-        if (page < 0) return false;
-        const __half* lb = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
+        if (pg != cpg) {
+            cpg = pg;
+            cpage = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
+        }
+        if (cpage < 0) return false;
+        const __half* lb = kv.pool + (size_t)cpage * kv.page_elems + (size_t)layer * kv.layer_elems;
         *kp = lb + (size_t)hk * kv.head_elems + (size_t)(key % PAGE) * HD;
         *vp = lb + (size_t)(dm.n_head_kv + hk) * kv.head_elems + (size_t)((key % PAGE) / KCH) * HD * KCH;
         return true;
@@ -159,8 +167,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
         bulk_g2s(st + SM::CHUNK_BYTES, vp, SM::CHUNK_BYTES, &bars[c % SM::NS]);
     };
     int pre = 0;                                 // chunks issued before the wait
-    if (threadIdx.x == 0)
-        for (; pre < SM::NS && pre < nchunks && min(key0 + (pre + 1) * KCH, key1) <= fresh; ++pre) issue(pre);
+    if constexpr (kUsePdl) {
+        const int fresh = b.descs[b.tok_desc[t]].n_past;      // first key written by this step
+        if (threadIdx.x == 0)
+            for (; pre < SM::NS && pre < nchunks && min(key0 + (pre + 1) * KCH, key1) <= fresh; ++pre) issue(pre);
+    }
     pdl_wait();
     pdl_release();
     if (threadIdx.x == 0)
@@ -193,7 +204,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
         const int kb = 16 * warp;                 // this warp's keys within the chunk
         const int kglob = key0 + c * KCH + kb;
         if (!failed && !s_bad && kglob < key1) {
-            float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0};
+            // four independent accumulator chains (two key tiles x even/odd k-steps)
+            float s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0}, s0o[4] = {0, 0, 0, 0}, s1o[4] = {0, 0, 0, 0};
             const int n = r;                      // B column of this lane
             const int key_a = kb + 4 * (n >> 1) + (n & 1), key_b = key_a + 2;
 #pragma unroll
@@ -201,9 +213,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const StepBufs b, const KVDev
                 const int e = QO * q + 4 * s, ch = e / 8, off = (e % 8) * 2;
                 const uint2 ka = *(const uint2*)(Ks + key_a * HD * 2 + ((ch ^ kswz<HD>(key_a)) * 16) + off);
                 const uint2 kbv = *(const uint2*)(Ks + key_b * HD * 2 + ((ch ^ kswz<HD>(key_b)) * 16) + off);
-                mma16816(s0, qa[s][0], 0u, qa[s][1], 0u, ka.x, ka.y);
-                mma16816(s1, qa[s][0], 0u, qa[s][1], 0u, kbv.x, kbv.y);
+                mma16816((s & 1) ? s0o : s0, qa[s][0], 0u, qa[s][1], 0u, ka.x, ka.y);
+                mma16816((s & 1) ? s1o : s1, qa[s][0], 0u, qa[s][1], 0u, kbv.x, kbv.y);
             }
+            s0[0] += s0o[0]; s0[1] += s0o[1]; s1[0] += s1o[0]; s1[1] += s1o[1];
             // lane holds head r, keys kb + 4q + {0, 1} (s0[0..1]) and {2, 3} (s1[0..1])
             float sv[4] = {s0[0] * scale, s0[1] * scale, s1[0] * scale, s1[1] * scale};
 #pragma unroll

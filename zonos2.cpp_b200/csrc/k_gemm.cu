@@ -69,41 +69,41 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Decode k-steps s..KS-1 of one 16-row tile chunk into the A block (rows row0.., k
-// offset kofs within the group): lane (r, q) holds rows r, r+8 at k = q*KC/4 + 4s.
+// Decode k-steps s..KS-1 of one 16-row tile chunk into the A block: lane (r, q) holds
+// rows r and r + 8 at k = kq + 4s with kq = kofs + q * KC / 4 a multiple of 8, so each
+// store lands at a compile-time offset from the lane's two base pointers:
+// (s / 2) * A_LBO + (s % 2) * 8 bytes.
 template <class D, int s, int KS> struct DqLoop {
-    __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, uint8_t* A, int row0, int kofs) {
+    __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, uint8_t* b0, uint8_t* b1) {
         uint32_t a[4];
         dec.template frag<s>(T, lane, a);
-        const int r = lane >> 2, q = lane & 3;
-        const int k = kofs + q * (D::KC / 4) + 4 * s;
-        uint8_t* p0 = A + (k >> 3) * A_LBO + ((row0 + r) >> 3) * 128 + ((row0 + r) & 7) * 16 + (k & 7) * 2;
-        uint8_t* p1 = A + (k >> 3) * A_LBO + ((row0 + r + 8) >> 3) * 128 + ((row0 + r + 8) & 7) * 16 + (k & 7) * 2;
-        *reinterpret_cast<uint2*>(p0) = make_uint2(a[0], a[2]);
-        *reinterpret_cast<uint2*>(p1) = make_uint2(a[1], a[3]);
-        DqLoop<D, s + 1, KS>::run(dec, T, lane, A, row0, kofs);
+        *reinterpret_cast<uint2*>(b0 + (s >> 1) * A_LBO + (s & 1) * 8) = make_uint2(a[0], a[2]);
+        *reinterpret_cast<uint2*>(b1 + (s >> 1) * A_LBO + (s & 1) * 8) = make_uint2(a[1], a[3]);
+        DqLoop<D, s + 1, KS>::run(dec, T, lane, b0, b1);
     }
 };
 template <class D, int KS> struct DqLoop<D, KS, KS> {
-    __device__ __forceinline__ static void run(const D&, const uint8_t*, int, uint8_t*, int, int) {}
+    __device__ __forceinline__ static void run(const D&, const uint8_t*, int, uint8_t*, uint8_t*) {}
 };
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
-                 :: "r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0) : "memory");
+// The lane's two base pointers into A for a chunk at k offset kofs (rows row0 + r, + 8).
+template <int KC>
+__device__ __forceinline__ void dq_bases(uint8_t* A, int lane, int row0, int kofs, uint8_t** b0, uint8_t** b1) {
+    const int r = lane >> 2, q = lane & 3;
+    const int kq8 = (kofs + q * (KC / 4)) >> 3;
+    *b0 = A + kq8 * A_LBO + ((row0 + r) >> 3) * 128 + ((row0 + r) & 7) * 16;
+    *b1 = A + kq8 * A_LBO + ((row0 + r + 8) >> 3) * 128 + ((row0 + r + 8) & 7) * 16;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 constexpr int GM_WARPS = 8;                      // one 16-row weight tile per warp
 constexpr int RAW_NS = 3;                        // raw weight stages per warp (K groups ahead)
 
 // Per tile: the (K group g, matrix m) stages stream in order s = g * NMAT + m. Each warp
-// bulk-copies its own 16-row tile's chunks of stage s into a ring RAW_NS stages ahead;
-// the activation rows of group g are gathered with cp.async into one of two B buffers a
-// group ahead; the single A buffer is rewritten once the MMAs of the previous stage have
-// released it (tcgen05.commit -> mma_bar), then one thread issues the stage's MMAs.
+// bulk-copies its own 16-row tile's chunks of stage s into a ring up to RAW_NS stages
+// ahead; the activation rows of group g are gathered with cp.async into one of two B
+// buffers a group ahead; the single A buffer is rewritten once the MMAs of the previous
+// stage have released it (tcgen05.commit -> mma_bar), then one thread issues the stage's
+// MMAs.
 template <int WT, int KSF, int MODE>
 __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
     using D = typename DecSel<WT, KSF>::T;
@@ -190,16 +190,21 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
             }
         };
         // B group g -> buffer g & 1 (token rows, 16 bytes per (token, 8-wide k chunk))
+        // this thread's token column of B (fixed for the tile) and its first 8-wide k chunk
+        constexpr int B_TPK = 32 * GM_WARPS / GT_N;     // threads per token (k chunks step by this)
+        const int bn = tid % GT_N, bkc0 = tid / GT_N;
+        const bool bn_ok = bn < nv;
+        int brow = tok0 + (bn_ok ? bn : 0);
+        if constexpr (MODE == GM_GATEUP) brow = p.route_tok[brow];
+        const __half* bsrc = p.X + (size_t)brow * p.ldx;
         auto issue_b = [&](int g) {
-            uint8_t* Bs = Bb + (g & 1) * B_BYTES;
+            uint8_t* bdst = Bb + (g & 1) * B_BYTES + (bn >> 3) * 128 + (bn & 7) * 16;
             const int kg = g * CPG * KC, klim = min(GT_K, p.K - kg);
-            for (int i = tid; i < GT_N * (GT_K / 8); i += blockDim.x) {
-                const int n = i % GT_N, kc = i / GT_N;
-                const bool ok = n < nv && kc * 8 < klim;
-                int row = tok0 + (ok ? n : 0);
-                if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
-                cp_async16(Bs + kc * B_LBO + (n >> 3) * 128 + (n & 7) * 16,
-                           p.X + (size_t)row * p.ldx + kg + (ok ? kc * 8 : 0), ok);
+#pragma unroll
+            for (int j = 0; j < GT_K / 8 / B_TPK; ++j) {
+                const int kc = bkc0 + j * B_TPK;
+                const bool ok = bn_ok && kc * 8 < klim;
+                cp_async16(bdst + kc * B_LBO, bsrc + kg + (ok ? kc * 8 : 0), ok);
             }
             cp_async_commit();
         };
@@ -227,21 +232,21 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
             if (m == 0 && g + 1 < n_groups) issue_b(g + 1);
             // dequantise this warp's row tile into A
             const uint8_t* T0 = myraw + (size_t)slot * stage_bytes;
+#pragma unroll
             for (int cc = 0; cc < CPG; ++cc) {
+                uint8_t *b0, *b1;
+                dq_bases<KC>(A, lane, 16 * warp, cc * KC, &b0, &b1);
                 if (rt_ok && cc < nc) {
                     const uint8_t* T = T0 + cc * p.tile_bytes;
                     D dec;
                     dec.prep(T, lane);
-                    DqLoop<D, 0, KS>::run(dec, T, lane, A, 16 * warp, cc * KC);
+                    DqLoop<D, 0, KS>::run(dec, T, lane, b0, b1);
                 } else {
-                    const int r = lane >> 2, q = lane & 3;
+                    // rows past the matrix or k past K: zeros
+#pragma unroll
                     for (int s2 = 0; s2 < KS; ++s2) {
-                        const int k = cc * KC + q * (KC / 4) + 4 * s2;
-                        for (int h = 0; h < 2; ++h) {
-                            const int row = 16 * warp + r + 8 * h;
-                            *reinterpret_cast<uint2*>(A + (k >> 3) * A_LBO + (row >> 3) * 128 + (row & 7) * 16 +
-                                                      (k & 7) * 2) = make_uint2(0u, 0u);
-                        }
+                        *reinterpret_cast<uint2*>(b0 + (s2 >> 1) * A_LBO + (s2 & 1) * 8) = make_uint2(0u, 0u);
+                        *reinterpret_cast<uint2*>(b1 + (s2 >> 1) * A_LBO + (s2 & 1) * 8) = make_uint2(0u, 0u);
                     }
                 }
             }

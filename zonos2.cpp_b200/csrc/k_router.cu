@@ -65,62 +65,111 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 // active[0, n_small) lists the experts with GEMV routes, active[n_small, n_active) those
 // with GEMM routes (an expert can be in both). tile_off (optional): prefix over the GEMV
 // list of ceil(routes / 8).
+// Up to SEG_STAGE routes are read from global memory once, in one pass, and placed from
+// shared memory; larger steps read them per expert.
+constexpr int SEG_STAGE = 2048;
 __device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
                                int* seg_off, int* seg_mid, int* active, int* n_active, int* route_tok,
                                float* route_w, int* route_pos, int* tile_off, int* n_small, int bulk_mode,
                                const int* tok_desc, const SlotDesc* descs) {
     __shared__ int cntb[MAX_EXPERTS];
+    __shared__ int s_off[MAX_EXPERTS];
+    __shared__ int s_se[SEG_STAGE];              // expert | GEMM-part flag << 16, or -1
+    __shared__ float s_sw[SEG_STAGE];
     auto tok_bulk = [&](int t) -> bool {
         return bulk_mode == 2 && descs[tok_desc[t]].n_new > 1;
     };
+    const int R = T * k;
+    const bool staged = R <= SEG_STAGE;
     for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cntb[e] = 0; }
     __syncthreads();
-    const int R = T * k;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        const int e = __ldcg(sel + (r / k) * kmax + r % k);
+        const int t = r / k, j = r % k;
+        int e = __ldcg(sel + t * kmax + j);
+        const float w = staged ? __ldcg(selw + t * kmax + j) : 0.0f;
+        const bool bk = tok_bulk(t);
         if (e >= 0 && e < E) {
             atomicAdd(&cnt[e], 1);
-            if (tok_bulk(r / k)) atomicAdd(&cntb[e], 1);
+            if (bk) atomicAdd(&cntb[e], 1);
+        } else {
+            e = -1;
         }
+        if (staged) { s_se[r] = e < 0 ? -1 : (e | (bk ? 1 << 16 : 0)); s_sw[r] = w; }
     }
     __syncthreads();
     if (bulk_mode == 1)
         for (int e = threadIdx.x; e < E; e += blockDim.x) cntb[e] = cnt[e] >= GEMM_MIN_TOKENS ? cnt[e] : 0;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int off = 0, na = 0, tiles = 0;
-        for (int e = 0; e < E; ++e) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (w == 0) {
+        // lane owns experts [PER lane, PER lane + PER): exclusive scans over lanes of the
+        // routes, GEMV experts, GEMV tiles and GEMM experts
+        constexpr int PER = MAX_EXPERTS / 32;
+        int c[PER], cb[PER];
+        int off = 0, na = 0, tiles = 0, nb = 0;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int e = PER * lane + i;
+            c[i] = e < E ? cnt[e] : 0;
+            cb[i] = e < E ? cntb[e] : 0;
+            off += c[i];
+            na += c[i] - cb[i] > 0;
+            tiles += (c[i] - cb[i] + 7) / 8;
+            nb += cb[i] > 0;
+        }
+        int x_off = off, x_na = na, x_tiles = tiles, x_nb = nb;   // inclusive scans
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a0 = __shfl_up_sync(0xffffffffu, x_off, o), a1 = __shfl_up_sync(0xffffffffu, x_na, o);
+            const int a2 = __shfl_up_sync(0xffffffffu, x_tiles, o), a3 = __shfl_up_sync(0xffffffffu, x_nb, o);
+            if (lane >= o) { x_off += a0; x_na += a1; x_tiles += a2; x_nb += a3; }
+        }
+        const int tot_off = __shfl_sync(0xffffffffu, x_off, 31), tot_na = __shfl_sync(0xffffffffu, x_na, 31);
+        const int tot_tiles = __shfl_sync(0xffffffffu, x_tiles, 31);
+        off = x_off - off; na = x_na - na; tiles = x_tiles - tiles; nb = tot_na + x_nb - nb;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int e = PER * lane + i;
+            if (e >= E) break;
             seg_off[e] = off;
-            if (seg_mid) seg_mid[e] = off + cnt[e] - cntb[e];
-            off += cnt[e];
+            s_off[e] = off;
+            if (seg_mid) seg_mid[e] = off + c[i] - cb[i];
+            off += c[i];
+            if (c[i] - cb[i] > 0) {
+                if (tile_off) tile_off[na] = tiles;
+                tiles += (c[i] - cb[i] + 7) / 8;
+                active[na++] = e;
+            }
+            if (cb[i] > 0) active[nb++] = e;
         }
-        seg_off[E] = off;
-        for (int e = 0; e < E; ++e) {
-            const int nsm = cnt[e] - cntb[e];
-            if (nsm == 0) continue;
-            if (tile_off) tile_off[na] = tiles;
-            tiles += (nsm + 7) / 8;
-            active[na++] = e;
+        if (lane == 31) {
+            seg_off[E] = tot_off;
+            if (tile_off) tile_off[tot_na] = tot_tiles;
+            if (n_small) *n_small = tot_na;
+            *n_active = nb;
         }
-        if (tile_off) tile_off[na] = tiles;
-        if (n_small) *n_small = na;
-        for (int e = 0; e < E; ++e)
-            if (cntb[e] > 0) active[na++] = e;
-        *n_active = na;
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int e = w; e < E; e += nw) {
         if (cnt[e] == 0) continue;
         for (int part = 0; part < 2; ++part) {
             // part 0: GEMV routes from seg_off[e]; part 1: GEMM routes from the middle
-            int p = part == 0 ? seg_off[e] : seg_off[e] + cnt[e] - cntb[e];
+            int p = part == 0 ? s_off[e] : s_off[e] + cnt[e] - cntb[e];
             if (part == 1 && cntb[e] == 0) break;
             for (int base = 0; base < R; base += 32) {
                 const int r = base + lane;
-                int se = r < R ? __ldcg(sel + (r / k) * kmax + r % k) : -1;
+                int se;
+                bool bk;
+                if (staged) {
+                    const int v = r < R ? s_se[r] : -1;
+                    se = v < 0 ? -1 : (v & 0xffff);
+                    bk = v >= 0 && (v >> 16) != 0;
+                } else {
+                    se = r < R ? __ldcg(sel + (r / k) * kmax + r % k) : -1;
+                    bk = se == e && bulk_mode == 2 && tok_bulk(r / k);
+                }
                 if (se == e && bulk_mode != 0) {
-                    const bool b = bulk_mode == 1 ? cntb[e] > 0 : tok_bulk(r / k);
+                    const bool b = bulk_mode == 1 ? cntb[e] > 0 : bk;
                     if (b != (part == 1)) se = -1;
                 }
                 const unsigned m = __ballot_sync(0xffffffffu, se == e);
@@ -128,7 +177,7 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
                     const int pos = p + __popc(m & ((1u << lane) - 1u));
                     const int tt = r / k, jj = r % k;
                     route_tok[pos] = tt;
-                    route_w[pos] = __ldcg(selw + tt * kmax + jj);
+                    route_w[pos] = staged ? s_sw[r] : __ldcg(selw + tt * kmax + jj);
                     route_pos[tt * kmax + jj] = pos;
                 }
                 p += __popc(m);
@@ -307,15 +356,27 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
             const float inv = red[0];
             for (int e = lane; e < E; e += 32) pr[e] = pr[e] * inv;
             __syncwarp();
-            // top-k over probs + bias (+ mask), ties to the lower expert id: k rounds of warp argmax
-            unsigned long long taken[MAX_EXPERTS / 64] = {0};
+            // top-k over probs + bias (+ mask), ties to the lower expert id: k rounds of
+            // warp argmax; lane owns experts lane + 32 i
+            float sv[MAX_EXPERTS / 32];
+#pragma unroll
+            for (int i = 0; i < MAX_EXPERTS / 32; ++i) {
+                const int e = lane + 32 * i;
+                float v = -INFINITY;
+                if (e < E) {
+                    v = pr[e] + ly.rbias[e];
+                    if (ly.rmask) v = v + ly.rmask[e];
+                }
+                sv[i] = v;
+            }
+            unsigned taken = 0;
             for (int j = 0; j < k; ++j) {
                 float bv = -INFINITY; int best = 0x7fffffff;
-                for (int e = lane; e < E; e += 32) {
-                    if (taken[e >> 6] >> (e & 63) & 1ull) continue;
-                    float sv = pr[e] + ly.rbias[e];
-                    if (ly.rmask) sv = sv + ly.rmask[e];
-                    if (sv > bv || (sv == bv && e < best)) { bv = sv; best = e; }
+#pragma unroll
+                for (int i = 0; i < MAX_EXPERTS / 32; ++i) {
+                    const int e = lane + 32 * i;
+                    if (e >= E || (taken >> i & 1u)) continue;
+                    if (sv[i] > bv || (sv[i] == bv && e < best)) { bv = sv[i]; best = e; }
                 }
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -324,10 +385,12 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
                     if (ov > bv || (ov == bv && oi < best)) { bv = ov; best = oi; }
                 }
                 if (best >= E) best = 0;              // all remaining scores -inf: keep a valid id
-                taken[best >> 6] |= 1ull << (best & 63);
+                if ((best & 31) == lane) taken |= 1u << (best >> 5);
                 if (lane == 0) {
-                    b.sel[t * b.kmax + j] = active ? best : -1;
+                    const int id = active ? best : -1;
+                    b.sel[t * b.kmax + j] = id;
                     b.selw[t * b.kmax + j] = pr[best];
+                    if (b.sel_log) b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + j] = id;
                 }
             }
         }
@@ -340,8 +403,8 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
         b.selw[t * b.kmax] = 1.0f;
     }
     __syncthreads();
-    if (b.sel_log && threadIdx.x == 0)
-        for (int j = 0; j < k; ++j) b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + j] = b.sel[t * b.kmax + j];
+    if (b.sel_log && !(ly.is_moe && ok) && threadIdx.x < k)   // dense layer, or the weights never arrived
+        b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + threadIdx.x] = b.sel[t * b.kmax + threadIdx.x];
 
     // ---- last block: expert segments ----
     __threadfence();
