@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     for (int item = it0; item < it1; ++item) {
         const ItemRef it = item_ref<MODE>(p, cpos, c0);
         item_next<MODE>(p, cpos);
-        if (!failed && ncw > 0 && item <= issued_upto) failed = !mbar_wait(&mybar[slot], parity, p.err);
+        // the item's weights are waited for after the first activation loads are issued
+        const bool need_wait = !failed && ncw > 0 && item <= issued_upto;
         const uint8_t* st = mystage + slot * p.stage_bytes;
         const int n_groups = (it.n_tok + 8 * NTG - 1) / (8 * NTG);
         const int key = (MODE == GM_PROJ) ? 0 : it.expert;
@@ -187,7 +188,9 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                     for (int e = 0; e < 4; ++e) acc[m][nt][e] = 0.0f;
             if (!failed && ncw > 0) {
                 // activation fragments: token n = lane/4 of each n-tile, k = chunk*KC + q*KC/4 + 4s;
-                // kept across items while the token set is the same
+                // kept across items while the token set is the same. Two k-steps per 16-byte
+                // load where a chunk has an even k-step count (every activation row stride is
+                // a multiple of 16 halves, the K granularity of all weight types).
                 if (!(n_groups == 1 && key == b_key)) {
 #pragma unroll
                     for (int nt = 0; nt < NTG; ++nt) {
@@ -196,17 +199,32 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                         const __half* xr = ok ? p.X + (size_t)x_row<MODE>(p, it, n) * p.ldx : nullptr;
 #pragma unroll
                         for (int cc = 0; cc < MAXCPW; ++cc) {
+                            if constexpr (KS % 2 == 0) {
 #pragma unroll
-                            for (int s = 0; s < KS; ++s) {
-                                uint2 v = make_uint2(0u, 0u);
-                                if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
-                                B[nt][cc * KS + s][0] = v.x;
-                                B[nt][cc * KS + s][1] = v.y;
+                                for (int s = 0; s < KS; s += 2) {
+                                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                                    if (ok && cc < ncw) v = *(const uint4*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
+                                    B[nt][cc * KS + s][0] = v.x;
+                                    B[nt][cc * KS + s][1] = v.y;
+                                    B[nt][cc * KS + s + 1][0] = v.z;
+                                    B[nt][cc * KS + s + 1][1] = v.w;
+                                }
+                            } else {
+#pragma unroll
+                                for (int s = 0; s < KS; ++s) {
+                                    uint2 v = make_uint2(0u, 0u);
+                                    if (ok && cc < ncw) v = *(const uint2*)(xr + (c0 + cc) * KC + q * (KC / 4) + 4 * s);
+                                    B[nt][cc * KS + s][0] = v.x;
+                                    B[nt][cc * KS + s][1] = v.y;
+                                }
                             }
                         }
                     }
                     b_key = (n_groups == 1) ? key : -2;
                 }
+            }
+            if (g == 0 && need_wait) failed = !mbar_wait(&mybar[slot], parity, p.err);
+            if (!failed && ncw > 0) {
 #pragma unroll
                 for (int cc = 0; cc < MAXCPW; ++cc) {
                     if (cc < ncw) {
@@ -274,6 +292,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                 }
             }
         }
+        if (n_groups == 0 && need_wait) failed = !mbar_wait(&mybar[slot], parity, p.err);
         if (++slot == NS) { slot = 0; parity ^= 1u; }
     }
     // After a failed wait (error already recorded) later copies may still be in flight:
