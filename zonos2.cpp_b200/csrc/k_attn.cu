@@ -173,7 +173,6 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
             for (; pre < SM::NS && pre < nchunks && min(key0 + (pre + 1) * KCH, key1) <= fresh; ++pre) issue(pre);
     }
     pdl_wait();
-    pdl_release();
     if (threadIdx.x == 0)
         for (int c = pre; c < SM::NS && c < nchunks; ++c) issue(c);
 
@@ -250,6 +249,7 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
         if (__syncthreads_or(failed ? 1 : 0) && !failed) { failed = true; c_fail = c; }
         if (threadIdx.x == 0 && !failed && c + SM::NS < nchunks) { fence_proxy_async(); issue(c + SM::NS); }
     }
+    pdl_release();
     // After a failed wait (error recorded, results invalid) copies may still be landing
     // in the stages: wait for them, bounded, before the stages become the merge area.
     if (failed && threadIdx.x == 0)

@@ -150,10 +150,8 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
         ipos = item_seek<MODE>(p, it0);
         for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
         pdl_wait();
-        pdl_release();
     } else {
         pdl_wait();
-        pdl_release();
         const int n_items = (*p.n_active) * p.n_row_tiles;
         it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
         it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
@@ -295,6 +293,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
         if (n_groups == 0 && need_wait) failed = !mbar_wait(&mybar[slot], parity, p.err);
         if (++slot == NS) { slot = 0; parity ^= 1u; }
     }
+    pdl_release();
     // After a failed wait (error already recorded) later copies may still be in flight:
     // wait for each of them, bounded, before the shared memory goes away. Every warp
     // stayed in the item loop above, so the block-wide barriers always matched.

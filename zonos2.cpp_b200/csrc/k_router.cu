@@ -219,7 +219,6 @@ __global__ void __launch_bounds__(256) router_proj_kernel(const StepBufs b, cons
     for (int i = threadIdx.x; i < L / 4; i += blockDim.x)
         reinterpret_cast<float4*>(fn)[i] = reinterpret_cast<const float4*>(ly.ffn_norm + k0)[i];
     pdl_wait();
-    pdl_release();
     __syncthreads();                         // fn (and ws) written by other threads
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int tt = warp; tt < RP_TOK; tt += nw) {
@@ -246,6 +245,7 @@ __global__ void __launch_bounds__(256) router_proj_kernel(const StepBufs b, cons
         acc += __shfl_xor_sync(0xffffffffu, acc, 16);
         if (h == 0 && t0 + tt < T) b.rpart[((size_t)ks * b.rpart_T + t0 + tt) * rd + rb * RP_ROWS + r] = acc;
     }
+    pdl_release();
 }
 
 // One block per token (512 threads): ffn_norm (src/zonos2-graph.cpp:347) -> cur (f16
@@ -290,7 +290,6 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
         W4 = wst + 2 * rd * rd;
     }
     pdl_wait();
-    pdl_release();
     const bool active = b.tok_slot[t] >= 0;
 
     // ffn_norm -> cur (f16)
@@ -406,6 +405,7 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     if (b.sel_log && !(ly.is_moe && ok) && threadIdx.x < k)   // dense layer, or the weights never arrived
         b.sel_log[((size_t)layer * b.sel_log_T + t) * b.kmax + threadIdx.x] = b.sel[t * b.kmax + threadIdx.x];
 
+    pdl_release();
     // ---- last block: expert segments ----
     __threadfence();
     __syncthreads();
