@@ -35,23 +35,24 @@ template <int HD> __device__ __forceinline__ int kswz(int key) {   // K row chun
 template <int HD>
 __global__ void rope_append_kernel(const StepBufs b, const KVDev kv, const float* __restrict__ temp,
                                    const Dims dm, int layer) {
-    // one warp per (token, head); heads: [0, nh) q, [nh, nh+nkv) k, [nh+nkv, nh+2nkv) v
-    pdl_wait();
-    pdl_release();
+    // one warp per (token, head); heads: [0, nh) q, [nh, nh+nkv) k, [nh+nkv, nh+2nkv) v.
+    // The token's slot, position and page come from the step's packer and page table, both
+    // complete before the predecessor started: read through L2 before the wait.
     const int t = blockIdx.x, lane = threadIdx.x & 31;
     const int nh = dm.n_head, nkv = dm.n_head_kv;
     const int h = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (h >= nh + 2 * nkv) return;
-    const int slot = b.tok_slot[t];
-    if (slot < 0) return;
-    const int pos = b.tok_pos[t];
-    const float* x = b.qkvg + (size_t)t * b.ldq + (size_t)h * HD;    // q | k | v are contiguous
+    const bool live = h < nh + 2 * nkv;
+    const int slot = live ? __ldcg(b.tok_slot + t) : -1;
+    const int pos = live ? __ldcg(b.tok_pos + t) : 0;
     const bool isq = h < nh, isk = !isq && h < nh + nkv;
+    const int j = pos % PAGE, pg = pos / PAGE;
+    const int page = (slot >= 0 && !isq && pg < kv.max_pages) ? __ldcg(kv.page_table + (size_t)slot * kv.max_pages + pg) : -1;
+    pdl_wait();
+    pdl_release();
+    if (slot < 0) return;
+    const float* x = b.qkvg + (size_t)t * b.ldq + (size_t)h * HD;    // q | k | v are contiguous
     __half* lbase = nullptr;
-    const int j = pos % PAGE;
     if (!isq) {
-        const int pg = pos / PAGE;
-        const int page = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
         if (page < 0) { if (lane == 0) atomicOr(b.err, (uint32_t)DERR_PAGE); return; }
         lbase = kv.pool + (size_t)page * kv.page_elems + (size_t)layer * kv.layer_elems;
     }
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
     // dependent), so those chunks are copied before the wait. Q and the keys appended by
     // this step come after it. The token's slot and position load together.
     const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
-    const int slot = b.tok_slot[t], pos = b.tok_pos[t];
+    const int slot = __ldcg(b.tok_slot + t), pos = __ldcg(b.tok_pos + t);
     if (slot < 0) return;
     const int n_keys = pos + 1;
     const int key0 = sp * split_keys;
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
     const int nchunks = (key1 - key0 + KCH - 1) / KCH;
     // the first chunk's page, loaded while the barriers are set up
     const int pg0 = key0 / PAGE;
-    const int page0 = threadIdx.x == 0 && pg0 < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg0] : -1;
+    const int page0 = threadIdx.x == 0 && pg0 < kv.max_pages ? __ldcg(kv.page_table + (size_t)slot * kv.max_pages + pg0) : -1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r = lane >> 2, q = lane & 3;
     const int nh = dm.n_head;
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
         const int key = key0 + c * KCH, pg = key / PAGE;
         if (pg != cpg) {
             cpg = pg;
-            cpage = pg < kv.max_pages ? kv.page_table[(size_t)slot * kv.max_pages + pg] : -1;
+            cpage = pg < kv.max_pages ? __ldcg(kv.page_table + (size_t)slot * kv.max_pages + pg) : -1;
         }
         if (cpage < 0) return false;
         const __half* lb = kv.pool + (size_t)cpage * kv.page_elems + (size_t)layer * kv.layer_elems;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
     };
     int pre = 0;                                 // chunks issued before the wait
     if constexpr (kUsePdl) {
-        const int fresh = b.descs[b.tok_desc[t]].n_past;      // first key written by this step
+        const int fresh = __ldcg(&b.descs[__ldcg(b.tok_desc + t)].n_past);   // first key written by this step
         if (threadIdx.x == 0)
             for (; pre < SM::NS && pre < nchunks && min(key0 + (pre + 1) * KCH, key1) <= fresh; ++pre) issue(pre);
     }

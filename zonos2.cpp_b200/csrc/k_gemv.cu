@@ -41,6 +41,28 @@ template <class D, int NTG, int s, int KS> struct KLoop {
         KLoop<D, NTG, s + 1, KS>::template run<NMAT, NTV>(dec, T, lane, kbase, B, acc, m);
     }
 };
+// gate/up variant of KLoop: both matrices' fragments per k-step, so the two accumulator
+// chains interleave
+template <class D, int NTG, int s, int KS> struct KLoop2 {
+    template <int NTV>
+    __device__ __forceinline__ static void run(const D& d0, const D& d1, const uint8_t* T0, const uint8_t* T1, int lane,
+                                               int kbase, const uint32_t (&B)[NTG][MAXKS][2], float (&acc)[2][NTG][4]) {
+        uint32_t a[4], c[4];
+        d0.template frag<s>(T0, lane, a);
+        d1.template frag<s>(T1, lane, c);
+#pragma unroll
+        for (int nt = 0; nt < NTV; ++nt) {
+            mma16816(acc[0][nt], a[0], a[1], a[2], a[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
+            mma16816(acc[1][nt], c[0], c[1], c[2], c[3], B[nt][kbase + s][0], B[nt][kbase + s][1]);
+        }
+        KLoop2<D, NTG, s + 1, KS>::template run<NTV>(d0, d1, T0, T1, lane, kbase, B, acc);
+    }
+};
+template <class D, int NTG, int KS> struct KLoop2<D, NTG, KS, KS> {
+    template <int NTV>
+    __device__ __forceinline__ static void run(const D&, const D&, const uint8_t*, const uint8_t*, int, int,
+                                               const uint32_t (&)[NTG][MAXKS][2], float (&)[2][NTG][4]) {}
+};
 template <class D, int NTG, int KS> struct KLoop<D, NTG, KS, KS> {
     template <int NMAT, int NTV>
     __device__ __forceinline__ static void run(const D&, const uint8_t*, int, int, const uint32_t (&)[NTG][MAXKS][2],
@@ -226,6 +248,16 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
 #pragma unroll
                 for (int cc = 0; cc < MAXCPW; ++cc) {
                     if (cc < ncw) {
+                        if constexpr (NMAT == 2 && WT != GT_F16) {
+                            // gate and up decoded per k-step: two independent MMA chains
+                            const uint8_t* T0 = st + cc * p.tile_bytes;
+                            const uint8_t* T1 = st + wbytes + cc * p.tile_bytes;
+                            D d0, d1;
+                            d0.prep(T0, lane);
+                            d1.prep(T1, lane);
+                            if (ntv == NTG) KLoop2<D, NTG, 0, KS>::template run<NTG>(d0, d1, T0, T1, lane, cc * KS, B, acc);
+                            else KLoop2<D, NTG, 0, KS>::template run<1>(d0, d1, T0, T1, lane, cc * KS, B, acc);
+                        } else {
 #pragma unroll
                         for (int m = 0; m < NMAT; ++m) {
                             const uint8_t* T = st + m * wbytes + cc * p.tile_bytes;
@@ -233,6 +265,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                             dec.prep(T, lane);
                             if (ntv == NTG) KLoop<D, NTG, 0, KS>::template run<NMAT, NTG>(dec, T, lane, cc * KS, B, acc, m);
                             else KLoop<D, NTG, 0, KS>::template run<NMAT, 1>(dec, T, lane, cc * KS, B, acc, m);
+                        }
                         }
                     }
                 }

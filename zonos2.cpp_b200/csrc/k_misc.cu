@@ -89,7 +89,7 @@ __device__ __forceinline__ float emb_elem(const uint8_t* tbl, uint32_t type, siz
 
 // emb = sum of 10 table rows (src/zonos2-graph.cpp:249-259), x = rms_norm(emb) seeds the
 // residual (:300), cur = rms_norm(x) * attn_norm[0] feeds layer 0 (:343).
-__global__ void embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0, const Dims dm) {
+__global__ void __launch_bounds__(1024) embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0, const Dims dm) {
     extern __shared__ float sh[];
     pdl_wait();
     pdl_release();
@@ -139,13 +139,16 @@ __global__ void embed_kernel(const StepBufs b, const EmbedDev e, const float* __
 __global__ void __launch_bounds__(512) moe_combine_kernel(const StepBufs b, int k, const float* __restrict__ next_norm,
                                                           const float* __restrict__ out_norm, const Dims dm, int last) {
     __shared__ float red[32];
-    pdl_wait();
-    pdl_release();
+    // the token's slot, output row and route positions come from the packer and the router,
+    // both complete before the predecessor started: read through L2 before the wait
     const int t = blockIdx.x, d = dm.n_embd, d4 = d / 4;
-    const bool active = b.tok_slot[t] >= 0;
+    const bool active = __ldcg(b.tok_slot + t) >= 0;
+    const int orow = __ldcg(b.tok_out + t);
     int pos[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) pos[j] = (active && j < k) ? b.route_pos[t * b.kmax + j] : -1;
+    for (int j = 0; j < 8; ++j) pos[j] = (active && j < k) ? __ldcg(b.route_pos + t * b.kmax + j) : -1;
+    pdl_wait();
+    pdl_release();
     float4* res = reinterpret_cast<float4*>(b.res + (size_t)t * d);
     float ss = 0.0f;
     for (int i = threadIdx.x; i < d4; i += blockDim.x) {
@@ -162,7 +165,6 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(const StepBufs b, int 
         res[i] = r;
         ss += r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w;
     }
-    const int orow = b.tok_out[t];
     if (last && orow < 0) return;              // uniform per block
     ss = block_sum(ss, red);
     const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
@@ -395,7 +397,7 @@ void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
 }
 
 void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s) {
-    launch_pdl(embed_kernel, dim3(T), dim3(256), (d.n_embd + 32) * sizeof(float), s, b, e, attn_norm0, d);
+    launch_pdl(embed_kernel, dim3(T), dim3(1024), (d.n_embd + 32) * sizeof(float), s, b, e, attn_norm0, d);
 }
 
 void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,

@@ -289,8 +289,18 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
         W2 = wst + rd * rd;
         W4 = wst + 2 * rd * rd;
     }
+    const bool active = __ldcg(b.tok_slot + t) >= 0;        // packer output, complete before the predecessor
     pdl_wait();
-    const bool active = b.tok_slot[t] >= 0;
+    // the router projection's inputs load with the residual row: partial sums over the K
+    // slices, bias, and the previous MoE layer's state
+    float pa = 0.0f, pb = 0.0f, pst = 0.0f, ped = 0.0f;
+    const bool eda_on = ly.is_moe && ly.eda && !first_moe;
+    if (ly.is_moe && threadIdx.x < rd) {
+        const int i = threadIdx.x;
+        for (int ks = 0; ks < router_kslices(d); ++ks) pa += b.rpart[((size_t)ks * b.rpart_T + t) * rd + i];
+        pb = ly.rdown_b[i];
+        if (eda_on) { pst = b.rstate[(size_t)t * rd + i]; ped = ly.eda[i]; }
+    }
 
     // ffn_norm -> cur (f16)
     const float4* r4 = reinterpret_cast<const float4*>(b.res + (size_t)t * d);
@@ -309,11 +319,10 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
 
     bool ok = true;
     if (ly.is_moe) {
-        for (int i = threadIdx.x; i < rd; i += blockDim.x) {
-            float a = 0.0f;
-            for (int ks = 0; ks < router_kslices(d); ++ks) a += b.rpart[((size_t)ks * b.rpart_T + t) * rd + i];
-            float v = a * sc + ly.rdown_b[i];
-            if (ly.eda && !first_moe) v = v + b.rstate[(size_t)t * rd + i] * ly.eda[i];
+        if (threadIdx.x < rd) {
+            const int i = threadIdx.x;
+            float v = pa * sc + pb;
+            if (eda_on) v = v + pst * ped;
             rh[i] = v;
             b.rstate[(size_t)t * rd + i] = v;
         }

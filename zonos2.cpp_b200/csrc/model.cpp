@@ -272,7 +272,7 @@ struct Loader {
         D.rd = rd; D.n_layer = (int)hp.n_layer; D.n_codebooks = (int)hp.n_codebooks;
         D.audio_vocab = (int)hp.audio_vocab; D.text_vocab = (int)hp.text_vocab;
         D.rms_eps = hp.rms_eps; D.qk_eps = hp.qk_norm_eps; D.rope_base = hp.rope_freq_base; D.softcap = hp.logit_softcap;
-        if (rd > 1024 || rd % 8) return fail(Z2B_ERR_UNSUPPORTED, "router_dim must be a multiple of 8, at most 1024");
+        if (rd > 512 || rd % 8) return fail(Z2B_ERR_UNSUPPORTED, "router_dim must be a multiple of 8, at most 512");
         if (d % 16) return fail(Z2B_ERR_UNSUPPORTED, "n_embd must be a multiple of 16 (router K slices)");
         return true;
     }
