@@ -138,6 +138,8 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                         // [NW][NS]
     uint8_t* stages = smem + 128 * ((NW * NS * 8 + 127) / 128);                  // [NW][NS][stage_bytes]
     float* red = reinterpret_cast<float*>(stages + (size_t)NW * NS * p.stage_bytes);   // [2][NW][NMAT][NTG][32][4]
+    // GM_PROJ: this warp's activation slice [8 NTG tokens][x_rs bytes]
+    uint8_t* xw = reinterpret_cast<uint8_t*>(red + 2 * NW * NMAT * NTG * 128) + (size_t)warp * 8 * NTG * p.x_rs;
     uint64_t* mybar = bars + warp * NS;
     uint8_t* mystage = stages + (size_t)warp * NS * p.stage_bytes;
 
@@ -211,7 +213,49 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                 // kept across items while the token set is the same. Two k-steps per 16-byte
                 // load where a chunk has an even k-step count (every activation row stride is
                 // a multiple of 16 halves, the K granularity of all weight types).
-                if (!(n_groups == 1 && key == b_key)) {
+                const bool need_b = !(n_groups == 1 && key == b_key);
+                bool b_done = false;
+                if constexpr (MODE == GM_PROJ && KS % 2 == 0) {
+                if (need_b && p.x_rs > 0) {
+                    // coalesced 16-byte copies of the pass's token rows into the warp's slice
+                    // (absent tokens zero-filled), then conflict-free 16-byte fragment reads
+                    constexpr int QU = KC / 32;                  // 16-byte units per quarter-chunk
+                    constexpr int QSB = (QU + 1) * 16;           // padded quarter-chunk bytes
+                    const int upr = ncw * 4 * QU;                // units per token row
+                    for (int i = lane; i < 8 * NTG * upr; i += 32) {
+                        const int n = i / upr, u = i - n * upr;
+                        const int cc = u / (4 * QU), w = u - cc * 4 * QU;
+                        const int qq = w / QU, uu = w - qq * QU;
+                        const int tok = g * 8 * NTG + n;
+                        const bool ok = tok < it.n_tok;
+                        const __half* src = p.X + (size_t)(ok ? x_row<MODE>(p, it, tok) : 0) * p.ldx + (c0 + cc) * KC + w * 8;
+                        cp_async16(xw + (size_t)n * p.x_rs + cc * 4 * QSB + qq * QSB + uu * 16, src, ok);
+                    }
+                    cp_async_commit();
+                    cp_async_wait_0();
+                    __syncwarp();
+#pragma unroll
+                    for (int nt = 0; nt < NTG; ++nt) {
+                        const uint8_t* xr = xw + (size_t)(nt * 8 + r8) * p.x_rs + q * QSB;
+#pragma unroll
+                        for (int cc = 0; cc < MAXCPW; ++cc) {
+#pragma unroll
+                            for (int s = 0; s < KS; s += 2) {
+                                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                                if (nt < ntv && cc < ncw) v = *(const uint4*)(xr + cc * 4 * QSB + (s / 2) * 16);
+                                B[nt][cc * KS + s][0] = v.x;
+                                B[nt][cc * KS + s][1] = v.y;
+                                B[nt][cc * KS + s + 1][0] = v.z;
+                                B[nt][cc * KS + s + 1][1] = v.w;
+                            }
+                        }
+                    }
+                    __syncwarp();                                // slice reads done before any refill
+                    b_key = (n_groups == 1) ? key : -2;
+                    b_done = true;
+                }
+                }
+                if (need_b && !b_done) {
 #pragma unroll
                     for (int nt = 0; nt < NTG; ++nt) {
                         const int n = g * 8 * NTG + nt * 8 + r8;
@@ -352,7 +396,7 @@ void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStrea
 }  // namespace
 
 void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
-                   int* cps) {
+                   int* cps, int* x_rs) {
     *cps = 1;
     const int max_cpw = std::max(1, MAXKS / m.steps);       // chunks a warp can hold in registers
     const int min_nw = (m.chunks + max_cpw - 1) / max_cpw;
@@ -370,12 +414,32 @@ void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stage
     const int cpw = (m.chunks + nw - 1) / nw;
     const int sb = cpw * m.tile_bytes * nmat;
     const int red = 2 * nw * nmat * ntg * 128 * 4;
-    auto total = [&](int ns) { return 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red; };
+    // projections: each warp stages its K-slice of the pass's tokens in shared memory, a
+    // token row as 4 quarter-chunks of KC/4 halves each padded by 16 bytes, the row padded
+    // so that the 8 lanes of a quarter-warp (2 tokens x 4 quarters) read 8 distinct 16-byte
+    // bank groups
+    int rs = 0;
+    if (x_rs && nmat == 1 && ntg == 2 && m.steps % 2 == 0) {
+        const int qsu = m.steps / 2 + 1;                     // 16-byte units per padded quarter
+        const int base = cpw * 4 * qsu;
+        for (int pad = 0; pad < 8 && rs == 0; ++pad) {
+            const int r = (base + pad) % 8;
+            bool ok = true;
+            for (int a = 0; a < 4; ++a)
+                for (int b2 = 0; b2 < 4; ++b2)
+                    if ((a * qsu) % 8 == (b2 * qsu + r) % 8) ok = false;
+            if (ok) rs = (base + pad) * 16;
+        }
+    }
+    int xbytes = nw * 8 * ntg * rs;
+    auto total = [&](int ns) { return 128 * ((nw * ns * 8 + 127) / 128) + nw * ns * sb + red + xbytes; };
     // deepest ring (up to 4 stages) at the target blocks per SM: three for the expert down
     // pass, two for gate/up (two matrices per stage) and the projections (one block's
     // barriers overlap the other's streaming)
     const int per_sm = 233472, per_block_reserved = 1024;
     const int want = (ntg == 1 && nmat == 1) ? 3 : 2;
+    if (xbytes > 0 && want * (total(1) + per_block_reserved) > per_sm) { rs = 0; xbytes = 0; }   // keep the blocks per SM
+    if (x_rs) *x_rs = rs;
     int ns = 0;
     for (int cand = 4; cand >= 1 && ns == 0; --cand)
         if (want * (total(cand) + per_block_reserved) <= per_sm) ns = cand;

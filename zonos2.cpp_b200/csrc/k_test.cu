@@ -166,7 +166,7 @@ extern "C" int z2b_test_gemv(uint32_t type, int64_t rows, int64_t k, const void*
         p.n_seg = 1; p.total_items = m.n_row_tiles;
         p.X = dx; p.ldx = (int)k; p.T = n_tok; p.out = dout; p.ldo = (int)rows; p.err = derr;
         int nw, smem;
-        gemv_geometry(m, 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
+        gemv_geometry(m, 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps, &p.x_rs);
         int nsm = 148;
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, 0);
         launch_gemv(p, nw, m.n_row_tiles < nsm ? m.n_row_tiles : nsm, smem, 0);

@@ -61,11 +61,12 @@ struct GemvParams {
     uint32_t* err;
     // launch geometry (host-filled)
     int n_stages, stage_bytes, cps;  // ring depth per warp, bytes per stage, chunks per stage
+    int x_rs;                       // GM_PROJ: bytes per token row of a warp's shared activation slice (0: none)
 };
 
 // Chooses warps/stages for a weight matrix and fills the launch geometry.
 void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stages, int* stage_bytes, int* smem,
-                   int* cps);
+                   int* cps, int* x_rs = nullptr);
 void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s);
 // tcgen05 grouped GEMM over the experts active[n_small, n_active) (k_gemm.cu)
 bool moe_gemm_supported(const DevMat& m);

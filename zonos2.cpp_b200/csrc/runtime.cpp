@@ -253,7 +253,7 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
     p.total_items = items;
     p.X = X; p.ldx = ldx; p.T = T; p.out = out; p.ldo = ldo; p.cap = cap; p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
+    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps, &p.x_rs);
     const int grid = std::min(items, c->m->n_sm * ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
