@@ -93,6 +93,15 @@ int z2b_slot_reset(z2b_ctx* ctx, int slot, const z2b_sampling* sp);
  * Replaces zonos2_batch_slot_prefill (src/zonos2.h:286-288, src/zonos2-graph.cpp:703-760). */
 int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* out_logits);
 
+/* z2b_slot_prefill with the reference's speaker arguments, in its order. spk
+ * (float[spk_dim], or NULL for none) is projected as spk_proj(spk_lda(spk)), plus
+ * spk_emotion_delta (float[n_embd]) when not NULL, and replaces the embedding of prompt
+ * row spk_pos (0 <= spk_pos < n0) before emb_norm. Replaces zonos2_batch_slot_prefill's
+ * spk / spk_pos / spk_emotion_delta (src/zonos2.h:286-288, 312-313;
+ * src/zonos2-graph.cpp:262-292, 703-760). Z2B_ERR_ARG if spk_pos is outside the prompt. */
+int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos,
+                         float* out_logits, const float* spk_emotion_delta);
+
 /* One batched step over n streams: rows ids[sum(n_new)][10] are fed in desc order
  * (decode streams feed one row; prompt chunks may be mixed in). For each desc with
  * Z2B_WANT_SAMPLE, out_codes[i*n_codebooks ..] receives the sampled frame; with

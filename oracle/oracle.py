@@ -66,6 +66,9 @@ def lib():
         L.o_ctx_new.restype = P
         L.o_ctx_free.argtypes = [P]
         L.o_prefill.argtypes = [P, I, V, I, V]
+        L.o_model_set_spk.argtypes = [P, V]
+        L.o_spk_row.argtypes = [P, V, V, V]
+        L.o_prefill_spk.argtypes = [P, I, V, I, V, I, V, V]
         L.o_step.argtypes = [P, V, V, V, I, V]
         L.o_last_sel.argtypes = [P, V, I]
         L.o_ctx_fake_fill.argtypes = [P, I, I, ctypes.c_uint32]
@@ -132,9 +135,22 @@ class Model:
                                    ctypes.addressof(self._text), ctypes.addressof(self._on),
                                    ctypes.addressof(self._out), ctypes.cast(self._layers, ctypes.c_void_p),
                                    _ptr(self.expert_used), mode)
+        spk_names = ["spk_lda.weight", "spk_lda.bias", "spk_proj.weight", "spk_proj.bias"]
+        self.has_spk = all(nm in self.t for nm in spk_names)
+        if self.has_spk:
+            self._spk = (OTensor * 4)(*[ot(nm) for nm in spk_names])
+            lib().o_model_set_spk(self.h, ctypes.cast(self._spk, ctypes.c_void_p))
 
     def set_mode(self, mode: int):
         lib().o_model_set_mode(self.h, mode)
+
+    def spk_row(self, spk, delta=None) -> np.ndarray:
+        """The projected speaker row [n_embd] that replaces a prompt row's embedding."""
+        spk = np.ascontiguousarray(spk, np.float32)
+        delta = None if delta is None else np.ascontiguousarray(delta, np.float32)
+        out = np.empty(self.hp.n_embd, np.float32)
+        assert lib().o_spk_row(self.h, _ptr(spk), _ptr(delta) if delta is not None else None, _ptr(out)) == 0
+        return out
 
     def set_expert_mask(self, keep: dict[int, list[int]]):
         for L in range(self.hp.n_layer):
@@ -160,10 +176,16 @@ class Ctx:
         self.h = lib().o_ctx_new(model.h, n_slots, cap)
         self.nout = model.hp.n_codebooks * model.hp.audio_vocab
 
-    def prefill(self, slot: int, ids) -> np.ndarray:
+    def prefill(self, slot: int, ids, spk=None, spk_pos: int = 0, spk_emotion_delta=None) -> np.ndarray:
         ids = np.ascontiguousarray(ids, np.int32)
         out = np.empty(self.nout, np.float32)
-        rc = lib().o_prefill(self.h, slot, _ptr(ids), ids.shape[0], _ptr(out))
+        if spk is None:
+            rc = lib().o_prefill(self.h, slot, _ptr(ids), ids.shape[0], _ptr(out))
+        else:
+            spk = np.ascontiguousarray(spk, np.float32)
+            dl = None if spk_emotion_delta is None else np.ascontiguousarray(spk_emotion_delta, np.float32)
+            rc = lib().o_prefill_spk(self.h, slot, _ptr(ids), ids.shape[0], _ptr(spk), int(spk_pos),
+                                     _ptr(dl) if dl is not None else None, _ptr(out))
         assert rc == 0
         return out.reshape(self.model.hp.n_codebooks, -1)
 

@@ -152,6 +152,7 @@ struct OHp {
 struct OModel {
     OHp hp;
     OT audio[16], text, out_norm, output;
+    OT spk_lda_w, spk_lda_b, spk_proj_w, spk_proj_b;   // speaker projection (optional)
     std::vector<OLayer> L;
     int mode = Z2O_EXACT;
 };
@@ -317,15 +318,21 @@ float sigm(float x) { return 1.0f / (1.0f + std::exp(-x)); }
 // cache as f16; decode: token t of slot slots[t] at pos[t] attends the f16 cache [0, pos]
 // (flash-attn path, :139-153). Logits rows for tokens with want[t].
 void forward(OCtx* c, const int32_t* ids, int n, const int* slots, const int* pos, bool prefill,
-             const char* want, float* out_logits) {
+             const char* want, float* out_logits, const float* over_row = nullptr, int over_t = -1) {
     OModel& M = *c->m;
     const OHp& hp = M.hp;
     const int d = hp.n_embd, hd = hp.head_dim, nh = hp.n_head, nkv = hp.n_head_kv, G = nh / nkv;
     const int ncb = hp.n_codebooks, av = hp.audio_vocab, mode = M.mode;
-    // embedding sum + emb_norm (:249-260, :300)
+    // embedding sum + emb_norm (:249-260, :300); token over_t takes the speaker row instead
+    // of the sum (:262-292)
     std::vector<float> x((size_t)n * d), res((size_t)n * d), cur((size_t)n * d), row((size_t)d);
     for (int t = 0; t < n; ++t) {
         float* e = &x[(size_t)t * d];
+        if (t == over_t) {
+            for (int i = 0; i < d; ++i) e[i] = over_row[i];
+            rms_norm(e, d, hp.rms_eps, nullptr, e);
+            continue;
+        }
         for (int k = 0; k <= ncb; ++k) {
             const OT& tb = k < ncb ? M.audio[k] : M.text;
             const int id = ids[t * (ncb + 1) + k];
@@ -666,6 +673,46 @@ int o_prefill(void* ctx, int slot, const int32_t* ids, int n0, float* out_logits
     for (int i = 0; i < n0; ++i) pos[i] = i;
     want[n0 - 1] = 1;
     forward(c, ids, n0, slots.data(), pos.data(), true, want.data(), out_logits);
+    return 0;
+}
+
+// Speaker projection tensors (t[0..3] = spk_lda.weight, spk_lda.bias, spk_proj.weight,
+// spk_proj.bias).
+void o_model_set_spk(void* m, const o_tensor* t) {
+    OModel* M = (OModel*)m;
+    M->spk_lda_w = cv(t[0]); M->spk_lda_b = cv(t[1]); M->spk_proj_w = cv(t[2]); M->spk_proj_b = cv(t[3]);
+}
+
+// The projected speaker row (src/zonos2-graph.cpp:262-275): W_proj (W_lda spk + b_lda)
+// + b_proj (+ delta), each product through matmul() in the model's arithmetic mode.
+int o_spk_row(void* m, const float* spk, const float* delta, float* out_row) {
+    OModel* M = (OModel*)m;
+    if (!M->spk_lda_w.data || !M->spk_proj_w.data) return 1;
+    const int ld = (int)M->spk_lda_w.ne1, d = (int)M->spk_proj_w.ne1;
+    std::vector<float> sl((size_t)ld);
+    matmul(M->mode, M->spk_lda_w, 0, spk, 1, sl.data(), ld);
+    const std::vector<float> lb = small(M->spk_lda_b), pb = small(M->spk_proj_b);
+    for (int i = 0; i < ld; ++i) sl[i] = sl[i] + lb[i];
+    matmul(M->mode, M->spk_proj_w, 0, sl.data(), 1, out_row, d);
+    for (int j = 0; j < d; ++j) {
+        out_row[j] = out_row[j] + pb[j];
+        if (delta) out_row[j] = out_row[j] + delta[j];
+    }
+    return 0;
+}
+
+// zonos2_batch_slot_prefill with spk / spk_pos / spk_emotion_delta (:703-760, :262-292)
+int o_prefill_spk(void* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
+                  float* out_logits) {
+    OCtx* c = (OCtx*)ctx;
+    if (slot < 0 || slot >= c->n_slots || n0 < 1 || n0 > c->cap || spk_pos < 0 || spk_pos >= n0) return 1;
+    std::vector<float> row((size_t)c->m->hp.n_embd);
+    if (o_spk_row(c->m, spk, delta, row.data())) return 1;
+    std::vector<int> slots(n0, slot), pos(n0);
+    std::vector<char> want(n0, 0);
+    for (int i = 0; i < n0; ++i) pos[i] = i;
+    want[n0 - 1] = 1;
+    forward(c, ids, n0, slots.data(), pos.data(), true, want.data(), out_logits, row.data(), spk_pos);
     return 0;
 }
 

@@ -74,3 +74,44 @@ def test_sampler_consumes_one_draw_per_codebook():
     lg = np.random.default_rng(1).standard_normal((9, 64)).astype(np.float32)
     s = O.Sampler(9, top_k=1, min_p=0.0, rep_penalty=1.0, seed=3)
     assert s.sample(lg).tolist() == lg.argmax(-1).tolist()
+
+
+def _spk_inputs(om, seed):
+    g = np.random.default_rng(seed)
+    sd = int(om.t["spk_lda.weight"].shape[0])
+    return g.standard_normal(sd).astype(np.float32), (0.1 * g.standard_normal(om.hp.n_embd)).astype(np.float32)
+
+
+def test_speaker_row_matches_numpy(om):
+    """spk_proj(spk_lda(spk)) + delta (src/zonos2-graph.cpp:262-275) against float64 numpy
+    over gguf-py's dequantised tensors."""
+    from gguf.quants import dequantize
+
+    def deq(name):
+        t = om.t[name]
+        return dequantize(t.data, t.tensor_type).astype(np.float64).reshape(
+            [int(x) for x in reversed(t.shape) if int(x) > 1] or [-1])
+
+    spk, delta = _spk_inputs(om, 11)
+    sl = deq("spk_lda.weight") @ spk.astype(np.float64) + deq("spk_lda.bias")
+    sp = deq("spk_proj.weight") @ sl.astype(np.float32).astype(np.float64) + deq("spk_proj.bias")
+    got = om.spk_row(spk)
+    assert np.allclose(got, sp, rtol=1e-5, atol=1e-6)
+    got_d = om.spk_row(spk, delta)
+    assert np.allclose(got_d, (got.astype(np.float64) + delta), rtol=1e-6, atol=1e-7)
+
+
+def test_speaker_replaces_the_row(om):
+    """The speaker row replaces (not adds to) the embedding at spk_pos: the ids of that
+    row no longer matter, and the logits differ from the prompt without a speaker."""
+    spk, delta = _spk_inputs(om, 12)
+    p = prompt(10, 5)
+    q = p.copy()
+    q[2] = (q[2] + 7) % 500
+    a = O.Ctx(om, 1, 64).prefill(0, p, spk=spk, spk_pos=2)
+    b = O.Ctx(om, 1, 64).prefill(0, q, spk=spk, spk_pos=2)
+    assert np.array_equal(a, b)
+    plain = O.Ctx(om, 1, 64).prefill(0, p)
+    assert not np.array_equal(a, plain)
+    e = O.Ctx(om, 1, 64).prefill(0, p, spk=spk, spk_pos=2, spk_emotion_delta=delta)
+    assert not np.array_equal(a, e)

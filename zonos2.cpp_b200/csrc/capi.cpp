@@ -93,6 +93,13 @@ int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* 
     return ctx_prefill(ctx->c, slot, ids, n0, out_logits);
 }
 
+int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos,
+                         float* out_logits, const float* spk_emotion_delta) {
+    if (!ctx || !ids) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_prefill_spk(ctx->c, slot, ids, n0, spk, spk_pos, spk_emotion_delta, out_logits);
+}
+
 int z2b_step(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes,
              float* out_logits) {
     if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }

@@ -87,9 +87,11 @@ __device__ __forceinline__ float emb_elem(const uint8_t* tbl, uint32_t type, siz
     }
 }
 
-// emb = sum of 10 table rows (src/zonos2-graph.cpp:249-259), x = rms_norm(emb) seeds the
-// residual (:300), cur = rms_norm(x) * attn_norm[0] feeds layer 0 (:343).
-__global__ void __launch_bounds__(1024) embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0, const Dims dm) {
+// emb = sum of 10 table rows (src/zonos2-graph.cpp:249-259), or for token spk_t the
+// speaker row, which replaces the sum (:262-292); x = rms_norm(emb) seeds the residual
+// (:300), cur = rms_norm(x) * attn_norm[0] feeds layer 0 (:343).
+__global__ void __launch_bounds__(1024) embed_kernel(const StepBufs b, const EmbedDev e, const float* __restrict__ w0,
+                                                     const Dims dm, int spk_t, const float* __restrict__ spk_row) {
     extern __shared__ float sh[];
     pdl_wait();
     pdl_release();
@@ -107,12 +109,17 @@ __global__ void __launch_bounds__(1024) embed_kernel(const StepBufs b, const Emb
     }
     if (bad && threadIdx.x == 0) atomicOr(b.err, (uint32_t)DERR_BOUNDS);
     float ss = 0.0f;
+    const bool spk = t == spk_t;
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
         float acc = 0.0f;
-        for (int c = 0; c < NCOL; ++c) {
-            const uint8_t* tbl = c < dm.n_codebooks ? e.audio[c] : e.text;
-            const float v = emb_elem(tbl, e.type, e.row_bytes, idc[c], j);
-            acc = (c == 0) ? v : __fadd_rn(acc, v);
+        if (spk) {
+            acc = spk_row[j];
+        } else {
+            for (int c = 0; c < NCOL; ++c) {
+                const uint8_t* tbl = c < dm.n_codebooks ? e.audio[c] : e.text;
+                const float v = emb_elem(tbl, e.type, e.row_bytes, idc[c], j);
+                acc = (c == 0) ? v : __fadd_rn(acc, v);
+            }
         }
         emb[j] = acc;
         ss += acc * acc;
@@ -130,6 +137,39 @@ __global__ void __launch_bounds__(1024) embed_kernel(const StepBufs b, const Emb
     const float sc2 = 1.0f / sqrtf(ss2 / (float)d + dm.rms_eps);
     for (int j = threadIdx.x; j < d; j += blockDim.x)
         b.cur[(size_t)t * d + j] = __float2half_rn((emb[j] * sc2) * w0[j]);
+}
+
+// ---------------------------------------------------------------- speaker injection
+// s_lda = W_lda spk + b_lda (spk_dim -> lda_dim), s_proj = W_proj s_lda + b_proj
+// (lda_dim -> n_embd), + the emotion delta when given (src/zonos2-graph.cpp:262-275). One
+// block; a warp per output row, lane-strided f32 products summed in a fixed order.
+__global__ void __launch_bounds__(1024) spk_proj_kernel(const float* __restrict__ lda_w, const float* __restrict__ lda_b,
+                                                        const float* __restrict__ proj_w, const float* __restrict__ proj_b,
+                                                        const float* __restrict__ spk, const float* __restrict__ delta,
+                                                        int spk_dim, int lda_dim, int n_embd, float* __restrict__ row) {
+    extern __shared__ float sl[];                 // [lda_dim]
+    pdl_wait();
+    pdl_release();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int i = w; i < lda_dim; i += nw) {
+        const float* wr = lda_w + (size_t)i * spk_dim;
+        float acc = 0.0f;
+        for (int k = lane; k < spk_dim; k += 32) acc += wr[k] * spk[k];
+        acc = warp_sum(acc);
+        if (lane == 0) sl[i] = acc + lda_b[i];
+    }
+    __syncthreads();
+    for (int j = w; j < n_embd; j += nw) {
+        const float* wr = proj_w + (size_t)j * lda_dim;
+        float acc = 0.0f;
+        for (int k = lane; k < lda_dim; k += 32) acc += wr[k] * sl[k];
+        acc = warp_sum(acc);
+        if (lane == 0) {
+            float v = acc + proj_b[j];
+            if (delta) v = v + delta[j];
+            row[j] = v;
+        }
+    }
 }
 
 // ---------------------------------------------------------------- MoE combine
@@ -396,8 +436,16 @@ void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
     launch_pdl(to_f16_kernel, dim3(grid), dim3(256), 0, s, x, y, n);
 }
 
-void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s) {
-    launch_pdl(embed_kernel, dim3(T), dim3(1024), (d.n_embd + 32) * sizeof(float), s, b, e, attn_norm0, d);
+void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, int spk_t,
+                  const float* spk_row, cudaStream_t s) {
+    launch_pdl(embed_kernel, dim3(T), dim3(1024), (d.n_embd + 32) * sizeof(float), s, b, e, attn_norm0, d, spk_t,
+               spk_row);
+}
+
+void launch_spk_proj(const float* lda_w, const float* lda_b, const float* proj_w, const float* proj_b, const float* spk,
+                     const float* delta, int spk_dim, int lda_dim, int n_embd, float* row, cudaStream_t s) {
+    launch_pdl(spk_proj_kernel, dim3(1), dim3(1024), (size_t)lda_dim * sizeof(float), s, lda_w, lda_b, proj_w, proj_b,
+               spk, delta, spk_dim, lda_dim, n_embd, row);
 }
 
 void launch_moe_combine(const StepBufs& b, const LayerSmall& ly, const float* next_norm, const float* out_norm,

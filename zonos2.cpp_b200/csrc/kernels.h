@@ -160,7 +160,12 @@ struct EmbedDev {
 };
 
 void launch_pack(const StepBufs& b, int T, int n_out, cudaStream_t s);
-void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, cudaStream_t s);
+// spk_t >= 0: token spk_t's embedding sum is replaced by spk_row (speaker injection).
+void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0, const Dims& d, int T, int spk_t,
+                  const float* spk_row, cudaStream_t s);
+// row = W_proj (W_lda spk + b_lda) + b_proj (+ delta), f32 (src/zonos2-graph.cpp:262-275).
+void launch_spk_proj(const float* lda_w, const float* lda_b, const float* proj_w, const float* proj_b, const float* spk,
+                     const float* delta, int spk_dim, int lda_dim, int n_embd, float* row, cudaStream_t s);
 void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T, cudaStream_t s);
 void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys, int max_split, cudaStream_t s);
 void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s);

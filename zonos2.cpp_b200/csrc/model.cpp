@@ -164,7 +164,20 @@ struct Loader {
         m->emb.text = up_raw(te);
         if (!m->emb.text) return false;
         m->emb_row_bytes = m->emb.row_bytes;
-        if (!req("spk_lda.weight") || !req("spk_lda.bias") || !req("spk_proj.weight") || !req("spk_proj.bias")) return false;
+        {
+            const int64_t sd = hp.spk_dim, ld = hp.spk_lda_dim;
+            if (sd < 1 || ld < 1 || sd > 8192 || ld > 1024) return fail(Z2B_ERR_UNSUPPORTED, "speaker dims out of range");
+            const GTensor* lw = req("spk_lda.weight");
+            const GTensor* pw = req("spk_proj.weight");
+            if (!lw || !pw) return false;
+            if (lw->ne[0] != sd || lw->ne[1] != ld || pw->ne[0] != ld || pw->ne[1] != d)
+                return fail(Z2B_ERR_FORMAT, "speaker projection shapes");
+            m->spk_lda_w = small(req("spk_lda.weight"), sd * ld);
+            m->spk_lda_b = small(req("spk_lda.bias"), ld);
+            m->spk_proj_w = small(req("spk_proj.weight"), ld * d);
+            m->spk_proj_b = small(req("spk_proj.bias"), d);
+            if (!m->spk_lda_w || !m->spk_lda_b || !m->spk_proj_w || !m->spk_proj_b) return false;
+        }
         m->out_norm = small(req("output_norm.weight"), d);
         if (!m->out_norm) return false;
         const int64_t nout = (int64_t)hp.n_codebooks * hp.audio_vocab;

@@ -30,6 +30,11 @@ struct Model {
     std::vector<void*> allocs;            // every cudaMalloc of the model
     DevMat head;
     const float* out_norm = nullptr;
+    // speaker injection (src/zonos2-graph.cpp:262-292): lda [lda_dim][spk_dim], proj [n_embd][lda_dim], f32
+    const float* spk_lda_w = nullptr;
+    const float* spk_lda_b = nullptr;
+    const float* spk_proj_w = nullptr;
+    const float* spk_proj_b = nullptr;
     std::vector<LayerDev> layers;
     uint64_t attn_bytes_per_layer = 0;    // GGUF bytes of the attention matrices (all layers equal)
     uint64_t head_bytes = 0, router_bytes_per_layer = 0;

@@ -35,6 +35,7 @@ Ctx::~Ctx() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     if (d_canon_all) cudaFree(d_canon_all);
     if (h_canon_all) cudaFreeHost(h_canon_all);
+    if (d_spk) cudaFree(d_spk);
     if (d_sched_descs) cudaFree(d_sched_descs);
     if (d_sched_src) cudaFree(d_sched_src);
     if (d_sched_rows) cudaFree(d_sched_rows);
@@ -310,7 +311,12 @@ void enqueue_step(Ctx* c, int T, int n_out) {
     B.n_desc = c->cur_n_desc;
     c->launches = 0;
     { ProfScope ps(c, PC_PACK); launch_pack(B, T, n_out, c->stream); c->launches++; }
-    { ProfScope ps(c, PC_EMBED); launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->stream); c->launches++; }
+    {
+        ProfScope ps(c, PC_EMBED);
+        const float* spk_row = c->d_spk ? c->d_spk + m->hp.spk_dim + D.n_embd : nullptr;
+        launch_embed(B, m->emb, m->layers[0].small.attn_norm, D, T, c->spk_t, spk_row, c->stream);
+        c->launches++;
+    }
     const int hd = D.head_dim, nh = D.n_head, nkv = D.n_head_kv;
     bool first_moe = true;
     for (int L = 0; L < D.n_layer; ++L) {
@@ -358,7 +364,7 @@ void enqueue_step(Ctx* c, int T, int n_out) {
 
 int run_step(Ctx* c, int T, int n_out) {
     // graphs for decode-only shapes (T == streams); steps carrying prompt rows run eagerly
-    const bool use_graph = c->graphs_enabled && !c->profiling && T == c->cur_n_desc;
+    const bool use_graph = c->graphs_enabled && !c->profiling && T == c->cur_n_desc && c->spk_t < 0;
     if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
     const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48);
     auto it = c->graphs.find(key);
@@ -526,6 +532,34 @@ int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits)
         const bool last = off + nn == n0;
         z2b_slot_desc d{slot, off, nn, last ? Z2B_WANT_LOGITS : 0, -1, 1.0f};
         const int rc = ctx_step(c, &d, 1, ids + (size_t)off * NCOL, nullptr, last ? out_logits : nullptr);
+        if (rc) return rc;
+    }
+    return Z2B_OK;
+}
+
+int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
+                    float* out_logits) {
+    if (!spk) return ctx_prefill(c, slot, ids, n0, out_logits);
+    if (n0 < 1 || n0 > c->slot_cap) { set_error("prefill n0 out of range"); return Z2B_ERR_ARG; }
+    if (spk_pos < 0 || spk_pos >= n0) { set_error("spk_pos outside the prompt rows"); return Z2B_ERR_ARG; }
+    const Model* m = c->m;
+    const int sd = (int)m->hp.spk_dim, ld = (int)m->hp.spk_lda_dim, d = m->dims.n_embd;
+    if (!c->d_spk) CK(cudaMalloc(&c->d_spk, ((size_t)sd + 2 * (size_t)d) * sizeof(float)));
+    float* d_in = c->d_spk;
+    float* d_delta = c->d_spk + sd;
+    float* d_row = c->d_spk + sd + d;
+    CK(cudaMemcpyAsync(d_in, spk, (size_t)sd * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (delta) CK(cudaMemcpyAsync(d_delta, delta, (size_t)d * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    launch_spk_proj(m->spk_lda_w, m->spk_lda_b, m->spk_proj_w, m->spk_proj_b, d_in, delta ? d_delta : nullptr, sd, ld,
+                    d, d_row, c->stream);
+    const int chunk = c->T_max;
+    for (int off = 0; off < n0; off += chunk) {
+        const int nn = std::min(chunk, n0 - off);
+        const bool last = off + nn == n0;
+        z2b_slot_desc dsc{slot, off, nn, last ? Z2B_WANT_LOGITS : 0, -1, 1.0f};
+        c->spk_t = (spk_pos >= off && spk_pos < off + nn) ? spk_pos - off : -1;
+        const int rc = ctx_step(c, &dsc, 1, ids + (size_t)off * NCOL, nullptr, last ? out_logits : nullptr);
+        c->spk_t = -1;
         if (rc) return rc;
     }
     return Z2B_OK;

@@ -52,6 +52,10 @@ struct Ctx {
     int last_T = 0;                          // tokens of the last z2b_step
     size_t last_h2d = 0, last_d2h = 0;       // bytes copied by the last z2b_step
     bool keep_logits = true;                 // read logits back even without out_logits
+    // speaker injection: token of the current step whose embedding is replaced (-1: none),
+    // and a device buffer [spk_dim (input) | n_embd (delta) | n_embd (row)]
+    int spk_t = -1;
+    float* d_spk = nullptr;
     // graphs keyed by (n_desc, T, n_out)
     bool graphs_enabled = true;
     std::map<uint64_t, cudaGraphExec_t> graphs;
@@ -88,6 +92,10 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out);
 int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp);
 int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes, float* out_logits);
 int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits);
+// Prefill with an optional speaker embedding replacing the embedding of prompt row spk_pos
+// (and an optional emotion delta added to the projected speaker row).
+int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
+                    float* out_logits);
 int ctx_decode_loop(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* first_ids, int n_steps);
 int ctx_sync(Ctx* c);
 void enqueue_step(Ctx* c, int T, int n_out);

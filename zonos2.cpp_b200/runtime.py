@@ -75,6 +75,7 @@ def lib():
             "z2b_ctx_destroy": ([P], I),
             "z2b_slot_reset": ([P, I, ctypes.POINTER(Sampling)], I),
             "z2b_slot_prefill": ([P, I, V, I, V], I),
+            "z2b_slot_prefill_spk": ([P, I, V, I, V, I, V, V], I),
             "z2b_step": ([P, V, I, V, V, V], I),
             "z2b_step_logits": ([P, I], ctypes.POINTER(ctypes.c_float)),
             "z2b_decode_loop": ([P, V, I, V, I], I),
@@ -185,11 +186,19 @@ class BatchCtx:
     def slot_reset(self, slot: int, sampling: Sampling | None = None):
         _check(lib().z2b_slot_reset(self.h, slot, ctypes.byref(sampling) if sampling else None))
 
-    def slot_prefill(self, slot: int, ids) -> np.ndarray:
-        """zonos2_batch_slot_prefill: returns the last prompt row's logits [ncb, av]."""
+    def slot_prefill(self, slot: int, ids, spk=None, spk_pos: int = 0, spk_emotion_delta=None) -> np.ndarray:
+        """zonos2_batch_slot_prefill: returns the last prompt row's logits [ncb, av]. With
+        spk ([spk_dim] f32), row spk_pos's embedding is replaced by the projected speaker
+        (+ spk_emotion_delta, [n_embd] f32, when given)."""
         ids = np.ascontiguousarray(ids, np.int32).reshape(-1, NCOL)
         out = np.empty((self.ncb, self.av), np.float32)
-        _check(lib().z2b_slot_prefill(self.h, slot, _ptr(ids), ids.shape[0], _ptr(out)))
+        if spk is None:
+            _check(lib().z2b_slot_prefill(self.h, slot, _ptr(ids), ids.shape[0], _ptr(out)))
+        else:
+            spk = np.ascontiguousarray(spk, np.float32)
+            delta = None if spk_emotion_delta is None else np.ascontiguousarray(spk_emotion_delta, np.float32)
+            _check(lib().z2b_slot_prefill_spk(self.h, slot, _ptr(ids), ids.shape[0], _ptr(spk), int(spk_pos),
+                                              _ptr(out), _ptr(delta) if delta is not None else None))
         return out
 
     def step(self, descs, ids, want_logits=True):
