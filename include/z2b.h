@@ -102,6 +102,14 @@ int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* 
 int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos,
                          float* out_logits, const float* spk_emotion_delta);
 
+/* Teacher-forced logits of one sequence: ids[n_tokens][10] run from position 0 through
+ * the decode kernels on a private single-slot context, and out_logits[n_tokens][n_codebooks]
+ * [audio_vocab] receives every row's logits (row t after rows 0..t). spk / spk_pos /
+ * spk_emotion_delta as z2b_slot_prefill_spk (spk NULL: none). Replaces zonos2_logits
+ * (src/zonos2.h:156-158, src/zonos2-graph.cpp:457-473), the quality evals' entry point. */
+int z2b_logits(z2b_model* model, const int32_t* ids, int n_tokens, float* out_logits, const float* spk, int spk_pos,
+               const float* spk_emotion_delta);
+
 /* One batched step over n streams: rows ids[sum(n_new)][10] are fed in desc order
  * (decode streams feed one row; prompt chunks may be mixed in). For each desc with
  * Z2B_WANT_SAMPLE, out_codes[i*n_codebooks ..] receives the sampled frame; with

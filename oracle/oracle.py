@@ -69,6 +69,7 @@ def lib():
         L.o_model_set_spk.argtypes = [P, V]
         L.o_spk_row.argtypes = [P, V, V, V]
         L.o_prefill_spk.argtypes = [P, I, V, I, V, I, V, V]
+        L.o_logits.argtypes = [P, V, I, V, I, V, V]
         L.o_step.argtypes = [P, V, V, V, I, V]
         L.o_last_sel.argtypes = [P, V, I]
         L.o_ctx_fake_fill.argtypes = [P, I, I, ctypes.c_uint32]
@@ -143,6 +144,18 @@ class Model:
 
     def set_mode(self, mode: int):
         lib().o_model_set_mode(self.h, mode)
+
+    def logits(self, ids, spk=None, spk_pos: int = 0, spk_emotion_delta=None) -> np.ndarray:
+        """zonos2_logits: every row's logits [n, ncb, av] of one sequence from position 0."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        n = ids.shape[0]
+        out = np.empty((n, self.hp.n_codebooks, self.hp.audio_vocab), np.float32)
+        sp = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        dl = None if spk_emotion_delta is None else np.ascontiguousarray(spk_emotion_delta, np.float32)
+        rc = lib().o_logits(self.h, _ptr(ids), n, _ptr(sp) if sp is not None else None, int(spk_pos),
+                            _ptr(dl) if dl is not None else None, _ptr(out))
+        assert rc == 0
+        return out
 
     def spk_row(self, spk, delta=None) -> np.ndarray:
         """The projected speaker row [n_embd] that replaces a prompt row's embedding."""

@@ -716,6 +716,27 @@ int o_prefill_spk(void* ctx, int slot, const int32_t* ids, int n0, const float* 
     return 0;
 }
 
+// zonos2_logits: every row's logits of one sequence from position 0, [n][ncb*av]
+// (src/zonos2-graph.cpp:457-473), with the optional speaker row as o_prefill_spk.
+int o_logits(void* model, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta,
+             float* out_logits) {
+    OModel* M = (OModel*)model;
+    if (n < 1 || (spk && (spk_pos < 0 || spk_pos >= n))) return 1;
+    std::vector<float> row;
+    if (spk) {
+        row.resize((size_t)M->hp.n_embd);
+        if (o_spk_row(M, spk, delta, row.data())) return 1;
+    }
+    OCtx* c = (OCtx*)o_ctx_new(M, 1, n);
+    std::vector<int> slots(n, 0), pos(n);
+    std::vector<char> want(n, 1);
+    for (int i = 0; i < n; ++i) pos[i] = i;
+    forward(c, ids, n, slots.data(), pos.data(), true, want.data(), out_logits, spk ? row.data() : nullptr,
+            spk ? spk_pos : -1);
+    o_ctx_free(c);
+    return 0;
+}
+
 // zonos2_batch_step for n active slots: slot[i] at position n_past[i] fed ids[i] -> logits [n][ncb*av]
 int o_step(void* ctx, const int32_t* slots, const int32_t* n_past, const int32_t* ids, int n, float* out_logits) {
     OCtx* c = (OCtx*)ctx;

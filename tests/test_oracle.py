@@ -115,3 +115,13 @@ def test_speaker_replaces_the_row(om):
     assert not np.array_equal(a, plain)
     e = O.Ctx(om, 1, 64).prefill(0, p, spk=spk, spk_pos=2, spk_emotion_delta=delta)
     assert not np.array_equal(a, e)
+
+
+def test_teacher_forced_logits_last_row_is_the_prefill(om):
+    """zonos2_logits restated: row t of the all-rows forward equals a prefill of rows 0..t."""
+    p = prompt(9, 6)
+    spk, _ = _spk_inputs(om, 13)
+    all_rows = om.logits(p, spk=spk, spk_pos=0)
+    assert all_rows.shape == (9, om.hp.n_codebooks, om.hp.audio_vocab)
+    assert np.array_equal(all_rows[-1], O.Ctx(om, 1, 64).prefill(0, p, spk=spk, spk_pos=0))
+    assert np.array_equal(all_rows[4], O.Ctx(om, 1, 64).prefill(0, p[:5], spk=spk, spk_pos=0))

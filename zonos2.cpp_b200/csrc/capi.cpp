@@ -100,6 +100,13 @@ int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, con
     return ctx_prefill_spk(ctx->c, slot, ids, n0, spk, spk_pos, spk_emotion_delta, out_logits);
 }
 
+int z2b_logits(z2b_model* model, const int32_t* ids, int n_tokens, float* out_logits, const float* spk, int spk_pos,
+               const float* spk_emotion_delta) {
+    if (!model || !ids || !out_logits) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(model->m->device);
+    return model_logits(model->m, ids, n_tokens, spk, spk_pos, spk_emotion_delta, out_logits);
+}
+
 int z2b_step(z2b_ctx* ctx, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes,
              float* out_logits) {
     if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }

@@ -22,9 +22,12 @@ __global__ void pack_kernel(const StepBufs b, int T) {
     __shared__ int s_start[1024], s_out[1024];
     const int n = b.n_desc, tid = threadIdx.x;
     if (tid == 0) *b.err = 0;          // first kernel of a step: clear the error word
+    auto n_out_of = [](const SlotDesc& d) {
+        return (d.flags & SD_OUTPUT) ? ((d.flags & SD_ALL_ROWS) ? d.n_new : 1) : 0;
+    };
     if (tid < n) {
         s_start[tid] = b.descs[tid].n_new;
-        s_out[tid] = (b.descs[tid].flags & SD_OUTPUT) ? 1 : 0;
+        s_out[tid] = n_out_of(b.descs[tid]);
     }
     __syncthreads();
     // Hillis-Steele inclusive scans (n <= 1024)
@@ -38,7 +41,9 @@ __global__ void pack_kernel(const StepBufs b, int T) {
     for (int i = tid; i < n; i += blockDim.x) {
         const SlotDesc d = b.descs[i];
         const int start = s_start[i] - d.n_new;
-        const int orow = (d.flags & SD_OUTPUT) ? s_out[i] - 1 : -1;
+        const bool all = (d.flags & SD_ALL_ROWS) != 0;
+        const int orow = (d.flags & SD_OUTPUT) ? s_out[i] - 1 : -1;    // the desc's last row
+        const int obase = orow >= 0 ? s_out[i] - n_out_of(d) : -1;
         b.desc_out[i] = orow;
         for (int r = 0; r < d.n_new; ++r) {
             const int t = start + r;
@@ -46,10 +51,11 @@ __global__ void pack_kernel(const StepBufs b, int T) {
             b.tok_slot[t] = d.slot;
             b.tok_pos[t] = d.n_past + r;
             b.tok_desc[t] = i;
-            b.tok_out[t] = (r == d.n_new - 1) ? orow : -1;
+            b.tok_out[t] = orow < 0 ? -1 : (all ? obase + r : (r == d.n_new - 1 ? orow : -1));
             for (int c = 0; c < NCOL; ++c) b.ids[t * NCOL + c] = b.ids_in[t * NCOL + c];
         }
-        if (orow >= 0) { b.out_tok[orow] = start + d.n_new - 1; b.out_desc[orow] = i; }
+        if (orow >= 0)
+            for (int o = obase; o <= orow; ++o) { b.out_tok[o] = start + d.n_new - 1 - (orow - o); b.out_desc[o] = i; }
     }
 }
 

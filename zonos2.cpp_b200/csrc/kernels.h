@@ -90,7 +90,7 @@ struct SlotDesc {
     int samp;        // index into the per-slot sampling table (= slot)
     int pad_;
 };
-enum SlotFlags { SD_OUTPUT = 1, SD_SAMPLE = 2 };
+enum SlotFlags { SD_OUTPUT = 1, SD_SAMPLE = 2, SD_ALL_ROWS = 4 };   // SD_ALL_ROWS: every row is an output row
 
 // Sampling parameters per slot, device copy (mirrors zonos2_sampling).
 struct SampDev {

@@ -8,6 +8,7 @@
 #include "runtime.h"
 
 #include <algorithm>
+#include <memory>
 #include <cstring>
 #include <random>
 
@@ -45,7 +46,7 @@ Ctx::~Ctx() {
     if (stream) cudaStreamDestroy(stream);
 }
 
-int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
+int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_rows) {
     if (n_slots < 1 || n_slots > 1024 || slot_cap_frames < 1) { set_error("bad n_slots / slot_cap"); return Z2B_ERR_ARG; }
     std::unique_ptr<Ctx> c(new Ctx());
     c->m = m;
@@ -58,7 +59,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out) {
     // rows per step: every slot decoding plus 4096 prompt rows admitted in the same step
     // (eight 512-row prompts, or one 4096-token expert-op batch), at most 8192
     c->T_max = std::min(8192, std::max(512, n_slots + 4096));
-    c->O_max = n_slots;
+    c->O_max = std::max(n_slots, std::min(out_rows, c->T_max));
     c->D_max = std::min(1024, c->T_max);
     c->kmax = 1;
     for (auto& ly : m->layers) c->kmax = std::max(c->kmax, ly.top_k);
@@ -401,7 +402,7 @@ int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_de
         if (d.n_past + d.n_new + extra_rows_per_desc > c->slot_cap) { set_error("stream exceeds slot capacity"); return Z2B_ERR_ARG; }
         if (d.cfg_twin >= n || d.cfg_twin == i) { set_error("bad cfg_twin"); return Z2B_ERR_ARG; }
         T += d.n_new;
-        if (d.flags & Z2B_WANT_LOGITS) ++n_out;
+        if (d.flags & Z2B_WANT_LOGITS) n_out += c->all_rows ? d.n_new : 1;
     }
     if (T > c->T_max) { set_error("rows per step exceed capacity (" + std::to_string(c->T_max) + ")"); return Z2B_ERR_ARG; }
     if (n_out > c->O_max) { set_error("too many output rows"); return Z2B_ERR_ARG; }
@@ -426,9 +427,12 @@ int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_de
         SlotDesc s{};
         s.slot = d.slot; s.n_past = d.n_past; s.n_new = d.n_new;
         s.flags = ((d.flags & Z2B_WANT_LOGITS) ? SD_OUTPUT : 0) | (((d.flags & Z2B_WANT_SAMPLE) == Z2B_WANT_SAMPLE) ? SD_SAMPLE : 0);
+        if (c->all_rows && (s.flags & SD_OUTPUT)) s.flags |= SD_ALL_ROWS;
         s.twin = d.cfg_twin; s.cfg_scale = d.cfg_scale; s.samp = d.slot;
         sd[i] = s;
-        c->desc_out_host[i] = (s.flags & SD_OUTPUT) ? o++ : -1;
+        const int rows = (s.flags & SD_OUTPUT) ? ((s.flags & SD_ALL_ROWS) ? d.n_new : 1) : 0;
+        c->desc_out_host[i] = rows ? o + rows - 1 : -1;                // the desc's last row
+        o += rows;
     }
     (void)D;
     c->cur_n_desc = n;
@@ -537,11 +541,10 @@ int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits)
     return Z2B_OK;
 }
 
-int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
-                    float* out_logits) {
-    if (!spk) return ctx_prefill(c, slot, ids, n0, out_logits);
-    if (n0 < 1 || n0 > c->slot_cap) { set_error("prefill n0 out of range"); return Z2B_ERR_ARG; }
-    if (spk_pos < 0 || spk_pos >= n0) { set_error("spk_pos outside the prompt rows"); return Z2B_ERR_ARG; }
+namespace {
+
+// The projected speaker row (+ delta) into the context's speaker buffer, on its stream.
+int spk_prepare(Ctx* c, const float* spk, const float* delta) {
     const Model* m = c->m;
     const int sd = (int)m->hp.spk_dim, ld = (int)m->hp.spk_lda_dim, d = m->dims.n_embd;
     if (!c->d_spk) CK(cudaMalloc(&c->d_spk, ((size_t)sd + 2 * (size_t)d) * sizeof(float)));
@@ -552,6 +555,18 @@ int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* s
     if (delta) CK(cudaMemcpyAsync(d_delta, delta, (size_t)d * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     launch_spk_proj(m->spk_lda_w, m->spk_lda_b, m->spk_proj_w, m->spk_proj_b, d_in, delta ? d_delta : nullptr, sd, ld,
                     d, d_row, c->stream);
+    return Z2B_OK;
+}
+
+}  // namespace
+
+int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
+                    float* out_logits) {
+    if (!spk) return ctx_prefill(c, slot, ids, n0, out_logits);
+    if (n0 < 1 || n0 > c->slot_cap) { set_error("prefill n0 out of range"); return Z2B_ERR_ARG; }
+    if (spk_pos < 0 || spk_pos >= n0) { set_error("spk_pos outside the prompt rows"); return Z2B_ERR_ARG; }
+    const int src = spk_prepare(c, spk, delta);
+    if (src) return src;
     const int chunk = c->T_max;
     for (int off = 0; off < n0; off += chunk) {
         const int nn = std::min(chunk, n0 - off);
@@ -561,6 +576,33 @@ int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* s
         const int rc = ctx_step(c, &dsc, 1, ids + (size_t)off * NCOL, nullptr, last ? out_logits : nullptr);
         c->spk_t = -1;
         if (rc) return rc;
+    }
+    return Z2B_OK;
+}
+
+int model_logits(Model* m, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta, float* out) {
+    if (!ids || !out || n < 1) { set_error("logits: bad arguments"); return Z2B_ERR_ARG; }
+    if (spk && (spk_pos < 0 || spk_pos >= n)) { set_error("spk_pos outside the rows"); return Z2B_ERR_ARG; }
+    constexpr int kRowsPerStep = 512;
+    Ctx* c = nullptr;
+    int rc = ctx_create(m, 1, n, &c, std::min(n, kRowsPerStep));
+    if (rc) return rc;
+    std::unique_ptr<Ctx> own(c);
+    rc = ctx_slot_reset(c, 0, nullptr);
+    if (rc) return rc;
+    if (spk && (rc = spk_prepare(c, spk, delta))) return rc;
+    c->all_rows = true;
+    c->keep_logits = true;
+    const size_t per = (size_t)m->dims.n_codebooks * m->dims.audio_vocab;
+    const int step = std::min(c->T_max, c->O_max);
+    for (int off = 0; off < n; off += step) {
+        const int nn = std::min(step, n - off);
+        z2b_slot_desc dsc{0, off, nn, Z2B_WANT_LOGITS, -1, 1.0f};
+        c->spk_t = (spk && spk_pos >= off && spk_pos < off + nn) ? spk_pos - off : -1;
+        rc = ctx_step(c, &dsc, 1, ids + (size_t)off * NCOL, nullptr, nullptr);
+        c->spk_t = -1;
+        if (rc) return rc;
+        std::memcpy(out + (size_t)off * per, c->h_logits, (size_t)nn * per * sizeof(float));
     }
     return Z2B_OK;
 }

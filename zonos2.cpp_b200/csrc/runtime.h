@@ -55,6 +55,8 @@ struct Ctx {
     // speaker injection: token of the current step whose embedding is replaced (-1: none),
     // and a device buffer [spk_dim (input) | n_embd (delta) | n_embd (row)]
     int spk_t = -1;
+    // every row of a Z2B_WANT_LOGITS desc is an output row (teacher-forced logits)
+    bool all_rows = false;
     float* d_spk = nullptr;
     // graphs keyed by (n_desc, T, n_out)
     bool graphs_enabled = true;
@@ -88,7 +90,10 @@ struct Ctx {
 
 void set_error(const std::string& e);
 const char* last_error();
-int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out);
+// out_rows: output (logits) rows per step, at least n_slots.
+int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_rows = 0);
+// Teacher-forced logits of every row of one sequence (zonos2_logits): out [n][ncb][av].
+int model_logits(Model* m, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta, float* out);
 int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp);
 int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes, float* out_logits);
 int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits);

@@ -76,6 +76,7 @@ def lib():
             "z2b_slot_reset": ([P, I, ctypes.POINTER(Sampling)], I),
             "z2b_slot_prefill": ([P, I, V, I, V], I),
             "z2b_slot_prefill_spk": ([P, I, V, I, V, I, V, V], I),
+            "z2b_logits": ([P, V, I, V, V, I, V], I),
             "z2b_step": ([P, V, I, V, V, V], I),
             "z2b_step_logits": ([P, I], ctypes.POINTER(ctypes.c_float)),
             "z2b_decode_loop": ([P, V, I, V, I], I),
@@ -135,6 +136,16 @@ class Model:
         offs = np.array(offs, np.int32)
         ids = np.array(ids or [0], np.int32)
         _check(lib().z2b_set_expert_mask(self.h, _ptr(layers), len(layers), _ptr(offs), _ptr(ids)))
+
+    def logits(self, ids, spk=None, spk_pos: int = 0, spk_emotion_delta=None) -> np.ndarray:
+        """zonos2_logits: teacher-forced logits [n, ncb, av] of every row of one sequence."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(-1, NCOL)
+        n = ids.shape[0]
+        out = np.empty((n, self.hp.n_codebooks, self.hp.audio_vocab), np.float32)
+        sp = None if spk is None else np.ascontiguousarray(spk, np.float32)
+        dl = None if spk_emotion_delta is None else np.ascontiguousarray(spk_emotion_delta, np.float32)
+        _check(lib().z2b_logits(self.h, _ptr(ids), n, _ptr(out), _ptr(sp), int(spk_pos), _ptr(dl)))
+        return out
 
     def close(self):
         if self.h:
