@@ -48,6 +48,14 @@ int z2b_host_repack(uint32_t type, int64_t rows, int64_t k, const void* src, voi
 /* Decode a tile-layout buffer back to f32 rows [rows][k] on the host (layout check). */
 int z2b_host_unpack_tiles(uint32_t type, int64_t rows, int64_t k, const void* tiles, float* out);
 
+/* Host-only: the tile GEMV's launch geometry for a weight type, K, matrices per item
+ * (1, or 2 for gate/up) and token tiles per pass (ntg 2 for projections and gate/up, 1
+ * for the down pass). out[0..6] = warps, ring stages, stage bytes, dynamic shared bytes,
+ * chunks per stage, bytes per token row of a warp's shared activation slice (0 when the
+ * activations are read into registers directly), chunks per warp. Returns 7 for an
+ * unsupported type / K. */
+int z2b_test_gemv_geometry(uint32_t type, int64_t k, int nmat, int ntg, int32_t* out);
+
 /* Device checks (libz2b.so, need a GPU). z2b_test_dequant decodes `rows` GGUF rows of
  * type/k on the device to f32 [rows][k], either from the tile image the GEMV reads
  * (from_tiles = 1) or straight from GGUF rows as the embedding gather does (0), with

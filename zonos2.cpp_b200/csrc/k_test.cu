@@ -135,6 +135,19 @@ done:
     return rc;
 }
 
+extern "C" int z2b_test_gemv_geometry(uint32_t type, int64_t k, int nmat, int ntg, int32_t* out) {
+    using namespace z2b;
+    TileGeom g{};
+    if (!out || nmat < 1 || nmat > 2 || ntg < 1 || ntg > 2 || !tile_geom(type, k, &g)) return 7;
+    DevMat m{};
+    m.type = type; m.K = (int)k; m.chunks = (int)g.chunks; m.tile_bytes = g.tile_bytes; m.steps = g.steps;
+    int nw = 0, ns = 0, sb = 0, smem = 0, cps = 0, xrs = 0;
+    gemv_geometry(m, nmat, ntg, &nw, &ns, &sb, &smem, &cps, &xrs);
+    out[0] = nw; out[1] = ns; out[2] = sb; out[3] = smem; out[4] = cps; out[5] = xrs;
+    out[6] = (m.chunks + nw - 1) / nw;
+    return 0;
+}
+
 extern "C" int z2b_test_gemv(uint32_t type, int64_t rows, int64_t k, const void* gguf_rows, const uint16_t* x_f16,
                              int n_tok, float* out) {
     int rc = 0;
