@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the batched MoE backbone decode step.
+"""Benchmark of the batched MoE backbone decode step (config 2, the headline workload).
 
 Workload (synthetic, seeded; no dataset): the ZONOS2-scale backbone (d 2048, 28 MoE
 layers, 32 experts top-4, ff 1408, 16x128 heads / 4 KV heads, Q4_K attention and expert
