@@ -96,9 +96,10 @@ int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* 
 /* z2b_slot_prefill with the reference's speaker arguments, in its order. spk
  * (float[spk_dim], or NULL for none) is projected as spk_proj(spk_lda(spk)), plus
  * spk_emotion_delta (float[n_embd]) when not NULL, and replaces the embedding of prompt
- * row spk_pos (0 <= spk_pos < n0) before emb_norm. Replaces zonos2_batch_slot_prefill's
- * spk / spk_pos / spk_emotion_delta (src/zonos2.h:286-288, 312-313;
- * src/zonos2-graph.cpp:262-292, 703-760). Z2B_ERR_ARG if spk_pos is outside the prompt. */
+ * row spk_pos (0 <= spk_pos < n0) before emb_norm; a negative spk_pos means no speaker,
+ * as in the reference. Replaces zonos2_batch_slot_prefill's spk / spk_pos /
+ * spk_emotion_delta (src/zonos2.h:286-288, 312-313; src/zonos2-graph.cpp:36-37, 262-292,
+ * 703-760). Z2B_ERR_ARG if spk_pos >= n0. */
 int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos,
                          float* out_logits, const float* spk_emotion_delta);
 
@@ -187,6 +188,28 @@ int z2b_time_expert_gemv(z2b_ctx* ctx, int which, int reps, double* ms_per_launc
  * No reference counterpart (the reference's expert op is ggml_mul_mat_id inside its graph). */
 int z2b_expert_op(z2b_ctx* ctx, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k,
                   float* out, int reps, double* ms, uint64_t* weight_bytes, int32_t* n_gemm_experts);
+
+/* A stream's graph-facing state between steps (zonos2_slot, src/zonos2.h:263-274); the
+ * caller owns it, as in the reference. */
+#define Z2B_MAX_ROW 32                 /* n_codebooks + 1 input columns at most */
+typedef struct z2b_slot_state {
+    int32_t index;                     /* cache band / column */
+    int32_t done;                      /* finished: EOS countdown elapsed, max_frames, or stopped */
+    int32_t n_past;                    /* position of the next row (advanced by the caller per step) */
+    int32_t step;                      /* frames sampled so far (frame index of the next sample) */
+    int32_t eos_frame;                 /* -1 until an end-of-audio code is seen */
+    int32_t countdown;                 /* frames left after EOS, -1 before */
+    int32_t next_ids[Z2B_MAX_ROW];     /* next input row: the frame's codes + the text pad */
+} z2b_slot_state;
+
+/* Per-frame bookkeeping of zonos2_slot_sample (src/zonos2-graph.cpp:843-870) after the
+ * frame codes[n_codebooks] was sampled (z2b_step with Z2B_WANT_SAMPLE): the first frame
+ * holding eoa_id in any codebook sets eos_frame = max(0, step - last such codebook) and a
+ * countdown of n_codebooks + 1 frames; next_ids = codes + text pad (text_vocab); step + 1;
+ * done when the countdown elapses, step reaches max_frames, or keep == 0 (keep: the
+ * on_frame callback's verdict, 1 when there is none). Host only; returns keep, or -1 for a
+ * bad argument. */
+int z2b_slot_after_frame(const z2b_hparams* hp, z2b_slot_state* s, const int32_t* codes, int max_frames, int keep);
 
 const char* z2b_last_error(void);
 

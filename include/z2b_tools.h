@@ -86,12 +86,15 @@ int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, i
 #define Z2B_NOALLOC_MAX_ROUTES 16384
 /* No reference counterpart. The segment builder of z2b_test_route (same arguments, same
  * results) without any device allocation: it works in a fixed scratch array compiled
- * into the library, for callers that may not call cudaMalloc/cudaFree (they synchronise
- * the device, and are refused while a stream is being captured into a CUDA graph).
- * Runs on the current device; the first call on each device looks up the scratch
- * address, so make it before any stream capture begins. Calls that overlap in time
- * share the scratch and race: serialise them. T * k > Z2B_NOALLOC_MAX_ROUTES returns
- * Z2B_ERR_ARG with z2b_last_error() naming the limit. */
+ * into the library (every GPU that loads the library holds it until exit). It is for
+ * callers that may not call cudaMalloc/cudaFree: a server that gave all but a fixed
+ * budget of the GPU to its KV page pool, or a latency-critical thread, since allocation
+ * can synchronise the whole device and stall decode steps queued by other threads.
+ * Runs on the current device and the calling thread's per-thread default stream, and
+ * returns when the results are in the host arrays. The first call on each device looks
+ * up the scratch address (set-up), so make it before any stream capture begins. Calls
+ * that overlap on the GPU share the scratch and race: serialise them. T * k >
+ * Z2B_NOALLOC_MAX_ROUTES returns Z2B_ERR_ARG with z2b_last_error() naming the limit. */
 int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
                                int32_t* route_tok, int32_t* route_pos);
 
@@ -99,6 +102,20 @@ int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int
  * large enough; returns the number of entries (or -1). */
 struct z2b_ctx;
 int z2b_debug_last_sel(struct z2b_ctx* ctx, int32_t* out, int cap);
+
+/* Test support, no reference counterpart (need a GPU).
+ * z2b_debug_fill_kv: positions [0, n) of `slot` get KV pages from the context's pool
+ * holding, in every layer, k / 1024 (k in [-2048, 2048), exact in f16) from a splitmix64
+ * hash of (seed, layer, K or V, position, kv head, dim): the values the CPU oracle's
+ * hash fill writes, so decode over long contexts can be checked without a prefill.
+ * Decode steps then continue from n_past = n.
+ * z2b_debug_router_capture: with enable = 1 the following steps run without graphs and
+ * record, before every MoE layer's router, the residual rows [T][n_embd] and the
+ * incoming router state [T][router_dim]; z2b_debug_router_inputs copies layer `layer`'s
+ * record of the last step into res / state (either may be NULL) and its T into *T. */
+int z2b_debug_fill_kv(struct z2b_ctx* ctx, int slot, int n, uint32_t seed);
+int z2b_debug_router_capture(struct z2b_ctx* ctx, int enable);
+int z2b_debug_router_inputs(struct z2b_ctx* ctx, int layer, float* res, float* state, int* T);
 
 #ifdef __cplusplus
 }

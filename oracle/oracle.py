@@ -73,6 +73,8 @@ def lib():
         L.o_step.argtypes = [P, V, V, V, I, V]
         L.o_last_sel.argtypes = [P, V, I]
         L.o_ctx_fake_fill.argtypes = [P, I, I, ctypes.c_uint32]
+        L.o_ctx_hash_fill.argtypes = [P, I, I, ctypes.c_uint32]
+        L.o_router.argtypes = [P, I, V, V, I, V, V, V]
         L.o_dequant.argtypes = [ctypes.c_uint32, V, ctypes.c_int64, V]
         L.o_sampler_new.argtypes = [ctypes.c_float, I, ctypes.c_float, ctypes.c_float, ctypes.c_float, I, I,
                                     ctypes.c_uint32, I, I]
@@ -165,6 +167,23 @@ class Model:
         assert lib().o_spk_row(self.h, _ptr(spk), _ptr(delta) if delta is not None else None, _ptr(out)) == 0
         return out
 
+    def router(self, layer: int, res, state_in=None):
+        """The router of MoE layer `layer` on residual rows res [n, d] (ffn_norm applied
+        inside) and the previous MoE layer's state [n, rd] (None for the first MoE layer):
+        returns (sel [n, k], weights [n, k], new state [n, rd])."""
+        res = np.ascontiguousarray(res, np.float32)
+        n = res.shape[0]
+        k = int(self.expert_used[layer])
+        rd = int(self.t[f"blk.{layer}.router_down.weight"].shape[1])
+        sel = np.empty((n, k), np.int32)
+        w = np.empty((n, k), np.float32)
+        st = np.empty((n, rd), np.float32)
+        si = None if state_in is None else np.ascontiguousarray(state_in, np.float32)
+        rc = lib().o_router(self.h, layer, _ptr(res), _ptr(si) if si is not None else None, n, _ptr(sel), _ptr(w),
+                            _ptr(st))
+        assert rc == 0
+        return sel, w, st
+
     def set_expert_mask(self, keep: dict[int, list[int]]):
         for L in range(self.hp.n_layer):
             if L in keep:
@@ -219,6 +238,10 @@ class Ctx:
 
     def fake_fill(self, slot: int, n: int, seed: int = 0):
         lib().o_ctx_fake_fill(self.h, slot, n, seed)
+
+    def hash_fill(self, slot: int, n: int, seed: int = 0):
+        """KV of positions [0, n) from the integer hash the GPU's z2b_debug_fill_kv uses."""
+        lib().o_ctx_hash_fill(self.h, slot, n, seed)
 
     def __del__(self):
         if getattr(self, "h", None):

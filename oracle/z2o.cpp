@@ -313,6 +313,66 @@ float gelu_erf(float x) { return 0.5f * x * (1.0f + std::erf(x * 0.7071067811865
 float silu(float x) { return x / (1.0f + std::exp(-x)); }
 float sigm(float x) { return 1.0f / (1.0f + std::exp(-x)); }
 
+// The stateful EDA router of one MoE layer (src/zonos2-graph.cpp:199-220) on the
+// ffn-normed rows cur[n][d]: rh = Wd cur + b (+ state * eda_scale when a previous MoE layer
+// left a state), which becomes the state; RMSNorm * router_norm, two erf-GELU layers,
+// logits (+ mask), softmax (double sum), top-k of probs + bias (+ mask) with ties to the
+// lower id; weight = probs[sel] (no renormalisation).
+void router(const OModel& M, const OLayer& ly, const float* cur, int n, std::vector<float>& rstate, bool have_state,
+            std::vector<int>& sel, std::vector<float>& w, std::vector<float>& probs) {
+    const OHp& hp = M.hp;
+    const int mode = M.mode;
+    const int E = (int)ly.uexp.ne2, kk = ly.top_k;
+    const int rd = (int)ly.rdown.ne1;
+    const std::vector<float> rb = small(ly.rdown_b), b0 = small(ly.m0b), b2 = small(ly.m2b), rnw = small(ly.rnorm),
+                             rbias = small(ly.rbias);
+    std::vector<float> eda;
+    if (ly.eda.data) eda = small(ly.eda);
+    std::vector<float> rh((size_t)n * rd), h0((size_t)n * rd), h2((size_t)n * rd), lg((size_t)n * E);
+    matmul(mode, ly.rdown, 0, cur, n, rh.data(), rd);
+    for (int t = 0; t < n; ++t)
+        for (int i = 0; i < rd; ++i) {
+            float vv = rh[(size_t)t * rd + i] + rb[i];
+            if (!eda.empty() && have_state) vv = vv + rstate[(size_t)t * rd + i] * eda[i];
+            rh[(size_t)t * rd + i] = vv;
+        }
+    rstate = rh;
+    std::vector<float> rn((size_t)n * rd);
+    for (int t = 0; t < n; ++t) rms_norm(&rh[(size_t)t * rd], rd, hp.rms_eps, rnw.data(), &rn[(size_t)t * rd]);
+    matmul(mode, ly.m0, 0, rn.data(), n, h0.data(), rd);
+    for (int t = 0; t < n; ++t) for (int i = 0; i < rd; ++i) h0[(size_t)t * rd + i] = gelu_erf(h0[(size_t)t * rd + i] + b0[i]);
+    matmul(mode, ly.m2, 0, h0.data(), n, h2.data(), rd);
+    for (int t = 0; t < n; ++t) for (int i = 0; i < rd; ++i) h2[(size_t)t * rd + i] = gelu_erf(h2[(size_t)t * rd + i] + b2[i]);
+    matmul(mode, ly.m4, 0, h2.data(), n, lg.data(), E);
+    sel.assign((size_t)n * kk, 0);
+    w.assign((size_t)n * kk, 0.0f);
+    probs.assign((size_t)n * E, 0.0f);
+    for (int t = 0; t < n; ++t) {
+        float* p = &probs[(size_t)t * E];
+        for (int e = 0; e < E; ++e) p[e] = lg[(size_t)t * E + e] + (ly.mask.empty() ? 0.0f : ly.mask[e]);
+        float mx = -INFINITY;
+        for (int e = 0; e < E; ++e) mx = std::max(mx, p[e]);
+        double sum = 0.0;
+        for (int e = 0; e < E; ++e) { p[e] = std::exp(p[e] - mx); sum += p[e]; }
+        const float inv = (float)(1.0 / sum);
+        for (int e = 0; e < E; ++e) p[e] = p[e] * inv;
+        // top-k of probs + bias (+ mask); ties to the lower id
+        std::vector<char> taken((size_t)E, 0);
+        for (int j = 0; j < kk; ++j) {
+            int best = -1; float bv = -INFINITY;
+            for (int e = 0; e < E; ++e) {
+                if (taken[e]) continue;
+                float sv = p[e] + rbias[e];
+                if (!ly.mask.empty()) sv = sv + ly.mask[e];
+                if (best < 0 || sv > bv) { bv = sv; best = e; }
+            }
+            taken[best] = 1;
+            sel[(size_t)t * kk + j] = best;
+            w[(size_t)t * kk + j] = p[best];
+        }
+    }
+}
+
 // One forward over `n` tokens. prefill: all tokens belong to `pslot`, positions 0..n-1,
 // self-attention in f32 over these tokens (manual path, :155-169) and K/V written to the
 // cache as f16; decode: token t of slot slots[t] at pos[t] attends the f16 cache [0, pos]
@@ -459,54 +519,10 @@ void forward(OCtx* c, const int32_t* ids, int n, const int* slots, const int* po
         }
         // router (:199-220)
         const int E = (int)ly.uexp.ne2, kk = ly.top_k;
-        const int rd = (int)ly.rdown.ne1;
-        const std::vector<float> rb = small(ly.rdown_b), b0 = small(ly.m0b), b2 = small(ly.m2b), rnw = small(ly.rnorm),
-                                 rbias = small(ly.rbias);
-        std::vector<float> eda;
-        if (ly.eda.data) eda = small(ly.eda);
-        std::vector<float> rh((size_t)n * rd), h0((size_t)n * rd), h2((size_t)n * rd), lg((size_t)n * E);
-        matmul(mode, ly.rdown, 0, cur.data(), n, rh.data(), rd);
-        for (int t = 0; t < n; ++t)
-            for (int i = 0; i < rd; ++i) {
-                float vv = rh[(size_t)t * rd + i] + rb[i];
-                if (!eda.empty() && have_state) vv = vv + rstate[(size_t)t * rd + i] * eda[i];
-                rh[(size_t)t * rd + i] = vv;
-            }
-        rstate = rh;
+        std::vector<int> sel;
+        std::vector<float> w, probs;
+        router(M, ly, cur.data(), n, rstate, have_state, sel, w, probs);
         have_state = true;
-        std::vector<float> rn((size_t)n * rd);
-        for (int t = 0; t < n; ++t) rms_norm(&rh[(size_t)t * rd], rd, hp.rms_eps, rnw.data(), &rn[(size_t)t * rd]);
-        matmul(mode, ly.m0, 0, rn.data(), n, h0.data(), rd);
-        for (int t = 0; t < n; ++t) for (int i = 0; i < rd; ++i) h0[(size_t)t * rd + i] = gelu_erf(h0[(size_t)t * rd + i] + b0[i]);
-        matmul(mode, ly.m2, 0, h0.data(), n, h2.data(), rd);
-        for (int t = 0; t < n; ++t) for (int i = 0; i < rd; ++i) h2[(size_t)t * rd + i] = gelu_erf(h2[(size_t)t * rd + i] + b2[i]);
-        matmul(mode, ly.m4, 0, h2.data(), n, lg.data(), E);
-        std::vector<int> sel((size_t)n * kk);
-        std::vector<float> w((size_t)n * kk), probs((size_t)n * E);
-        for (int t = 0; t < n; ++t) {
-            float* p = &probs[(size_t)t * E];
-            for (int e = 0; e < E; ++e) p[e] = lg[(size_t)t * E + e] + (ly.mask.empty() ? 0.0f : ly.mask[e]);
-            float mx = -INFINITY;
-            for (int e = 0; e < E; ++e) mx = std::max(mx, p[e]);
-            double sum = 0.0;
-            for (int e = 0; e < E; ++e) { p[e] = std::exp(p[e] - mx); sum += p[e]; }
-            const float inv = (float)(1.0 / sum);
-            for (int e = 0; e < E; ++e) p[e] = p[e] * inv;
-            // top-k of probs + bias (+ mask); ties to the lower id
-            std::vector<char> taken((size_t)E, 0);
-            for (int j = 0; j < kk; ++j) {
-                int best = -1; float bv = -INFINITY;
-                for (int e = 0; e < E; ++e) {
-                    if (taken[e]) continue;
-                    float sv = p[e] + rbias[e];
-                    if (!ly.mask.empty()) sv = sv + ly.mask[e];
-                    if (best < 0 || sv > bv) { bv = sv; best = e; }
-                }
-                taken[best] = 1;
-                sel[(size_t)t * kk + j] = best;
-                w[(size_t)t * kk + j] = p[best];
-            }
-        }
         c->sel_log.insert(c->sel_log.end(), sel.begin(), sel.end());
         c->probs_log.insert(c->probs_log.end(), probs.begin(), probs.end());
         // experts (:222-238): up/gate per route, silu(gate)*up, down, * weight, sum over j
@@ -705,7 +721,8 @@ int o_spk_row(void* m, const float* spk, const float* delta, float* out_row) {
 int o_prefill_spk(void* ctx, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
                   float* out_logits) {
     OCtx* c = (OCtx*)ctx;
-    if (slot < 0 || slot >= c->n_slots || n0 < 1 || n0 > c->cap || spk_pos < 0 || spk_pos >= n0) return 1;
+    if (slot < 0 || slot >= c->n_slots || n0 < 1 || n0 > c->cap || spk_pos >= n0) return 1;
+    if (!spk || spk_pos < 0) return o_prefill(ctx, slot, ids, n0, out_logits);   // no speaker (:36-37)
     std::vector<float> row((size_t)c->m->hp.n_embd);
     if (o_spk_row(c->m, spk, delta, row.data())) return 1;
     std::vector<int> slots(n0, slot), pos(n0);
@@ -721,7 +738,8 @@ int o_prefill_spk(void* ctx, int slot, const int32_t* ids, int n0, const float* 
 int o_logits(void* model, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta,
              float* out_logits) {
     OModel* M = (OModel*)model;
-    if (n < 1 || (spk && (spk_pos < 0 || spk_pos >= n))) return 1;
+    if (spk_pos < 0) spk = nullptr;                  // no speaker (src/zonos2-graph.cpp:36-37)
+    if (n < 1 || (spk && spk_pos >= n)) return 1;
     std::vector<float> row;
     if (spk) {
         row.resize((size_t)M->hp.n_embd);
@@ -771,6 +789,58 @@ void o_ctx_fake_fill(void* ctx, int slot, int n, uint32_t seed) {
                 c->V[L][at] = f2h(nd(g));
             }
     }
+}
+
+// Fill positions [0, n) of a slot's cache with a portable integer hash of (seed, layer,
+// K/V, position, kv head, dim) mapped to k / 1024, k in [-2048, 2048): exact in f16. The
+// product library's debug fill (z2b_debug_fill_kv) computes the same values, so the GPU
+// and this oracle hold identical long contexts without computing a prefill.
+static uint16_t kv_hash_f16(uint32_t seed, int layer, int kv, int pos, int head, int dim) {
+    uint64_t x = (((((uint64_t)seed * 256u + (uint64_t)layer) * 2u + (uint64_t)kv) * 1048576u + (uint64_t)pos) * 64u +
+                  (uint64_t)head) * 1024u + (uint64_t)dim;
+    x += 0x9E3779B97F4A7C15ull;                      // splitmix64 finaliser
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    x ^= x >> 31;
+    const int v = (int)((x >> 40) & 0xFFFu) - 2048;
+    return f2h((float)v / 1024.0f);
+}
+
+void o_ctx_hash_fill(void* ctx, int slot, int n, uint32_t seed) {
+    OCtx* c = (OCtx*)ctx;
+    const OHp& hp = c->m->hp;
+#pragma omp parallel for schedule(dynamic)
+    for (int L = 0; L < hp.n_layer; ++L)
+        for (int p = 0; p < n && p < c->cap; ++p)
+            for (int h = 0; h < hp.n_head_kv; ++h)
+                for (int i = 0; i < hp.head_dim; ++i) {
+                    const size_t at = (((size_t)slot * c->cap + p) * hp.n_head_kv + h) * hp.head_dim + i;
+                    c->K[L][at] = kv_hash_f16(seed, L, 0, p, h, i);
+                    c->V[L][at] = kv_hash_f16(seed, L, 1, p, h, i);
+                }
+}
+
+// The router of MoE layer `layer` on given residual rows res[n][d] (ffn_norm applied here)
+// and the previous MoE layer's state state_in[n][rd] (NULL: none, the first MoE layer):
+// sel[n][k], weights w[n][k] and the new state state_out[n][rd] (may be NULL).
+int o_router(void* model, int layer, const float* res, const float* state_in, int n, int32_t* sel_out, float* w_out,
+             float* state_out) {
+    OModel* M = (OModel*)model;
+    if (layer < 0 || layer >= M->hp.n_layer || !M->L[layer].is_moe || n < 1) return 1;
+    const OLayer& ly = M->L[layer];
+    const int d = M->hp.n_embd, rd = (int)ly.rdown.ne1;
+    const std::vector<float> fn = small(ly.ffn_norm);
+    std::vector<float> cur((size_t)n * d);
+    for (int t = 0; t < n; ++t) rms_norm(res + (size_t)t * d, d, M->hp.rms_eps, fn.data(), &cur[(size_t)t * d]);
+    std::vector<float> rstate;
+    if (state_in) rstate.assign(state_in, state_in + (size_t)n * rd);
+    std::vector<int> sel;
+    std::vector<float> w, probs;
+    router(*M, ly, cur.data(), n, rstate, state_in != nullptr, sel, w, probs);
+    std::copy(sel.begin(), sel.end(), sel_out);
+    std::copy(w.begin(), w.end(), w_out);
+    if (state_out) std::copy(rstate.begin(), rstate.end(), state_out);
+    return 0;
 }
 
 void o_dequant(uint32_t type, const void* data, int64_t n, float* out) { deq(type, (const uint8_t*)data, out, n); }

@@ -1,7 +1,9 @@
 """The isolated MoE expert op (config 4 of the benchmark set: E 32, d 2048, ff 1408, Q4_K
 gate/up, F16 down, top-4 routing skewed by a Zipf(1.1) bias) through z2b_expert_op,
-against a float32 numpy restatement over gguf-py's dequantised weights. T = 16 runs on
-the tile GEMV only; T = 320 sends the most-loaded experts to the tcgen05 GEMM."""
+against a float32 numpy restatement over gguf-py's dequantised weights, at every token
+count of the config-4 sweep (T = 16, 64, 256, 1024, 4096) plus 320. T = 16 runs on the tile
+GEMV only; from T = 64 the experts with >= 17 routes take the tcgen05 GEMM, and at 1024 and
+4096 the most-loaded experts span many 64-token tiles, the last one partial."""
 from __future__ import annotations
 
 import numpy as np
@@ -25,13 +27,24 @@ def routing(T, E, k, seed):
     return sel, np.take_along_axis(p, sel, 1).astype(np.float32)
 
 
+_W = {}
+
+
+def _weights(path):
+    if path not in _W:
+        from gguf import GGUFReader
+        from gguf.quants import dequantize
+        rd = GGUFReader(path)
+        t = {tt.name: tt for tt in rd.tensors}
+        _W.clear()
+        _W[path] = {n: dequantize(t[f"blk.0.ffn_{n}_exps.weight"].data,
+                                  t[f"blk.0.ffn_{n}_exps.weight"].tensor_type).astype(np.float32)
+                    for n in ("gate", "up", "down")}
+    return _W[path]
+
+
 def reference(path, x, sel, w):
-    from gguf import GGUFReader
-    from gguf.quants import dequantize
-    rd = GGUFReader(path)
-    t = {tt.name: tt for tt in rd.tensors}
-    W = {n: dequantize(t[f"blk.0.ffn_{n}_exps.weight"].data, t[f"blk.0.ffn_{n}_exps.weight"].tensor_type).astype(np.float32)
-         for n in ("gate", "up", "down")}
+    W = _weights(path)
     out = np.zeros_like(x)
     for e in np.unique(sel):
         rows, cols = np.nonzero(sel == e)
@@ -42,7 +55,7 @@ def reference(path, x, sel, w):
     return out
 
 
-@pytest.mark.parametrize("T", [16, 320])
+@pytest.mark.parametrize("T", [16, 64, 256, 320, 1024, 4096])
 def test_expert_op_vs_float32(model_dir, T):
     path = S.cached("zonos2", directory=model_dir, n_layer=1, expert_used=[4])
     m = R.Model(path)
@@ -59,8 +72,8 @@ def test_expert_op_vs_float32(model_dir, T):
     else:
         assert n_gemm == 0
     ref = reference(path, x, sel, w)
-    for t in range(T):
-        a, b = out[t].astype(np.float64), ref[t].astype(np.float64)
-        c = a @ b / (np.linalg.norm(a) * np.linalg.norm(b))
-        assert c >= 0.9999, (t, c)
+    a, b = out.astype(np.float64), ref.astype(np.float64)
+    c = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    print(f"T {T}: {n_gemm} experts on the tcgen05 GEMM, worst token cos {c.min():.7f}")
+    assert c.min() >= 0.9999, (int(c.argmin()), c.min())
     assert np.abs(out - ref).max() / np.abs(ref).max() <= 1e-2

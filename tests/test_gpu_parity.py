@@ -128,29 +128,46 @@ def test_dummy_fixture_greedy_frames(dummy_path):
     m.close()
 
 
-def test_device_sampler_matches_reference_sampler(tiny):
+SAMPLER_CASES = [
+    # the reference defaults (src/zonos2.h:197-208): top-k 106, min-p 0.18, repetition penalty
+    dict(temperature=1.15, top_k=106, top_p=0.0, min_p=0.18, rep_penalty=1.2, rep_window=50, rep_codebooks=8),
+    # top-p after a top-k cut
+    dict(temperature=0.9, top_k=40, top_p=0.8, min_p=0.0, rep_penalty=1.0, rep_window=50, rep_codebooks=8),
+    # every token a candidate: top-p over the probability order, CDF walk in token order
+    dict(temperature=1.3, top_k=0, top_p=0.9, min_p=0.05, rep_penalty=1.1, rep_window=20, rep_codebooks=9),
+]
+
+
+@pytest.mark.parametrize("case", range(len(SAMPLER_CASES)))
+def test_device_sampler_matches_reference_sampler(tiny, case):
     """Non-greedy sampling on the device vs the reference sampler restated on the host
-    (std::mt19937, same seed) fed the very logits the device sampled from."""
+    (std::mt19937, same seed) fed the very logits the device sampled from: every code
+    agrees. Logit ties order by token id on both sides (the reference's partial_sort
+    leaves tie order unspecified)."""
     hp = tiny.hp
-    sp = dict(temperature=1.15, top_k=106, top_p=0.0, min_p=0.18, rep_penalty=1.2, rep_window=50, rep_codebooks=8)
+    sp = SAMPLER_CASES[case]
     ctx = R.BatchCtx(tiny, 2, 256)
-    agree = total = 0
-    for slot, seed in ((0, 1234), (1, 99)):
+    seeds = (1234 + case, 99 + case)
+    for slot, seed in zip((0, 1), seeds):
         ctx.slot_reset(slot, R.Sampling(seed=seed, **sp))
-    host = [O.Sampler(hp.n_codebooks, seed=s, **sp) for s in (1234, 99)]
+    host = [O.Sampler(hp.n_codebooks, seed=s, **sp) for s in seeds]
     lg0 = [ctx.slot_prefill(s, prompt(10 + s, 30 + s)) for s in (0, 1)]
     nxt = [np.r_[x.argmax(-1), hp.text_vocab] for x in lg0]
     past = [10, 11]
+    mism = []
+    total = 0
     for step in range(40):
         codes, logits = ctx.step([(0, past[0], 1, R.WANT_SAMPLE), (1, past[1], 1, R.WANT_SAMPLE)],
                                  np.stack(nxt).astype(np.int32))
         for s in (0, 1):
             hc = host[s].sample(logits[s])
-            agree += int((hc == codes[s]).sum())
             total += hp.n_codebooks
+            for cb in np.nonzero(hc != codes[s])[0]:
+                mism.append((step, s, int(cb), int(hc[cb]), int(codes[s][cb])))
             nxt[s] = np.r_[codes[s], hp.text_vocab]
             past[s] += 1
-    assert agree / total >= 0.99, (agree, total)
+    print(f"sampler case {case}: {total - len(mism)}/{total} codes agree")
+    assert not mism, mism[:10]
 
 
 def test_cfg_twin_guidance(tiny):
@@ -223,3 +240,37 @@ def test_decode_loop_matches_stepping(tiny):
     ca, la = a.step([(i, past[i] + 5, 1, R.WANT_SAMPLE) for i in range(3)], nxt)
     cb, lb = b.step([(i, past[i] + 5, 1, R.WANT_SAMPLE) for i in range(3)], nxt)
     assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
+def test_step_logits_view(tiny):
+    """z2b_step_logits (zonos2_batch_slot_logits) after a z2b_step given no out_logits: the
+    per-desc host view equals, bit for bit, the logits a second context returned through
+    out_logits; descs without Z2B_WANT_LOGITS and out-of-range indices have none; with
+    readback off and no out_logits there is no view."""
+    hp = tiny.hp
+    prompts = [prompt(9, 300), prompt(14, 301), prompt(4, 302)]
+    a, b = R.BatchCtx(tiny, 3, 64), R.BatchCtx(tiny, 3, 64)
+    rows = []
+    for i, p in enumerate(prompts):
+        for c in (a, b):
+            c.slot_reset(i, R.Sampling(greedy=True))
+        rows.append(np.r_[a.slot_prefill(i, p).argmax(-1), hp.text_vocab])
+        b.slot_prefill(i, p)
+    ids = np.stack(rows).astype(np.int32)
+    past = [len(p) for p in prompts]
+    for s in range(3):
+        descs = [(0, past[0] + s, 1, R.WANT_SAMPLE), (1, past[1] + s, 1, 0), (2, past[2] + s, 1, R.WANT_LOGITS)]
+        ca, la = a.step(descs, ids)
+        cb, _ = b.step(descs, ids, want_logits=False)
+        assert np.array_equal(ca[0], cb[0])
+        for i in (0, 2):
+            v = b.step_logits(i)
+            assert v is not None and np.array_equal(v.view(np.uint32), la[i].view(np.uint32))
+        assert b.step_logits(1) is None and b.step_logits(3) is None and b.step_logits(-1) is None
+        ids = np.concatenate([ca[:1], ca[:1], ca[:1]], 0)
+        ids = np.concatenate([ids, np.full((3, 1), hp.text_vocab, np.int32)], 1).astype(np.int32)
+    b.set_logits_readback(False)
+    b.step([(0, past[0] + 3, 1, R.WANT_SAMPLE)], ids[:1])
+    assert b.step_logits(0) is None
+    a.close()
+    b.close()

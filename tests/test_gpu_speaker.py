@@ -98,3 +98,22 @@ def test_speaker_pos_outside_prompt_is_an_error(tiny):
         ctx.slot_prefill(0, prompt(6, 24), spk=spk, spk_pos=6)
     assert e.value.rc == 1 and "spk_pos" in str(e.value)          # Z2B_ERR_ARG
     ctx.close()
+
+
+def test_negative_speaker_pos_means_no_speaker(tiny, tiny_path):
+    """As the reference (src/zonos2-graph.cpp:36-37, 716): a speaker with spk_pos < 0 is
+    not injected, so the prefill equals a plain prefill bit for bit; the same holds for the
+    teacher-forced logits entry point."""
+    hp = tiny.hp
+    spk, delta = _inputs(hp, 34)
+    p = prompt(7, 25)
+    ctx = R.BatchCtx(tiny, 2, 64)
+    for s in (0, 1):
+        ctx.slot_reset(s, R.Sampling(greedy=True))
+    a = ctx.slot_prefill(0, p, spk=spk, spk_pos=-1, spk_emotion_delta=delta)
+    b = ctx.slot_prefill(1, p)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    la = tiny.logits(p, spk=spk, spk_pos=-3)
+    lb = tiny.logits(p)
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    ctx.close()

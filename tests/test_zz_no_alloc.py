@@ -1,6 +1,7 @@
-"""The allocation-free segment builder (z2b_route_segments_noalloc) against the
-allocating entry point (z2b_test_route) on the same router ids, two calls in a row, plus
-its size limit. Collected last so it also runs after every other GPU test."""
+"""The allocation-free segment builder (z2b_route_segments_noalloc): against the
+allocating entry point (z2b_test_route) on the same router ids, two calls in a row; its
+size limit; and that calls after the first leave the device's free memory unchanged.
+Collected last so it also runs after every other GPU test."""
 from __future__ import annotations
 
 import ctypes
@@ -65,3 +66,26 @@ def test_noalloc_rejects_sizes_beyond_the_limit():
     rc, *_ = _call(L.z2b_route_segments_noalloc, sel, w, 8)
     assert rc == 1                                       # Z2B_ERR_ARG
     assert b"Z2B_NOALLOC_MAX_ROUTES" in L.z2b_last_error()
+
+
+def _free_device_bytes():
+    """cuMemGetInfo on the calling thread's current (primary) context."""
+    cu = ctypes.CDLL("libcuda.so.1")
+    free, total = ctypes.c_size_t(), ctypes.c_size_t()
+    assert cu.cuMemGetInfo_v2(ctypes.byref(free), ctypes.byref(total)) == 0
+    return free.value
+
+
+def test_noalloc_calls_allocate_nothing():
+    """After the first call (which does the per-device set-up), further calls do not change
+    the device's free memory."""
+    L = _lib()
+    sel, w = _ids(64, 8, 1024, seed=11)
+    rc, *first = _call(L.z2b_route_segments_noalloc, sel, w, 64)
+    assert rc == 0, L.z2b_last_error()
+    before = _free_device_bytes()
+    for i in range(4):
+        rc, *again = _call(L.z2b_route_segments_noalloc, sel, w, 64)
+        assert rc == 0, L.z2b_last_error()
+        assert all(np.array_equal(a, b) for a, b in zip(first, again))
+    assert _free_device_bytes() == before

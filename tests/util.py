@@ -81,3 +81,47 @@ def run_oracle(O, om, prompts, fed, capture_sel=False):
             sels.append(c.last_sel())
         past = [x + 1 for x in past]
     return dict(pre=pre, logits=np.stack(logits) if logits else None, sel=sels)
+
+
+def run_gpu_filled(R, model, ctx_lens, steps, seed, capture_sel=False):
+    """Streams whose KV of positions [0, ctx_lens[i]) comes from the hash fill (seed + i),
+    then `steps` batched greedy decode steps starting from a random row each. Returns
+    per-step logits [steps][n][ncb][av], the fed rows and, optionally, router ids."""
+    hp = model.hp
+    n = len(ctx_lens)
+    ctx = R.BatchCtx(model, n, max(ctx_lens) + steps + 8)
+    for i, L in enumerate(ctx_lens):
+        ctx.slot_reset(i, R.Sampling(greedy=True))
+        ctx.fill_kv(i, int(L), seed + i)
+    ids = np.stack([prompt(1, seed + 500 + i)[0] for i in range(n)]).astype(np.int32)
+    past = [int(L) for L in ctx_lens]
+    fed, logits, sels = [], [], []
+    for s in range(steps):
+        fed.append(ids)
+        codes, lg = ctx.step([(i, past[i] + s, 1, R.WANT_SAMPLE) for i in range(n)], ids)
+        logits.append(lg)
+        if capture_sel:
+            sels.append(ctx.last_sel().reshape(hp.n_layer, n, -1))
+        ids = np.concatenate([codes, np.full((n, 1), hp.text_vocab, np.int32)], 1).astype(np.int32)
+    ctx.close()
+    return dict(logits=np.stack(logits), fed=np.stack(fed), sel=sels)
+
+
+def run_oracle_filled(O, om, ctx_lens, fed, seed):
+    """The oracle over the same hash-filled contexts, teacher-forced with the GPU's rows."""
+    n = len(ctx_lens)
+    c = O.Ctx(om, n, max(ctx_lens) + len(fed) + 8)
+    for i, L in enumerate(ctx_lens):
+        c.hash_fill(i, int(L), seed + i)
+    past = [int(L) for L in ctx_lens]
+    logits, sels = [], []
+    for s, ids in enumerate(fed):
+        logits.append(c.step(list(range(n)), [p + s for p in past], ids))
+        sels.append(c.last_sel().reshape(-1, n, int(max(om.expert_used))))
+    return dict(logits=np.stack(logits), sel=sels)
+
+
+def topk_set_flips(a, b):
+    """Per (layer, token) whether the sets of router ids differ: a, b [L][n][k]."""
+    a, b = np.sort(np.asarray(a), -1), np.sort(np.asarray(b), -1)
+    return (a != b).any(-1)

@@ -1,6 +1,7 @@
 // capi.cpp — extern "C" entry points declared in include/z2b.h.
 #include "runtime.h"
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -225,6 +226,47 @@ int z2b_expert_op(z2b_ctx* ctx, int layer, const float* x, int T, const int32_t*
     const int rc = ctx_expert_op(ctx->c, layer, x, T, sel, selw, k, out, reps, ms, weight_bytes, &ng);
     if (n_gemm_experts) *n_gemm_experts = ng;
     return rc;
+}
+
+int z2b_debug_fill_kv(z2b_ctx* ctx, int slot, int n, uint32_t seed) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_debug_fill_kv(ctx->c, slot, n, seed);
+}
+
+int z2b_debug_router_capture(z2b_ctx* ctx, int enable) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_debug_router_capture(ctx->c, enable);
+}
+
+int z2b_debug_router_inputs(z2b_ctx* ctx, int layer, float* res, float* state, int* T) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_debug_router_inputs(ctx->c, layer, res, state, T);
+}
+
+int z2b_slot_after_frame(const z2b_hparams* hp, z2b_slot_state* s, const int32_t* codes, int max_frames, int keep) {
+    if (!hp || !s || !codes || hp->n_codebooks < 1 || hp->n_codebooks + 1 > Z2B_MAX_ROW) {
+        set_error("slot_after_frame: bad argument");
+        return -1;
+    }
+    const int ncb = (int)hp->n_codebooks;
+    const int frame_idx = s->step;
+    int max_eoa = -1;                                   // last codebook holding end-of-audio
+    for (int cb = 0; cb < ncb; ++cb)
+        if (codes[cb] == (int32_t)hp->eoa_id) max_eoa = cb;
+    if (s->eos_frame < 0 && max_eoa >= 0) {
+        s->eos_frame = std::max(0, frame_idx - max_eoa);
+        s->countdown = ncb + 1;
+    }
+    bool finished = false;
+    if (s->countdown > 0) finished = --s->countdown == 0;
+    for (int cb = 0; cb < ncb; ++cb) s->next_ids[cb] = codes[cb];
+    s->next_ids[ncb] = (int32_t)hp->text_vocab;
+    s->step += 1;
+    if (!keep || finished || s->step >= max_frames) s->done = 1;
+    return keep ? 1 : 0;
 }
 
 const char* z2b_last_error(void) { return last_error(); }

@@ -386,7 +386,52 @@ void attn_launch_h(const StepBufs& b, const KVDev& kv, const Dims& d, int layer,
     }
 }
 
+// ---------------------------------------------------------------- test fill
+// Positions [0, n) of one slot, every layer: value k / 1024, k in [-2048, 2048), from a
+// splitmix64 hash of (seed, layer, K/V, position, kv head, dim); exact in f16. The CPU
+// oracle's hash fill computes the same values, so both hold identical long contexts.
+__device__ __forceinline__ float kv_hash_value(uint32_t seed, int layer, int kv, int pos, int head, int dim) {
+    uint64_t x = (((((uint64_t)seed * 256u + (uint64_t)layer) * 2u + (uint64_t)kv) * 1048576u + (uint64_t)pos) * 64u +
+                  (uint64_t)head) * 1024u + (uint64_t)dim;
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    x ^= x >> 31;
+    return (float)((int)((x >> 40) & 0xFFFu) - 2048) / 1024.0f;
+}
+
+template <int HD>
+__global__ void kv_hash_fill_kernel(const KVDev kv, const int* __restrict__ pages, int nkv, uint32_t seed) {
+    const int pos = blockIdx.x, layer = blockIdx.y;
+    const int j = pos % PAGE;
+    __half* lbase = kv.pool + (size_t)pages[pos / PAGE] * kv.page_elems + (size_t)layer * kv.layer_elems;
+    for (int e = threadIdx.x; e < 2 * nkv * HD; e += blockDim.x) {
+        const int which = e / (nkv * HD), h = (e / HD) % nkv, i = e % HD;
+        const __half v = __float2half_rn(kv_hash_value(seed, layer, which, pos, h, i));
+        if (which == 0) {
+            __half* kb = lbase + (size_t)h * kv.head_elems + (size_t)j * HD;
+            kb[((i / 8) ^ kswz<HD>(j)) * 8 + (i % 8)] = v;
+        } else {
+            __half* vb = lbase + (size_t)(nkv + h) * kv.head_elems + (size_t)(j / KCH) * HD * KCH;
+            const int col = j % KCH;
+            vb[(size_t)i * KCH + (((col / 8) ^ (i & 7)) * 8) + (col % 8)] = v;
+        }
+    }
+}
+
 }  // namespace
+
+void launch_kv_hash_fill(const KVDev& kv, const int* pages, int n, int n_layer, int nkv, int hd, uint32_t seed,
+                         cudaStream_t s) {
+    if (n < 1) return;
+    dim3 grid(n, n_layer);
+    switch (hd) {
+        case 16: kv_hash_fill_kernel<16><<<grid, 128, 0, s>>>(kv, pages, nkv, seed); break;
+        case 32: kv_hash_fill_kernel<32><<<grid, 128, 0, s>>>(kv, pages, nkv, seed); break;
+        case 64: kv_hash_fill_kernel<64><<<grid, 128, 0, s>>>(kv, pages, nkv, seed); break;
+        default: kv_hash_fill_kernel<128><<<grid, 128, 0, s>>>(kv, pages, nkv, seed); break;
+    }
+}
 
 void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T,
                         cudaStream_t s) {

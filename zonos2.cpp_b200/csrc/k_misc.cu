@@ -234,12 +234,33 @@ __device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {   /
     return va > vb || (va == vb && ia < ib);
 }
 
+// Block-wide bitonic sort of (v, i)[SORT_N] into descending value, ascending index; entries
+// from n on are padding (-inf, INT_MAX). Ends with a barrier.
+__device__ void sort_desc(float* v, int* ix, int n) {
+    for (int i = n + threadIdx.x; i < SORT_N; i += blockDim.x) { v[i] = -INFINITY; ix[i] = 0x7fffffff; }
+    __syncthreads();
+    for (int size = 2; size <= SORT_N; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < SORT_N; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool asc = (i & size) == 0;     // segment direction
+                    const bool sw = asc ? before(v[j], ix[j], v[i], ix[i]) : before(v[i], ix[i], v[j], ix[j]);
+                    if (sw) { float tv = v[i]; v[i] = v[j]; v[j] = tv; int ti = ix[i]; ix[i] = ix[j]; ix[j] = ti; }
+                }
+            }
+            __syncthreads();
+        }
+}
+
 __global__ void __launch_bounds__(256) sampler_kernel(const StepBufs b, const SampDev* __restrict__ samp,
                                                       int* hist, int* hist_len, int hist_cap, const Dims dm) {
     __shared__ float lv[SORT_N];
     __shared__ int li[SORT_N];
     __shared__ float pv[SORT_N];
-    __shared__ unsigned char drop_p[SORT_N];   // top-p rejections
+    __shared__ float sv[SORT_N];                // probability order when every token is a candidate
+    __shared__ int si[SORT_N];
+    __shared__ unsigned char keep[SORT_N];
     __shared__ int s_code;
     pdl_wait();
     pdl_release();
@@ -283,61 +304,66 @@ __global__ void __launch_bounds__(256) sampler_kernel(const StepBufs b, const Sa
         if (sp.temperature > 0.0f)
             for (int i = threadIdx.x; i < av; i += blockDim.x) lv[i] = lv[i] / sp.temperature;
         const int k = (sp.top_k > 0 && sp.top_k < av) ? sp.top_k : av;
+        const bool use_p = sp.top_p > 0.0f && sp.top_p < 1.0f;
         if (k < av) {
-            for (int i = av + threadIdx.x; i < SORT_N; i += blockDim.x) { lv[i] = -INFINITY; li[i] = 0x7fffffff; }
+            // candidates: the top k logits in descending order, ties by position (the order
+            // std::partial_sort gives when ties are broken by index)
             __syncthreads();
-            for (int size = 2; size <= SORT_N; size <<= 1)
-                for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                    for (int i = threadIdx.x; i < SORT_N; i += blockDim.x) {
-                        const int j = i ^ stride;
-                        if (j > i) {
-                            const bool asc = (i & size) == 0;     // segment direction
-                            const bool sw = asc ? before(lv[j], li[j], lv[i], li[i]) : before(lv[i], li[i], lv[j], li[j]);
-                            if (sw) { float tv = lv[i]; lv[i] = lv[j]; lv[j] = tv; int ti = li[i]; li[i] = li[j]; li[j] = ti; }
-                        }
-                    }
-                    __syncthreads();
-                }
+            sort_desc(lv, li, av);
         }
         __syncthreads();
-        __shared__ double s_sum;
-        __shared__ float s_pmax;
+        // Softmax over the candidates in candidate order with a double sum (:48-53); exp is
+        // taken in double and rounded once to float, the correctly rounded expf of the host
+        // libm the reference calls.
         if (threadIdx.x == 0) {
             float mx = -1e30f;
             for (int j = 0; j < k; ++j) mx = fmaxf(mx, lv[j]);
             double sum = 0.0;
-            for (int j = 0; j < k; ++j) { pv[j] = expf(lv[j] - mx); sum += (double)pv[j]; }
-            float pm = 0.0f;
-            for (int j = 0; j < k; ++j) { pv[j] = (float)((double)pv[j] / sum); pm = fmaxf(pm, pv[j]); }
-            s_pmax = pm;
+            for (int j = 0; j < k; ++j) { pv[j] = (float)exp((double)(lv[j] - mx)); sum += (double)pv[j]; }
+            for (int j = 0; j < k; ++j) pv[j] = (float)((double)pv[j] / sum);
         }
         __syncthreads();
-        // top-p over candidates ordered by probability (descending, ties by position)
-        if (sp.top_p > 0.0f && sp.top_p < 1.0f) {
-            for (int j = threadIdx.x; j < k; j += blockDim.x) {
-                double c = 0.0;
-                for (int i = 0; i < k; ++i)
-                    if (pv[i] > pv[j] || (pv[i] == pv[j] && i < j)) c += (double)pv[i];
-                // kept iff the mass before it has not yet reached top_p
-                drop_p[j] = c >= (double)sp.top_p ? 1 : 0;
+        // top-p walks the candidates by descending probability (:55-63). After a top-k cut
+        // that order is the candidate order itself (probabilities follow the logits); with
+        // every token a candidate, the (probability, position) pairs are sorted first.
+        const float* pord = pv;
+        const int* iord = nullptr;
+        if (use_p && k == av) {
+            for (int i = threadIdx.x; i < SORT_N; i += blockDim.x) {
+                sv[i] = i < av ? pv[i] : -INFINITY;
+                si[i] = i < av ? i : 0x7fffffff;
             }
             __syncthreads();
+            sort_desc(sv, si, av);
+            __syncthreads();
+            pord = sv;
+            iord = si;
         }
         if (threadIdx.x == 0) {
-            const bool use_p = sp.top_p > 0.0f && sp.top_p < 1.0f;
-            const float thr = sp.min_p * s_pmax;
-            int best = 0;
-            for (int j = 1; j < k; ++j) if (pv[j] > pv[best]) best = j;
+            float pmax = 0.0f;
+            for (int j = 0; j < k; ++j) pmax = fmaxf(pmax, pv[j]);
+            for (int j = 0; j < k; ++j) keep[j] = 1;
+            if (use_p) {
+                double cc = 0.0;
+                bool done = false;
+                for (int r = 0; r < k; ++r) {
+                    const int j = iord ? iord[r] : r;
+                    if (done) keep[j] = 0;
+                    cc += (double)pord[r];
+                    if (cc >= (double)sp.top_p) done = true;
+                }
+            }
+            const float thr = sp.min_p * pmax;                     // min-p (:64-67)
             double s2 = 0.0;
+            int top = 0;                                           // first candidate of the largest probability
             for (int j = 0; j < k; ++j) {
-                bool keep = true;
-                if (use_p && drop_p[j]) keep = false;
-                if (sp.min_p > 0.0f && pv[j] < thr) keep = false;
-                if (!keep) pv[j] = 0.0f;
+                if (pv[j] > pv[top]) top = j;
+                if (sp.min_p > 0.0f && pv[j] < thr) keep[j] = 0;
+                if (!keep[j]) pv[j] = 0.0f;
                 s2 += (double)pv[j];
             }
-            int code = li[best];
-            if (s2 > 0.0) {
+            int code = li[top];
+            if (s2 > 0.0) {                                        // CDF walk with one draw (:70-75)
                 const double r = b.canon[(size_t)o * dm.n_codebooks + cb] * s2;
                 double acc = 0.0;
                 for (int j = 0; j < k; ++j) { acc += (double)pv[j]; if (acc >= r) { code = li[j]; break; } }

@@ -13,6 +13,7 @@
 #include "../../include/z2b.h"
 #include "../../include/z2b_tools.h"
 
+#include <atomic>
 #include <string>
 
 namespace z2b {
@@ -449,6 +450,8 @@ __global__ void route_test_kernel(const int* sel, const float* selw, int T, int 
 
 }  // namespace
 
+constexpr int kMaxRouterDevices = 64;
+
 size_t router_mlp_smem(const Dims& d, int E, bool* stage) {
     const size_t base = (size_t)(3 * d.rd + MAX_EXPERTS) * sizeof(float);
     const size_t w = (size_t)(2 * d.rd * d.rd + E * d.rd) * sizeof(float);
@@ -458,11 +461,15 @@ size_t router_mlp_smem(const Dims& d, int E, bool* stage) {
 
 void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
                    cudaStream_t s) {
-    static bool configured = false;
-    if (!configured) {
+    // the dynamic shared memory opt-in is a per-device function attribute: set it once on
+    // every device a context runs on (one process may drive several GPUs)
+    static std::atomic<bool> configured[kMaxRouterDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxRouterDevices || !configured[dev].load(std::memory_order_acquire)) {
         cudaFuncSetAttribute(router_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         cudaFuncSetAttribute(router_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        configured = true;
+        if (dev >= 0 && dev < kMaxRouterDevices) configured[dev].store(true, std::memory_order_release);
     }
     if (ly.is_moe) {
         const int nks = router_kslices(d.n_embd), L = d.n_embd / nks, S = L + 4;
@@ -510,12 +517,14 @@ extern "C" int z2b_test_route(const int32_t* sel, const float* selw, int T, int 
 
 // ---------------------------------------------------------------- allocation-free variant
 // z2b_route_segments_noalloc runs the same segment builder as z2b_test_route on a fixed
-// device scratch area instead of buffers allocated per call. It is for callers that
-// must not allocate device memory: cudaMalloc and cudaFree synchronise the whole device
-// (stalling decode steps queued by other threads) and are refused while a stream of the
-// process is being captured into a CUDA graph in the global capture mode. The scratch
-// is one file-scope array, so calls that overlap in time (from several host threads)
-// race on it and must be serialised by the caller.
+// device scratch area instead of buffers allocated per call. It is for callers that may
+// not allocate device memory: a serving process that has handed all but a fixed budget of
+// the GPU to its KV page pool, or a latency-critical thread, since cudaMalloc and cudaFree
+// can synchronise the whole device and stall decode steps queued by other threads. The
+// work runs on the calling thread's per-thread default stream, which does not join the
+// streams of other threads or libraries. The scratch is one file-scope array, so calls
+// that overlap on the GPU (from several host threads) race on it and must be serialised
+// by the caller.
 namespace z2b {
 namespace {
 
@@ -568,7 +577,7 @@ extern "C" int z2b_route_segments_noalloc(const int32_t* sel, const float* selw,
     int* dact = dseg + MAX_EXPERTS + 1;
     int* dna = dact + MAX_EXPERTS;
     const size_t R = (size_t)T * k;
-    cudaStream_t s = 0;
+    cudaStream_t s = cudaStreamPerThread;
     bool ok = cudaMemcpyAsync(dsel, sel, R * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
               cudaMemcpyAsync(dw, selw, R * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
               // route_pos of routes with no expert stays -1; everything else is written

@@ -167,6 +167,10 @@ void launch_embed(const StepBufs& b, const EmbedDev& e, const float* attn_norm0,
 void launch_spk_proj(const float* lda_w, const float* lda_b, const float* proj_w, const float* proj_b, const float* spk,
                      const float* delta, int spk_dim, int lda_dim, int n_embd, float* row, cudaStream_t s);
 void launch_rope_append(const StepBufs& b, const KVDev& kv, const float* temp, const Dims& d, int layer, int T, cudaStream_t s);
+// Test fill: positions [0, n) of one slot (pages[] = the slot's page ids) in every layer
+// from an integer hash of (seed, layer, K/V, position, kv head, dim); exact in f16.
+void launch_kv_hash_fill(const KVDev& kv, const int* pages, int n, int n_layer, int nkv, int hd, uint32_t seed,
+                         cudaStream_t s);
 void launch_attention(const StepBufs& b, const KVDev& kv, const Dims& d, int layer, int T, int split_keys, int max_split, cudaStream_t s);
 void launch_attn_combine(const StepBufs& b, const Dims& d, int T, int split_keys, int max_split, cudaStream_t s);
 void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,

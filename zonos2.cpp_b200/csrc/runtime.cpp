@@ -37,6 +37,7 @@ Ctx::~Ctx() {
     if (d_canon_all) cudaFree(d_canon_all);
     if (h_canon_all) cudaFreeHost(h_canon_all);
     if (d_spk) cudaFree(d_spk);
+    if (d_rcap) cudaFree(d_rcap);
     if (d_sched_descs) cudaFree(d_sched_descs);
     if (d_sched_src) cudaFree(d_sched_src);
     if (d_sched_rows) cudaFree(d_sched_rows);
@@ -339,6 +340,13 @@ void enqueue_step(Ctx* c, int T, int n_out) {
             const int offs[1] = {0};
             gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f, PC_WO);
         }
+        if (c->rcap_on && c->d_rcap && ly.is_moe) {
+            const size_t per = (size_t)D.n_embd + D.rd;
+            float* rec = c->d_rcap + (size_t)L * c->T_max * per;
+            cudaMemcpyAsync(rec, B.res, (size_t)T * D.n_embd * 4, cudaMemcpyDeviceToDevice, c->stream);
+            cudaMemcpyAsync(rec + (size_t)c->T_max * D.n_embd, B.rstate, (size_t)T * D.rd * 4, cudaMemcpyDeviceToDevice,
+                            c->stream);
+        }
         { ProfScope ps(c, PC_ROUTER); launch_router(B, ly.small, D, T, (ly.is_moe && first_moe) ? 1 : 0, L, c->stream); c->launches += router_launches(ly.small); }
         if (ly.is_moe) first_moe = false;
         const bool bulk = T > c->cur_n_desc;                 // the step carries prompt rows
@@ -365,7 +373,7 @@ void enqueue_step(Ctx* c, int T, int n_out) {
 
 int run_step(Ctx* c, int T, int n_out) {
     // graphs for decode-only shapes (T == streams); steps carrying prompt rows run eagerly
-    const bool use_graph = c->graphs_enabled && !c->profiling && T == c->cur_n_desc && c->spk_t < 0;
+    const bool use_graph = c->graphs_enabled && !c->profiling && !c->rcap_on && T == c->cur_n_desc && c->spk_t < 0;
     if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
     const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48);
     auto it = c->graphs.find(key);
@@ -562,9 +570,10 @@ int spk_prepare(Ctx* c, const float* spk, const float* delta) {
 
 int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* spk, int spk_pos, const float* delta,
                     float* out_logits) {
-    if (!spk) return ctx_prefill(c, slot, ids, n0, out_logits);
+    // as the reference (src/zonos2-graph.cpp:36-37, 716): a negative spk_pos means no speaker
+    if (!spk || spk_pos < 0) return ctx_prefill(c, slot, ids, n0, out_logits);
     if (n0 < 1 || n0 > c->slot_cap) { set_error("prefill n0 out of range"); return Z2B_ERR_ARG; }
-    if (spk_pos < 0 || spk_pos >= n0) { set_error("spk_pos outside the prompt rows"); return Z2B_ERR_ARG; }
+    if (spk_pos >= n0) { set_error("spk_pos outside the prompt rows"); return Z2B_ERR_ARG; }
     const int src = spk_prepare(c, spk, delta);
     if (src) return src;
     const int chunk = c->T_max;
@@ -582,7 +591,8 @@ int ctx_prefill_spk(Ctx* c, int slot, const int32_t* ids, int n0, const float* s
 
 int model_logits(Model* m, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta, float* out) {
     if (!ids || !out || n < 1) { set_error("logits: bad arguments"); return Z2B_ERR_ARG; }
-    if (spk && (spk_pos < 0 || spk_pos >= n)) { set_error("spk_pos outside the rows"); return Z2B_ERR_ARG; }
+    if (spk_pos < 0) spk = nullptr;                  // no speaker, as the reference
+    if (spk && spk_pos >= n) { set_error("spk_pos outside the rows"); return Z2B_ERR_ARG; }
     constexpr int kRowsPerStep = 512;
     Ctx* c = nullptr;
     int rc = ctx_create(m, 1, n, &c, std::min(n, kRowsPerStep));
@@ -741,6 +751,55 @@ int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, con
         total_launches += c->launches + 1;
     }
     c->sched_launches = total_launches;
+    return Z2B_OK;
+}
+
+// Test support: KV of positions [0, n) of `slot` from the integer hash the CPU oracle's
+// hash fill uses (pages allocated from the pool as a step would).
+int ctx_debug_fill_kv(Ctx* c, int slot, int n, uint32_t seed) {
+    const Dims& D = c->m->dims;
+    if (slot < 0 || slot >= c->n_slots || n < 1 || n > c->slot_cap) { set_error("fill_kv: bad slot or length"); return Z2B_ERR_ARG; }
+    auto& pages = c->slot_pages[slot];
+    const int need = (n - 1) / PAGE + 1;
+    while ((int)pages.size() < need) {
+        if (c->free_pages.empty()) { set_error("KV page pool exhausted"); return Z2B_ERR_OOM; }
+        const int pg = c->free_pages.back();
+        c->free_pages.pop_back();
+        c->h_pt[(size_t)slot * c->pages_per_slot + pages.size()] = pg;
+        pages.push_back(pg);
+    }
+    int* d_pages = nullptr;
+    CK(cudaMalloc(&d_pages, (size_t)need * 4));
+    cudaMemcpy(d_pages, pages.data(), (size_t)need * 4, cudaMemcpyHostToDevice);
+    launch_kv_hash_fill(c->kv, d_pages, n, D.n_layer, D.n_head_kv, D.head_dim, seed, c->stream);
+    const cudaError_t e = cudaStreamSynchronize(c->stream);
+    cudaFree(d_pages);
+    if (e != cudaSuccess) { set_error(std::string("fill_kv: ") + cudaGetErrorString(e)); return Z2B_ERR_CUDA; }
+    return Z2B_OK;
+}
+
+int ctx_debug_router_capture(Ctx* c, int enable) {
+    const Dims& D = c->m->dims;
+    if (enable && !c->d_rcap) {
+        const size_t bytes = (size_t)D.n_layer * c->T_max * ((size_t)D.n_embd + D.rd) * 4;
+        CK(cudaMalloc(&c->d_rcap, bytes));
+    }
+    c->rcap_on = enable != 0;
+    return Z2B_OK;
+}
+
+int ctx_debug_router_inputs(Ctx* c, int layer, float* res, float* state, int* T) {
+    const Dims& D = c->m->dims;
+    if (!c->d_rcap || layer < 0 || layer >= D.n_layer || !c->m->layers[layer].is_moe || c->last_T < 1) {
+        set_error("router_inputs: no capture for that layer");
+        return Z2B_ERR_ARG;
+    }
+    const size_t per = (size_t)D.n_embd + D.rd;
+    const float* rec = c->d_rcap + (size_t)layer * c->T_max * per;
+    CK(cudaStreamSynchronize(c->stream));
+    if (res) CK(cudaMemcpy(res, rec, (size_t)c->last_T * D.n_embd * 4, cudaMemcpyDeviceToHost));
+    if (state) CK(cudaMemcpy(state, rec + (size_t)c->T_max * D.n_embd, (size_t)c->last_T * D.rd * 4, cudaMemcpyDeviceToHost));
+    if (T) *T = c->last_T;
     return Z2B_OK;
 }
 

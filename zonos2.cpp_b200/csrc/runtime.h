@@ -82,6 +82,9 @@ struct Ctx {
     int* d_sched_src = nullptr;              // [steps][n] row offset or -1 (feed from codes)
     size_t sched_src_cap = 0;
     long sched_launches = 0;                 // kernel launches of the last schedule
+    // test support: router inputs recorded before every MoE router of a step
+    bool rcap_on = false;
+    float* d_rcap = nullptr;                 // [n_layer][T_max][n_embd + rd]
     // accounting of the last step
     uint64_t last_wbytes = 0, last_kvbytes = 0, last_other = 0;
     std::vector<void*> dallocs, hallocs;
@@ -111,6 +114,9 @@ enum ProfClass { PC_PACK, PC_EMBED, PC_QKV, PC_ROPE, PC_ATTN, PC_ATTN_COMB, PC_W
 void account(Ctx* c, const z2b_slot_desc* descs, int n, int T);
 void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode);
 int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch);
+int ctx_debug_fill_kv(Ctx* c, int slot, int n, uint32_t seed);
+int ctx_debug_router_capture(Ctx* c, int enable);
+int ctx_debug_router_inputs(Ctx* c, int layer, float* res, float* state, int* T);
 int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k, float* out,
                   int reps, double* ms, uint64_t* weight_bytes, int* n_gemm);
 

@@ -99,6 +99,11 @@ def lib():
             "z2b_host_tiles_bytes": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
             "z2b_host_repack": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V], I),
             "z2b_host_unpack_tiles": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V], I),
+            "z2b_slot_after_frame": ([ctypes.POINTER(HParams), ctypes.POINTER(SlotState), V, I, I], I),
+            "z2b_debug_fill_kv": ([P, I, I, ctypes.c_uint32], I),
+            "z2b_debug_router_capture": ([P, I], I),
+            "z2b_debug_router_inputs": ([P, I, V, V, ctypes.POINTER(ctypes.c_int)], I),
+            "z2b_debug_last_sel": ([P, V, I], I),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)
@@ -226,6 +231,39 @@ class BatchCtx:
         _check(lib().z2b_step(self.h, ctypes.cast(arr, ctypes.c_void_p), n, _ptr(ids), _ptr(codes), _ptr(logits)))
         return codes, logits
 
+    def fill_kv(self, slot: int, n: int, seed: int):
+        """Test support: KV of positions [0, n) from the hash the oracle's hash_fill uses."""
+        _check(lib().z2b_debug_fill_kv(self.h, slot, n, seed))
+
+    def router_capture(self, enable: bool):
+        """Test support: record every MoE router's inputs of the following steps."""
+        _check(lib().z2b_debug_router_capture(self.h, 1 if enable else 0))
+
+    def router_inputs(self, layer: int):
+        """(residual rows [T, d], incoming router state [T, rd]) of `layer` in the last step."""
+        T = ctypes.c_int(0)
+        _check(lib().z2b_debug_router_inputs(self.h, layer, None, None, ctypes.byref(T)))
+        hp = self.model.hp
+        res = np.empty((T.value, hp.n_embd), np.float32)
+        st = np.empty((T.value, hp.router_dim), np.float32)
+        _check(lib().z2b_debug_router_inputs(self.h, layer, _ptr(res), _ptr(st), ctypes.byref(T)))
+        return res, st
+
+    def last_sel(self) -> np.ndarray:
+        """Router ids of every layer of the last step: [n_layer, T, kmax]."""
+        need = lib().z2b_debug_last_sel(self.h, None, 0)
+        buf = np.empty(need, np.int32)
+        lib().z2b_debug_last_sel(self.h, _ptr(buf), need)
+        return buf
+
+    def step_logits(self, index: int):
+        """zonos2_batch_slot_logits: logits [ncb, av] of desc `index` of the last step (a copy of
+        the context's host view), or None when that desc has none."""
+        p = lib().z2b_step_logits(self.h, int(index))
+        if not p:
+            return None
+        return np.ctypeslib.as_array(p, shape=(self.ncb * self.av,)).reshape(self.ncb, self.av).copy()
+
     def decode_loop(self, descs, first_ids, n_steps: int):
         n = len(descs)
         arr = (SlotDesc * n)()
@@ -315,25 +353,25 @@ class BatchCtx:
             return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(self.PROF_CLASSES)}
 
 
-def slot_after_sample(hp: HParams, s: Slot, codes, max_frames: int) -> None:
-    """EOS / countdown / next_ids bookkeeping of zonos2_slot_sample (src/zonos2-graph.cpp:852-868)."""
+class SlotState(ctypes.Structure):
+    """z2b_slot_state (include/z2b.h): zonos2_slot's per-stream fields."""
+    _fields_ = [("index", ctypes.c_int32), ("done", ctypes.c_int32), ("n_past", ctypes.c_int32),
+                ("step", ctypes.c_int32), ("eos_frame", ctypes.c_int32), ("countdown", ctypes.c_int32),
+                ("next_ids", ctypes.c_int32 * 32)]
+
+
+def slot_after_sample(hp: HParams, s: Slot, codes, max_frames: int, keep: bool = True) -> bool:
+    """EOS / countdown / next_ids bookkeeping of zonos2_slot_sample (src/zonos2-graph.cpp:852-868),
+    through z2b_slot_after_frame; updates `s` in place and returns keep."""
     ncb = hp.n_codebooks
-    frame_idx = s.step
-    max_eoa = -1
-    for cb in range(ncb):
-        if int(codes[cb]) == hp.eoa_id:
-            max_eoa = cb
-    if s.eos_frame < 0 and max_eoa >= 0:
-        s.eos_frame = max(0, frame_idx - max_eoa)
-        s.countdown = ncb + 1
-    finished = False
-    if s.countdown > 0:
-        s.countdown -= 1
-        finished = s.countdown == 0
-    s.next_ids = [int(c) for c in codes[:ncb]] + [hp.text_vocab]
-    s.step += 1
-    if finished or s.step >= max_frames:
-        s.done = True
+    st = SlotState(s.index, 1 if s.done else 0, s.n_past, s.step, s.eos_frame, s.countdown)
+    c = np.ascontiguousarray(np.asarray(codes[:ncb], np.int32))
+    rc = lib().z2b_slot_after_frame(ctypes.byref(hp), ctypes.byref(st), _ptr(c), int(max_frames), 1 if keep else 0)
+    if rc < 0:
+        raise Z2BError(1, lib().z2b_last_error().decode())
+    s.done, s.step, s.eos_frame, s.countdown = bool(st.done), st.step, st.eos_frame, st.countdown
+    s.next_ids = [int(x) for x in st.next_ids[:ncb + 1]]
+    return bool(rc)
 
 
 def test_dequant(qtype: int, rows: int, k: int, raw: np.ndarray, from_tiles: bool) -> np.ndarray:
