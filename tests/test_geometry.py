@@ -30,7 +30,7 @@ CASES = ([(t, k) for t in ("Q4_K", "Q6_K", "Q8_0") for k in (256, 1024, 2048, 40
 
 
 @pytest.mark.parametrize("wt,k", CASES)
-@pytest.mark.parametrize("nmat,ntg,want", [(1, 2, 2), (2, 2, 2), (1, 1, 3)])
+@pytest.mark.parametrize("nmat,ntg,want", [(1, 2, 2), (2, 2, 2), (2, 1, 2), (1, 1, 3)])
 def test_shared_memory_fits(wt, k, nmat, ntg, want):
     g = _geom(GT[wt], k, nmat, ntg)
     assert 1 <= g["ns"] <= 4 and g["nw"] >= 1

@@ -270,7 +270,7 @@ def test_step_logits_view(tiny):
         ids = np.concatenate([ca[:1], ca[:1], ca[:1]], 0)
         ids = np.concatenate([ids, np.full((3, 1), hp.text_vocab, np.int32)], 1).astype(np.int32)
     b.set_logits_readback(False)
-    b.step([(0, past[0] + 3, 1, R.WANT_SAMPLE)], ids[:1])
+    b.step([(0, past[0] + 3, 1, R.WANT_SAMPLE)], ids[:1], want_logits=False)
     assert b.step_logits(0) is None
     a.close()
     b.close()

@@ -74,20 +74,25 @@ def test_config2_decode_flips_at_scale(z2_path):
     ox = run_oracle_filled(O, O.Model(z2_path, O.EXACT), lens, g["fed"], seed)
     oe = run_oracle_filled(O, O.Model(z2_path, O.GGML_EMU), lens, g["fed"], seed)
     flips_gpu = flips_emu = checked = 0
+    worst_flipped, bad = 1.0, []
     for s in range(steps):
         fg = topk_set_flips(g["sel"][s][:, :, :4], ox["sel"][s])       # [28][n]
         flips_gpu += int(fg.sum())
         flips_emu += int(topk_set_flips(oe["sel"][s], ox["sel"][s]).sum())
         for i in range(n):
             c = cos(g["logits"][s, i], ox["logits"][s, i])
-            assert c >= 0.999, (s, i, c)
             if not fg[:, i].any():
                 checked += 1
-                assert c >= 0.9999, (s, i, c)
-                assert max_abs_rel(g["logits"][s, i], ox["logits"][s, i]) <= 1e-2, (s, i)
+                if c < 0.9999 or max_abs_rel(g["logits"][s, i], ox["logits"][s, i]) > 1e-2:
+                    bad.append((s, i, c))
+            else:
+                worst_flipped = min(worst_flipped, c)
     total = steps * n * 28
     print(f"config 2, {n} streams x {steps} steps, ctx {min(lens)}..{max(lens)}: routing decisions {total}; "
           f"GPU vs exact agree {1 - flips_gpu / total:.5f} ({flips_gpu} flips); ggml-emu vs exact agree "
-          f"{1 - flips_emu / total:.5f} ({flips_emu} flips); tokens checked at the logit bars {checked}/{steps * n}")
+          f"{1 - flips_emu / total:.5f} ({flips_emu} flips); tokens with identical routing {checked}/{steps * n}; "
+          f"worst logits cos of a token with a flipped decision {worst_flipped:.5f}")
+    assert not bad, bad[:5]
+    assert worst_flipped >= 0.99                    # a flip changes one expert of one layer, not the model
     assert flips_gpu <= flips_emu, (flips_gpu, flips_emu)
     assert checked >= steps * n // 2

@@ -289,8 +289,7 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
     }
     p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, mode == GM_GATEUP ? 2 : 1, &nw, &p.n_stages, &p.stage_bytes, &smem,
-                  &p.cps);
+    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 1, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
     // blocks per SM the kernel is built for: two for gate/up, three for down
     const int grid = c->m->n_sm * std::min(mode == GM_GATEUP ? 2 : 3, ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);

@@ -7,11 +7,12 @@ the role the reference's single worker loop plays for one device
 (src/server.cpp:1034-1275: admit into a free slot, step all active slots, retire
 finished streams).
 
-Control plane: rank 0 owns the queue and the slot table; once per tick it broadcasts
-each rank's admissions and gathers each rank's finished streams (torch.distributed
-object collectives: gloo on CPU, or the replicas' NCCL group). Admission goes to the
-replica with the most free slots, ties to the lowest rank, so assignments depend only
-on the arrival order.
+Dispatch: a request goes to a replica when it arrives, by its arrival order (request i to
+replica i mod N), so every replica can compute its own queue from the arrival stream and
+no message passes between replicas while they serve. Each replica then runs the
+reference's admission policy locally: arrived requests wait in a FIFO and take the
+lowest free slot (Router over one replica's SlotTable). A replica never waits for
+another; the only collective is one reduction of the totals after serving.
 """
 from __future__ import annotations
 
@@ -168,32 +169,45 @@ class Z2BEngine:
         return fin
 
 
+def dispatch(requests, n_replicas: int, replica: int):
+    """The requests replica `replica` serves: every n_replicas-th arrival, in arrival order."""
+    order = sorted(requests, key=lambda r: (r.arrival_tick, r.rid))
+    return [r for i, r in enumerate(order) if i % n_replicas == replica]
+
+
+def serve_local(engine, requests, slots, clock=None, max_ticks=1_000_000, on_tick=None):
+    """Serve `requests` on one replica until all are done: per tick, admit the arrived
+    requests into free slots (FIFO, lowest slot first), step the engine, retire the
+    finished streams. clock(tick) gives the arrival time a tick has reached (default: the
+    tick itself). Returns (ticks, frames, rids in retirement order)."""
+    router = Router(requests, 1, slots)
+    tick = 0
+    clock = clock or (lambda t: t)
+    while tick < max_ticks and not router.all_done():
+        for a in router.tick(clock(tick))[0]:
+            engine.admit(*a)
+        router.retire([engine.step()])
+        if on_tick:
+            on_tick(tick)
+        tick += 1
+    return tick, engine.frames, router.done
+
+
 def serve(engine, requests, slots_per_replica, max_ticks=1_000_000):
     """Run the request set to completion over all ranks of the default process group
-    (or this process alone without one). Returns (ticks, frames of this rank, rids
-    retired in order on rank 0 / [] elsewhere)."""
+    (or this process alone without one): each rank serves its dispatched share with no
+    communication, then one all-reduce sums the frames and takes the longest tick count.
+    Returns (max ticks, total frames, rids this rank retired)."""
+    import torch
     import torch.distributed as dist
     world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
     rank = dist.get_rank() if world > 1 else 0
-    router = Router(requests, world, slots_per_replica) if rank == 0 else None
-    tick = 0
-    while tick < max_ticks:
-        msg = [None]
-        if rank == 0:
-            msg = [(router.tick(tick), router.all_done())]
-        if world > 1:
-            dist.broadcast_object_list(msg, src=0)
-        admissions, stop = msg[0]
-        if stop:
-            break
-        for a in admissions[rank]:
-            engine.admit(*a)
-        fin = engine.step()
-        gathered = [fin]
-        if world > 1:
-            gathered = [None] * world
-            dist.all_gather_object(gathered, fin)
-        if rank == 0:
-            router.retire(gathered)
-        tick += 1
-    return tick, engine.frames, (router.done if rank == 0 else [])
+    mine = dispatch(requests, world, rank)
+    ticks, frames, done = serve_local(engine, mine, slots_per_replica, max_ticks=max_ticks)
+    if world > 1:
+        t = torch.tensor([ticks, frames], dtype=torch.int64)
+        red = [t.clone(), t.clone()]
+        dist.all_reduce(red[0], op=dist.ReduceOp.MAX)
+        dist.all_reduce(red[1], op=dist.ReduceOp.SUM)
+        ticks, frames = int(red[0][0]), int(red[1][1])
+    return ticks, frames, done
