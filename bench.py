@@ -14,10 +14,14 @@ the device, as the reference's --decode-bench (src/main.cpp:107-157).
 value: frames/s with every step's inputs resident in HBM (z2b_run_schedule: prompt rows
 uploaded before the timed region, decode rows fed back from the device sampler), CUDA
 events on the context's stream; e2e: the same steps through the public z2b_step call
-with host buffers (per step: H2D of the input rows, D2H of the sampled frames).
+with host buffers (per step: H2D of the input rows, D2H of the sampled frames). Both
+arms start from freshly prefilled streams and time the same window of the seeded
+schedule (steps W .. W+K-1), so they see the same refills.
 Weights streamed per step (~6-8 GB) exceed the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --config5 [--gpus N] ...    whole-box serving (config 5), see config5()
+    python bench.py --expert-sweep               the isolated expert op (config 4)
 Under torchrun each rank runs an independent replica on its GPU (replicas only: the
 decode path has no collective); value = frames of all ranks / max rank time.
 """
@@ -163,51 +167,68 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline(path, seconds, cores):
-    """The CPU restatement (oracle, ggml-emu arithmetic) on the host cores: 16 streams with
-    contexts of the benchmark's distribution (KV filled with random f16 instead of a
-    prefill), decode steps until `seconds` have elapsed."""
+def cpu_baseline(path, seconds, cores, warmup):
+    """The CPU restatement (oracle, ggml-emu arithmetic) on the host cores, on the GPU arms'
+    schedule: the same seeded workload, its timed window starting at step `warmup`, decode
+    rows as single-row steps and refill prompts as prefills, until `seconds` have elapsed.
+    The streams' earlier rows (the prefill the GPU arms run outside their timed region) are
+    filled with the integer-hash KV instead of being computed."""
     sys.path.insert(0, ROOT)
     from oracle import oracle as O
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     om = O.Model(path, O.GGML_EMU)
     wl = Workload(seed=1)
+    for _ in range(warmup):                          # the GPU arms' warm-up steps
+        wl.next_step()
     c = O.Ctx(om, STREAMS, CTX_RANGE[1] + STEPS_PER_STREAM + 8)
     for i in range(STREAMS):
-        c.fake_fill(i, int(wl.ctx0[i]), seed=i)
+        c.hash_fill(i, int(wl.n_past[i]), seed=i)
     g = np.random.default_rng(3)
     ids = random_rows(g, STREAMS)
-    past = wl.ctx0.astype(np.int32).copy()
-    c.step(list(range(STREAMS)), past, ids)           # page in the weights
-    past += 1
     steps, t0 = 0, time.time()
     while time.time() - t0 < seconds:
-        lg = c.step(list(range(STREAMS)), past, ids)
-        ids = np.concatenate([lg.argmax(-1).astype(np.int32), np.full((STREAMS, 1), 519, np.int32)], 1)
-        past += 1
+        descs, prompts = wl.next_step()
+        dec = [i for i in range(STREAMS) if prompts[i] is None]
+        nxt = ids.copy()
+        for i in range(STREAMS):
+            if prompts[i] is not None:
+                lg = c.prefill(i, prompts[i])
+                nxt[i, :9] = lg.argmax(-1)
+        if dec:
+            lg = c.step(dec, [int(descs[i][1]) for i in dec], ids[dec])
+            nxt[dec, :9] = lg.argmax(-1)
+        ids = nxt
         steps += 1
     dt = time.time() - t0
     return dict(value=STREAMS * steps / dt, unit="frames/s", cores=cores, kind="port",
-                sample=f"{steps} decode steps x {STREAMS} streams (contexts U[64,2048], KV pre-filled), "
-                       f"oracle/z2o.cpp ggml-emu arithmetic, {dt:.1f}s")
+                sample=f"{steps} steps of the config-2 schedule from step {warmup} ({STREAMS} streams, "
+                       f"contexts U[64,2048], refill prompts prefilled), oracle/z2o.cpp ggml-emu arithmetic, "
+                       f"{dt:.1f}s")
+
+
+def synth_path_in_child(**over):
+    """The synthetic GGUF path, written if needed by a child process, so that the calling
+    process maps none of this repository's product libraries."""
+    code = ("import sys; sys.path.insert(0, %r); import bench; bench.load_pkg(); import z2b.synth as S; "
+            "print(S.cached('zonos2', directory=%r, **%r))" % (ROOT, model_dir(), over))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+    return r.stdout.strip().splitlines()[-1]
 
 
 def run_reference(args, rank, world):
     """Reference arm: the reference's CPU implementation of this path timed on the host. The
     reference cannot be built here (its ggml submodule is not vendored), so this is the
-    CPU restatement in oracle/ on all host threads."""
+    CPU restatement in oracle/ on all host threads, on the GPU arms' workload and config."""
     if rank != 0:
         return
-    z2b = load_pkg()
-    import z2b.synth as S
-    path = S.cached("zonos2", directory=model_dir())
+    path = synth_path_in_child()
     cores = os.cpu_count() or 1
     budget = float(os.environ.get("Z2B_REF_SECONDS", "60"))
-    cb = cpu_baseline(path, budget, cores)
+    cb = cpu_baseline(path, budget, cores, args.warmup)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "frames/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (ggml-emu: int8 activations for quantised weights)",
-            "data": "synthetic", "config": {"workload": workload_name(), "streams": STREAMS},
+            "data": "synthetic", "config": config_dict(args.gpus),
             "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "frames/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -250,9 +271,119 @@ def expert_sweep(args):
     m.close()
 
 
+C5_SLOTS, C5_RATE, C5_PROMPT, C5_GEN, C5_REQUESTS = 32, 50.0, (32, 256), (300, 1500), 8192
+
+
+def config5(args, rank, world, local):
+    """Config 5, whole-box serving: 32 streams per GPU, requests arriving as a Poisson
+    process at 50 req/s over the whole box with prompts U[32, 256] rows and generations
+    U[300, 1500] frames, dealt to the replicas at arrival (zonos2.cpp_b200/replicas.py:
+    request i to replica i mod N, no message between replicas while they serve). Each
+    replica admits arrived requests into free slots (their prompt rows packed into the next
+    decode step), steps its streams through the public z2b_step call and retires finished
+    ones. The box starts in steady state: every slot holds a stream part-way through its
+    generation (its prompt and generated rows prefilled during warm-up). A step is one
+    replica step; value = frames of all replicas in K steps / slowest replica's time."""
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    load_pkg()
+    import z2b.replicas as RP
+    import z2b.runtime as R
+    import z2b.synth as S
+    if rank == 0:
+        path = S.cached("zonos2", directory=model_dir())
+    if dist:
+        dist.barrier()
+    path = S.cached("zonos2", directory=model_dir())
+    model = R.Model(path, device=local if world > 1 else 0)
+    hp = model.hp
+    ctx = R.BatchCtx(model, C5_SLOTS, C5_PROMPT[1] + C5_GEN[1] + 8)
+    ctx.set_logits_readback(False)
+    reqs = RP.poisson_requests(C5_REQUESTS, C5_RATE, C5_PROMPT, C5_GEN, seed=5, whole_ticks=False)
+    g = np.random.default_rng(6)
+    t0 = reqs[C5_SLOTS * world].arrival_tick        # the run starts as the first request past a full box arrives
+    for r in reqs[:C5_SLOTS * world]:               # in flight when the run starts: part-way through
+        done = int(g.integers(0, r.gen_frames))
+        r.prompt_len += done
+        r.gen_frames -= done
+        r.arrival_tick = 0.0
+    for r in reqs[C5_SLOTS * world:]:
+        r.arrival_tick -= t0
+    mine = RP.dispatch(reqs, world, rank)
+    eng = RP.Z2BEngine(ctx, hp, C5_SLOTS, seed=rank)
+    t_start = [time.perf_counter()]
+    rep = RP.Replica(eng, mine, C5_SLOTS, clock=lambda tick: time.perf_counter() - t_start[0])
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local if world > 1 else 0))
+    while len(eng.streams) < C5_SLOTS or any(len(s["rows"]) > 1 for s in eng.streams.values()):
+        rep.tick()                                   # admission of the initial streams (prefill)
+    t_start[0] = time.perf_counter() - 1e-3         # arrivals count from the steady state
+    for _ in range(args.warmup):
+        rep.tick()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0, a0 = eng.frames, rep.router.next_arrival
+    e0.record(stream)
+    for _ in range(args.steps):
+        rep.tick()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    frames = eng.frames - f0
+    admitted = rep.router.next_arrival - a0
+    if dist:
+        t = torch.tensor([ms, frames, admitted], device="cuda", dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ms, frames, admitted = float(mx[0]), float(t[1]), float(t[2])
+    if rank == 0:
+        line = {"metric": "codec frames/s, whole box (config 5: Poisson 50 req/s, 32 streams/GPU)",
+                "value": frames / (ms * 1e-3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16 (mma.sync f16 x f16 -> f32)",
+                "data": "synthetic",
+                "config": {"workload": "config5: ZONOS2-scale Q4_K backbone, 32 streams/GPU, Poisson 50 req/s "
+                                       "over the box, prompts U[32,256], generations U[300,1500], dispatch "
+                                       "i mod N", "parallelism": f"replicas x{world}"},
+                "frames": frames, "requests_arrived_in_window": admitted,
+                "timing": "CUDA events on each replica's stream around K host-driven z2b_step calls "
+                          "(admissions, H2D rows, D2H frames inside); max over replicas"}
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def workload_name():
     return (f"config2: ZONOS2-scale Q4_K backbone, {STREAMS} streams/GPU, ctx U[{CTX_RANGE[0]},{CTX_RANGE[1]}], "
             f"{STEPS_PER_STREAM} frames per stream, continuous refill with {REFILL_PROMPT}-row prompts")
+
+
+def config_dict(world):
+    return {"workload": workload_name(), "global_batch": world * STREAMS, "seq_len": "ctx U[64,2048]",
+            "parallelism": f"replicas x{world}", "model": "zonos2 synthetic (28L, E32 top-4, Q4_K, F16 down)",
+            "l2": "weights streamed per step (GBs) exceed L2; no flush needed", "sampling": "greedy"}
+
+
+def prefill_streams(ctx, R, hp, wl):
+    """Admit the workload's 16 streams with their seeded context rows; returns each
+    stream's first input row (greedy frame of its last prompt row + text pad)."""
+    g = np.random.default_rng(2)
+    first = []
+    for i in range(STREAMS):
+        ctx.slot_reset(i, R.Sampling(greedy=True))
+        lg = ctx.slot_prefill(i, random_rows(g, int(wl.ctx0[i])))
+        first.append(np.r_[lg.argmax(-1), hp.text_vocab])
+    return np.stack(first).astype(np.int32)
 
 
 def main():
@@ -267,6 +398,8 @@ def main():
                     help="fewer layers for small ncu captures (the headline run uses 28)")
     ap.add_argument("--expert-sweep", action="store_true",
                     help="config 4: the isolated expert op over T in {16, 64, 256, 1024, 4096}, one JSON line each")
+    ap.add_argument("--config5", action="store_true",
+                    help="config 5: whole-box serving of Poisson arrivals through the replica dispatcher")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.expert_sweep:
@@ -277,6 +410,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.config5:
+        return config5(args, rank, world, local)
 
     import torch
     dist = None
@@ -303,13 +438,7 @@ def main():
     ctx = R.BatchCtx(model, STREAMS, CTX_RANGE[1] + STEPS_PER_STREAM + 8)
     ctx.set_logits_readback(False)          # frames only, as the device samples
     wl = Workload(seed=1)
-    g = np.random.default_rng(2)
-    first = []
-    for i in range(STREAMS):
-        ctx.slot_reset(i, R.Sampling(greedy=True))
-        lg = ctx.slot_prefill(i, random_rows(g, int(wl.ctx0[i])))
-        first.append(np.r_[lg.argmax(-1), hp.text_vocab])
-    first = np.stack(first).astype(np.int32)
+    first = prefill_streams(ctx, R, hp, wl)
 
     def build_schedule(n_steps, first_rows):
         descs = np.zeros((n_steps, STREAMS, 6))
@@ -353,7 +482,6 @@ def main():
     value_ms = e0.elapsed_time(e1)
     launches = ctx.last_run_launches()
 
-    # ---- kernel breakdown + routed-expert bytes: event-profiled steps of the same workload
     def host_rows(descs, prompts, prev_codes):
         out = []
         for i in range(STREAMS):
@@ -361,7 +489,7 @@ def main():
                        np.r_[prev_codes[i], hp.text_vocab][None].astype(np.int32))
         return np.concatenate(out)
 
-    # frames the device sampled in the last scheduled step feed the host-driven steps
+    # ---- kernel breakdown + routed-expert bytes: event-profiled steps after the timed window
     cur_rows = ctx.last_codes(STREAMS)
     exps = model_expert_bytes(path)
     prof_bytes = {"gateup": 0, "down": 0, "step": 0}
@@ -378,7 +506,11 @@ def main():
         prof_bytes["step"] += w + kv + o
     prof = ctx.profile(False)
 
-    # ---- e2e: public call with host buffers, per step H2D rows + D2H frames
+    # ---- e2e: public call with host buffers, per step H2D rows + D2H frames, on the same
+    # window of the same schedule as `value` (fresh streams, W warm-up steps, K timed steps)
+    wl = Workload(seed=1)
+    first = prefill_streams(ctx, R, hp, wl)
+    cur_rows = first[:, :hp.n_codebooks]
     for s in range(args.warmup):
         dsc, prompts = wl.next_step()
         cur_rows, _ = ctx.step([tuple(x) for x in dsc], host_rows(dsc, prompts, cur_rows), want_logits=False)
@@ -439,10 +571,7 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 (mma.sync f16 x f16 -> f32; Q4_K/F16/Q8_0 weights decoded in registers)",
         "data": "synthetic",
-        "config": {"workload": workload_name(), "global_batch": world * STREAMS, "seq_len": "ctx U[64,2048]",
-                   "parallelism": f"replicas x{world}", "model": "zonos2 synthetic (28L, E32 top-4, Q4_K, F16 down)",
-                   "l2": "weights streamed per step (GBs) exceed L2; no flush needed",
-                   "sampling": "greedy on device"},
+        "config": config_dict(world),
         "per_gpu_frames_per_s": frames_per_step * args.steps / (t_value * 1e-3),
         "roofline": {"bound": "hbm", "kernel": "expert gate/up grouped GEMV + SwiGLU (Q4_K)",
                      "achieved": achieved, "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
@@ -466,7 +595,7 @@ def main():
     if args.layers != 28:
         line["config"]["layers"] = args.layers
     if world == 1 and args.cpu_seconds > 0:
-        line["cpu_baseline"] = cpu_baseline(path, args.cpu_seconds, os.cpu_count() or 1)
+        line["cpu_baseline"] = cpu_baseline(path, args.cpu_seconds, os.cpu_count() or 1, args.warmup)
     print(json.dumps(line), flush=True)
     ctx.close()
     model.close()

@@ -87,6 +87,10 @@ int z2b_ctx_destroy(z2b_ctx* ctx);
 /* Admit a stream into `slot`: frees its KV pages and resets its sampler (history, RNG
  * seeded with sp->seed). sp may be NULL for greedy. */
 int z2b_slot_reset(z2b_ctx* ctx, int slot, const z2b_sampling* sp);
+/* Set a stream's sampler (parameters, mt19937 seeded with sp->seed, empty repetition
+ * history) without touching its KV pages, e.g. after its prefill. The counterpart of
+ * constructing zonos2_sampler (src/zonos2-sampler.cpp:6-7, src/zonos2-graph.cpp:528, 889). */
+int z2b_set_slot_sampling(z2b_ctx* ctx, int slot, const z2b_sampling* sp);
 
 /* Prefill prompt rows ids[n0][10] (int32, row-major) into `slot` from position 0 and
  * return the last row's logits [n_codebooks * audio_vocab] in out_logits.

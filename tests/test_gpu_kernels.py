@@ -46,8 +46,10 @@ def test_gemv_vs_fp32(name, n_tok):
 
 
 def test_pack_prefix_sum_bitexact():
-    """Ragged packing: token t of desc i sits at prefix(n_new)[i] + r with position n_past + r;
-    descs with an output flag get output rows in desc order (their last token)."""
+    """Ragged packing: single-row descs take tokens [0, T_dec) in desc order, then the rows of
+    each prompt chunk follow in desc order (token of row r of a chunk: T_dec + prefix of
+    the chunks' rows + r) with position n_past + r; descs with an output flag get output
+    rows in desc order (their last token)."""
     L = R.lib()
     L.z2b_test_pack.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int] + [ctypes.c_void_p] * 4
     g = np.random.default_rng(5)
@@ -62,9 +64,14 @@ def test_pack_prefix_sum_bitexact():
         ts, tp, to = (np.empty(T, np.int32) for _ in range(3))
         ot = np.empty(max(int(d[:, 3].sum()), 1), np.int32)
         assert L.z2b_test_pack(d.ctypes.data, n, T, ts.ctypes.data, tp.ctypes.data, to.ctypes.data, ot.ctypes.data) == 0
-        start = np.concatenate([[0], np.cumsum(d[:, 2])[:-1]])
-        es = np.repeat(d[:, 0], d[:, 2])
-        ep = np.concatenate([d[i, 1] + np.arange(d[i, 2]) for i in range(n)])
+        dec = d[:, 2] == 1
+        t_dec = int(dec.sum())
+        start = np.where(dec, np.cumsum(dec) - 1, t_dec + np.cumsum(np.where(dec, 0, d[:, 2])) - d[:, 2])
+        es = np.full(T, -1, np.int32)
+        ep = np.full(T, -1, np.int32)
+        for i in range(n):
+            es[start[i]:start[i] + d[i, 2]] = d[i, 0]
+            ep[start[i]:start[i] + d[i, 2]] = d[i, 1] + np.arange(d[i, 2])
         orow = np.cumsum(d[:, 3]) - 1
         eo = np.full(T, -1, np.int32)
         eot = []

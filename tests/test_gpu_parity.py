@@ -274,3 +274,26 @@ def test_step_logits_view(tiny):
     assert b.step_logits(0) is None
     a.close()
     b.close()
+
+
+def test_set_sampling_after_prefill_keeps_the_stream(tiny):
+    """z2b_set_slot_sampling after a prefill (the shim's device-sampling opt-in) samples
+    exactly as a stream whose sampler was set before its prefill, and keeps its KV."""
+    hp = tiny.hp
+    sp = R.Sampling(seed=77, temperature=1.1, top_k=50, min_p=0.1)
+    p = prompt(12, 310)
+    a, b = R.BatchCtx(tiny, 1, 64), R.BatchCtx(tiny, 1, 64)
+    a.slot_reset(0, sp)
+    la = a.slot_prefill(0, p)
+    b.slot_reset(0, R.Sampling(greedy=True))
+    lb = b.slot_prefill(0, p)
+    b.set_sampling(0, sp)
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    ids = np.r_[la.argmax(-1), hp.text_vocab][None].astype(np.int32)
+    for s in range(6):
+        ca, ga = a.step([(0, 12 + s, 1, R.WANT_SAMPLE)], ids)
+        cb, gb = b.step([(0, 12 + s, 1, R.WANT_SAMPLE)], ids)
+        assert np.array_equal(ca, cb) and np.array_equal(ga.view(np.uint32), gb.view(np.uint32))
+        ids = np.r_[ca[0], hp.text_vocab][None].astype(np.int32)
+    a.close()
+    b.close()

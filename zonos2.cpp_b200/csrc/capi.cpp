@@ -88,6 +88,12 @@ int z2b_slot_reset(z2b_ctx* ctx, int slot, const z2b_sampling* sp) {
     return ctx_slot_reset(ctx->c, slot, sp);
 }
 
+int z2b_set_slot_sampling(z2b_ctx* ctx, int slot, const z2b_sampling* sp) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    cudaSetDevice(ctx->c->m->device);
+    return ctx_set_sampling(ctx->c, slot, sp);
+}
+
 int z2b_slot_prefill(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, float* out_logits) {
     if (!ctx || !ids) { set_error("null argument"); return Z2B_ERR_ARG; }
     cudaSetDevice(ctx->c->m->device);

@@ -116,7 +116,12 @@ __global__ void __launch_bounds__(128, 3) attn_kernel(const StepBufs b, const KV
     // this grid runs (each kernel waits on its own predecessor before it releases its
     // dependent), so those chunks are copied before the wait. Q and the keys appended by
     // this step come after it. The token's slot and position load together.
-    const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
+    // block -> (work-list item, kv head): the packer lists the (token, split) pairs that
+    // hold keys first, so every block with work starts in the first wave
+    const int hk = blockIdx.x % dm.n_head_kv, item = blockIdx.x / dm.n_head_kv;
+    if (item >= __ldcg(b.attn_n_items)) return;
+    const int2 ts = __ldcg(b.attn_items + item);
+    const int t = ts.x, sp = ts.y;
     const int slot = __ldcg(b.tok_slot + t), pos = __ldcg(b.tok_pos + t);
     if (slot < 0) return;
     const int n_keys = pos + 1;
@@ -370,7 +375,7 @@ void attn_launch_hg(const StepBufs& b, const KVDev& kv, const Dims& d, int layer
                     int max_split, cudaStream_t s) {
     using SM = AttnSmem<HD>;
     cudaFuncSetAttribute(attn_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM::BYTES);
-    dim3 grid(T, d.n_head_kv, max_split);
+    dim3 grid(T * max_split * d.n_head_kv);       // bound on the work list; blocks past it exit at once
     launch_pdl(attn_kernel<HD, G>, grid, dim3(128), (size_t)SM::BYTES, s, b, kv, d, layer, split_keys);
 }
 

@@ -2,7 +2,9 @@
 // experts that receive many routed tokens in a step (prompt rows, large batches).
 //
 // Replaces ggml_mul_mat_id (src/zonos2-graph.cpp:223-231) for those experts; the tile
-// GEMV in k_gemv.cu keeps the experts with few tokens. Tile = (expert, 128 weight rows,
+// GEMV in k_gemv.cu keeps the experts with few tokens. The same kernel runs the attention
+// projections (ggml_mul_mat, :107-111, 175) over the prompt rows of a step (GM_PROJ: the
+// segments' weights over a contiguous token range, store / add / softcap epilogue). Tile = (expert, 128 weight rows,
 // 64 routed tokens). Per 256-wide K group the four warps dequantise the block's eight
 // 16-row weight tiles (the same in-register decoders as the GEMV, so the weight values
 // are identical) into shared memory in the UMMA K-major interleaved layout, gather the
@@ -139,15 +141,23 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
     pdl_wait();
     pdl_release();
 
-    // experts with GEMM routes: active[n_small .. n_active), routes [seg_mid[e], seg_off[e + 1])
-    const int e_lo = *p.n_small, e_hi = *p.n_active;
-    const int n_rb = (p.out_rows + GT_M - 1) / GT_M;   // 128-row blocks per expert
+    // experts with GEMM routes: active[n_small .. n_active), routes [seg_mid[e], seg_off[e + 1]);
+    // projections (GM_PROJ): the segments' rows over tokens [tok0, tok0 + T)
     const int n_groups = (p.chunks + CPG - 1) / CPG;
     const int n_st = n_groups * NMAT;
-    int n_tiles = 0;
-    for (int a = e_lo; a < e_hi; ++a) {
-        const int e = p.active[a];
-        n_tiles += (p.seg_off[e + 1] - p.seg_mid[e] + GT_N - 1) / GT_N * n_rb;
+    int e_lo = 0, e_hi = 0, n_rb = 0, n_tiles = 0;
+    if constexpr (MODE == GM_PROJ) {
+        e_hi = p.n_seg;
+        for (int a = 0; a < e_hi; ++a)
+            n_tiles += (p.T + GT_N - 1) / GT_N * ((p.seg[a].rows + GT_M - 1) / GT_M);
+    } else {
+        e_lo = *p.n_small;
+        e_hi = *p.n_active;
+        n_rb = (p.out_rows + GT_M - 1) / GT_M;   // 128-row blocks per expert
+        for (int a = e_lo; a < e_hi; ++a) {
+            const int e = p.active[a];
+            n_tiles += (p.seg_off[e + 1] - p.seg_mid[e] + GT_N - 1) / GT_N * n_rb;
+        }
     }
     uint32_t mma_phase = 0;
     int mma_pending = 0;                             // commits not yet waited for
@@ -164,27 +174,41 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
     };
 
     for (int t = blockIdx.x; t < n_tiles && !failed; t += gridDim.x) {
-        int a = e_lo, base = 0, e = 0, ne = 0;
+        int a = e_lo, base = 0, e = 0, ne = 0, nrb = n_rb;
         for (; a < e_hi; ++a) {
-            e = p.active[a];
-            ne = p.seg_off[e + 1] - p.seg_mid[e];
-            const int nt = (ne + GT_N - 1) / GT_N * n_rb;
+            if constexpr (MODE == GM_PROJ) {
+                e = a;
+                ne = p.T;
+                nrb = (p.seg[a].rows + GT_M - 1) / GT_M;
+            } else {
+                e = p.active[a];
+                ne = p.seg_off[e + 1] - p.seg_mid[e];
+            }
+            const int nt = (ne + GT_N - 1) / GT_N * nrb;
             if (t < base + nt) break;
             base += nt;
         }
-        const int tb = (t - base) / n_rb, rb = (t - base) % n_rb;
-        const int tok0 = p.seg_mid[e] + tb * GT_N;
+        const int tb = (t - base) / nrb, rb = (t - base) % nrb;
+        int tok0;
+        if constexpr (MODE == GM_PROJ) tok0 = p.tok0 + tb * GT_N;
+        else tok0 = p.seg_mid[e] + tb * GT_N;
         const int nv = min(GT_N, ne - tb * GT_N);
         const int rt = rb * GT_WARPS_ROWS + warp;        // this warp's row tile
-        const bool rt_ok = rt < p.n_row_tiles;
+        int n_row_tiles = p.n_row_tiles;
+        const uint8_t* wsrc0 = p.w0 + (size_t)e * p.expert_stride;
+        const uint8_t* wsrc1 = p.w1 + (size_t)e * p.expert_stride;
+        if constexpr (MODE == GM_PROJ) {
+            n_row_tiles = p.seg[e].n_row_tiles;
+            wsrc0 = p.seg[e].tiles;
+        }
+        const bool rt_ok = rt < n_row_tiles;
 
         // raw stage s -> this warp's ring slot s % RAW_NS
         auto issue_raw = [&](int s) {
             if (lane == 0 && rt_ok) {
                 const int g = s / NMAT, m = s % NMAT, c0 = g * CPG, nc = min(CPG, p.chunks - c0);
                 uint64_t* bar = &raw_bar[warp][s % ns];
-                const uint8_t* src = (m == 0 ? p.w0 : p.w1) + (size_t)e * p.expert_stride +
-                                     ((size_t)rt * p.chunks + c0) * p.tile_bytes;
+                const uint8_t* src = (m == 0 ? wsrc0 : wsrc1) + ((size_t)rt * p.chunks + c0) * p.tile_bytes;
                 mbar_expect_tx(bar, (uint32_t)(nc * p.tile_bytes));
                 bulk_g2s(myraw + (size_t)(s % ns) * stage_bytes, src, (uint32_t)(nc * p.tile_bytes), bar);
             }
@@ -276,6 +300,7 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
         if (!failed) {
             // epilogue: warp w reads TMEM lanes 32 (w % 4).., token columns 32 (w / 4) ..
             const int row = rb * GT_M + 32 * (warp & 3) + lane;
+            const int row_lim = MODE == GM_PROJ ? p.seg[e].rows : p.out_rows;
             const uint32_t lane_addr = tm + ((uint32_t)(32 * (warp & 3)) << 16);
 #pragma unroll 1
             for (int c = 32 * (warp >> 2); c < 32 * (warp >> 2) + 32; c += 16) {
@@ -285,11 +310,16 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int n = c + i;
-                    if (n >= nv || row >= p.out_rows) continue;
+                    if (n >= nv || row >= row_lim) continue;
                     if constexpr (MODE == GM_GATEUP) {
                         const float gt = v0[i], up = v1[i];
                         const float si = gt / (1.0f + expf(-gt));
                         p.yout[(size_t)(tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
+                    } else if constexpr (MODE == GM_PROJ) {
+                        float* o = p.out + (size_t)(tok0 + n) * p.ldo + p.seg[e].out_off + row;
+                        if (p.epi == EPI_ADD) *o = v0[i] + *o;
+                        else if (p.epi == EPI_SOFTCAP) *o = tanhf(v0[i] * (1.0f / p.cap)) * p.cap;
+                        else *o = v0[i];
                     } else {
                         p.out[(size_t)(tok0 + n) * p.ldo + row] = v0[i] * p.route_w[tok0 + n];
                     }
@@ -316,6 +346,7 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
 template <int WT, int KSF>
 void gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
     void (*k)(const GemvParams) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
+                                  : p.mode == GM_PROJ ? moe_gemm_kernel<WT, KSF, GM_PROJ>
                                                       : moe_gemm_kernel<WT, KSF, GM_DOWN>;
     constexpr int CPG = GT_K / DecSel<WT, KSF>::T::KC;
     // deepest raw ring (up to RAW_NS stages) that fits next to A and the two B buffers

@@ -122,10 +122,9 @@ __device__ __forceinline__ int x_row(const GemvParams& p, const ItemRef& it, int
     else return it.tok0 + n;
 }
 
-// Token tiles per pass: 2 (up to 16 tokens) for the projections, 1 (8 tokens) for the
-// expert passes, which see 1-4 tokens per expert at decode (an expert with more takes
-// several passes over the same weight stage); the down pass's lighter registers let three
-// blocks share an SM, gate/up keeps its two-stage ring at two blocks per SM.
+// Token tiles per pass: 2 (up to 16 tokens) for the projections and gate/up, 1 for the
+// down pass, whose lighter registers let three blocks share an SM (measured: gate/up
+// keeps its two-stage ring at two blocks per SM; down gains from the third block).
 template <int WT, int KSF, int MODE, int NTG, int MAXT, int MINB>
 __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     using D = typename DecSel<WT, KSF>::T;
@@ -331,19 +330,15 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
                         make_float4(acc[m][nt][0], acc[m][nt][1], acc[m][nt][2], acc[m][nt][3]);
             __syncthreads();
             red_par ^= 1;
-            // outputs map token-major onto threads (thread t: token t / 16 of the pass, row
-            // t % 16), so a pass with few tokens keeps few warps busy here
             for (int t = threadIdx.x; t < NTG * 128; t += blockDim.x) {
-                const int nl = t >> 4, rr = t & 15;
-                const int n = g * 8 * NTG + nl;
-                if (n >= it.n_tok) break;                // later t of this thread: later tokens
-                const int nt = nl >> 3, nn = nl & 7;
-                const int ln = (rr & 7) * 4 + (nn >> 1), e = (rr >> 3) * 2 + (nn & 1);
+                const int nt = t >> 7, ln = (t & 127) >> 2, e = t & 3;
+                const int rr = (ln >> 2) + 8 * (e >> 1);
+                const int n = g * 8 * NTG + nt * 8 + 2 * (ln & 3) + (e & 1);
+                if (n >= it.n_tok) continue;
                 float v[NMAT];
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m) {
                     float sum = 0.0f;
-#pragma unroll 8
                     for (int w = 0; w < NW; ++w) sum += rbuf[(((size_t)w * NMAT + m) * NTG + nt) * 128 + ln * 4 + e];
                     v[m] = sum;
                 }
@@ -392,7 +387,7 @@ template <int WT, int KSF>
 void launch_typed(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s) {
     void (*k)(const GemvParams);
     if (p.mode == GM_PROJ) k = gemv_kernel<WT, KSF, GM_PROJ, 2, 512, 1>;
-    else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP, 1, 256, 2>;
+    else if (p.mode == GM_GATEUP) k = gemv_kernel<WT, KSF, GM_GATEUP, 2, 256, 2>;
     else k = gemv_kernel<WT, KSF, GM_DOWN, 1, 256, 3>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     launch_pdl(k, dim3(grid), dim3(nwarps * 32), (size_t)smem, s, p);

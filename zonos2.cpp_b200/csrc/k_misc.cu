@@ -13,50 +13,81 @@ namespace z2b {
 namespace {
 
 // ---------------------------------------------------------------- packer
-// Device-side ragged packing: exclusive prefix sum over the per-stream row counts gives
-// each stream's token range; every token gets (slot, logical position, input row) and
+// Device-side ragged packing: prefix sums over the per-stream row counts give each
+// stream's token range; every token gets (slot, logical position, input row) and
 // streams that want logits get an output row. Replaces the host fill of ids / pos /
 // mask in zonos2_batch_step (src/zonos2-graph.cpp:784-812); no dense mask is built,
-// attention reads each token's slot and position directly.
+// attention reads each token's slot and position directly. Single-row descriptors
+// (decode) take tokens [0, T_dec) in descriptor order and the rows of prompt chunks
+// follow, so the projections can run the decode rows on the tile GEMV and the prompt
+// rows on the tensor-core GEMM. Input rows and output rows stay in descriptor order.
 __global__ void pack_kernel(const StepBufs b, int T) {
-    __shared__ int s_start[1024], s_out[1024];
+    __shared__ int s_in[1024], s_out[1024], s_dec[1024], s_prm[1024];
     const int n = b.n_desc, tid = threadIdx.x;
     if (tid == 0) *b.err = 0;          // first kernel of a step: clear the error word
     auto n_out_of = [](const SlotDesc& d) {
         return (d.flags & SD_OUTPUT) ? ((d.flags & SD_ALL_ROWS) ? d.n_new : 1) : 0;
     };
     if (tid < n) {
-        s_start[tid] = b.descs[tid].n_new;
-        s_out[tid] = n_out_of(b.descs[tid]);
+        const SlotDesc d = b.descs[tid];
+        s_in[tid] = d.n_new;
+        s_out[tid] = n_out_of(d);
+        s_dec[tid] = d.n_new == 1 ? 1 : 0;
+        s_prm[tid] = d.n_new == 1 ? 0 : d.n_new;
     }
     __syncthreads();
     // Hillis-Steele inclusive scans (n <= 1024)
     for (int off = 1; off < n; off <<= 1) {
-        int a = 0, c = 0;
-        if (tid < n && tid >= off) { a = s_start[tid - off]; c = s_out[tid - off]; }
+        int a = 0, c = 0, e = 0, f = 0;
+        if (tid < n && tid >= off) { a = s_in[tid - off]; c = s_out[tid - off]; e = s_dec[tid - off]; f = s_prm[tid - off]; }
         __syncthreads();
-        if (tid < n && tid >= off) { s_start[tid] += a; s_out[tid] += c; }
+        if (tid < n && tid >= off) { s_in[tid] += a; s_out[tid] += c; s_dec[tid] += e; s_prm[tid] += f; }
         __syncthreads();
     }
+    const int t_dec = n > 0 ? s_dec[n - 1] : 0;
     for (int i = tid; i < n; i += blockDim.x) {
         const SlotDesc d = b.descs[i];
-        const int start = s_start[i] - d.n_new;
+        const int in0 = s_in[i] - d.n_new;                                // first input row
+        const int start = d.n_new == 1 ? s_dec[i] - 1 : t_dec + s_prm[i] - d.n_new;   // first token
         const bool all = (d.flags & SD_ALL_ROWS) != 0;
         const int orow = (d.flags & SD_OUTPUT) ? s_out[i] - 1 : -1;    // the desc's last row
         const int obase = orow >= 0 ? s_out[i] - n_out_of(d) : -1;
         b.desc_out[i] = orow;
         for (int r = 0; r < d.n_new; ++r) {
             const int t = start + r;
-            if (t >= T) { atomicOr(b.err, (uint32_t)DERR_BOUNDS); break; }
+            if (t >= T || in0 + r >= T) { atomicOr(b.err, (uint32_t)DERR_BOUNDS); break; }
             b.tok_slot[t] = d.slot;
             b.tok_pos[t] = d.n_past + r;
             b.tok_desc[t] = i;
             b.tok_out[t] = orow < 0 ? -1 : (all ? obase + r : (r == d.n_new - 1 ? orow : -1));
-            for (int c = 0; c < NCOL; ++c) b.ids[t * NCOL + c] = b.ids_in[t * NCOL + c];
+            for (int c = 0; c < NCOL; ++c) b.ids[t * NCOL + c] = b.ids_in[(in0 + r) * NCOL + c];
         }
         if (orow >= 0)
             for (int o = obase; o <= orow; ++o) { b.out_tok[o] = start + d.n_new - 1 - (orow - o); b.out_desc[o] = i; }
     }
+    // Attention work list: token t needs ceil((pos + 1) / split_keys) split blocks; the
+    // (token, split) pairs are listed in token order, so the attention grid's blocks with
+    // work come first and start in one wave.
+    __syncthreads();                   // every token's position is written
+    const int per = (T + blockDim.x - 1) / blockDim.x;
+    const int t0 = min(T, tid * per), t1 = min(T, t0 + per);
+    int cnt = 0;
+    auto n_splits = [&](int t) { return min(max(b.tok_pos[t], 0) / b.split_keys + 1, b.max_split); };
+    for (int t = t0; t < t1; ++t) cnt += n_splits(t);
+    s_in[tid] = cnt;
+    __syncthreads();
+    for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+        const int a = tid >= off ? s_in[tid - off] : 0;
+        __syncthreads();
+        s_in[tid] += a;
+        __syncthreads();
+    }
+    int item = s_in[tid] - cnt;
+    for (int t = t0; t < t1; ++t) {
+        const int ns = n_splits(t);
+        for (int sp = 0; sp < ns; ++sp) b.attn_items[item++] = make_int2(t, sp);
+    }
+    if (tid == (int)blockDim.x - 1) *b.attn_n_items = s_in[tid];
 }
 
 // ---------------------------------------------------------------- embedding
@@ -512,7 +543,9 @@ extern "C" int z2b_test_pack(const int32_t* desc4, int n, int T, int32_t* tok_sl
     if (tsum != T) return 1;
     StepBufs b{};
     void* base = nullptr;
-    const size_t bytes = (size_t)n * sizeof(SlotDesc) + (size_t)T * NCOL * 4 * 2 + (size_t)T * 16 + (size_t)n * 12 + 4096;
+    constexpr int kTestSplits = 64;               // positions below 64 * 256 in the test descriptors
+    const size_t bytes = (size_t)n * sizeof(SlotDesc) + (size_t)T * NCOL * 4 * 2 + (size_t)T * 16 + (size_t)n * 12 +
+                         (size_t)T * kTestSplits * 8 + 8192;
     if (cudaMalloc(&base, bytes) != cudaSuccess) return 4;
     cudaMemset(base, 0, bytes);
     uint8_t* p = (uint8_t*)base;
@@ -524,6 +557,8 @@ extern "C" int z2b_test_pack(const int32_t* desc4, int n, int T, int32_t* tok_sl
     b.tok_slot = (int*)take(T * 4); b.tok_pos = (int*)take(T * 4); b.tok_desc = (int*)take(T * 4);
     b.tok_out = (int*)take(T * 4); b.out_tok = (int*)take(n * 4); b.out_desc = (int*)take(n * 4);
     b.desc_out = (int*)take(n * 4); b.err = (uint32_t*)take(4);
+    b.attn_items = (int2*)take((size_t)T * kTestSplits * 8); b.attn_n_items = (int*)take(4);
+    b.split_keys = PAGE; b.max_split = kTestSplits;
     cudaMemcpy((void*)b.descs, d.data(), n * sizeof(SlotDesc), cudaMemcpyHostToDevice);
     pack_kernel<<<1, 1024>>>(b, T);
     int rc = 0;

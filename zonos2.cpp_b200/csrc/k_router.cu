@@ -60,9 +60,11 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 // Which part a route joins depends on bulk_mode:
 //   0: none take the GEMM;
 //   1: all routes of an expert with >= GEMM_MIN_TOKENS routes (the isolated expert op);
-//   2: the routes of prompt rows, i.e. tokens whose descriptor feeds more than one row
-//      (the decode step). A token's path then depends on the token alone, so packing
-//      other streams into the step never changes its result.
+//   2: the routes of prompt rows (tokens whose descriptor feeds more than one row) of
+//      experts with >= GEMM_MIN_PROMPT_ROUTES such routes (the decode step); an expert
+//      with fewer takes them in its GEMV pass, which streams its weights anyway. Decode
+//      rows always take the GEMV, and the choice for prompt rows depends on the step's
+//      prompt routes only, so packing decode streams into a step never changes a result.
 // active[0, n_small) lists the experts with GEMV routes, active[n_small, n_active) those
 // with GEMM routes (an expert can be in both). tile_off (optional): prefix over the GEMV
 // list of ceil(routes / 8).
@@ -100,6 +102,8 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
     __syncthreads();
     if (bulk_mode == 1)
         for (int e = threadIdx.x; e < E; e += blockDim.x) cntb[e] = cnt[e] >= GEMM_MIN_TOKENS ? cnt[e] : 0;
+    if (bulk_mode == 2)
+        for (int e = threadIdx.x; e < E; e += blockDim.x) if (cntb[e] < GEMM_MIN_PROMPT_ROUTES) cntb[e] = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     if (w == 0) {
@@ -170,7 +174,7 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
                     bk = se == e && bulk_mode == 2 && tok_bulk(r / k);
                 }
                 if (se == e && bulk_mode != 0) {
-                    const bool b = bulk_mode == 1 ? cntb[e] > 0 : bk;
+                    const bool b = cntb[e] > 0 && (bulk_mode == 1 || bk);
                     if (b != (part == 1)) se = -1;
                 }
                 const unsigned m = __ballot_sync(0xffffffffu, se == e);

@@ -11,6 +11,10 @@ namespace z2b {
 constexpr int MAX_EXPERTS = 256;
 constexpr int GEMM_MIN_TOKENS = 17;  // isolated expert op: routes from which an expert takes the
                                      // tensor-core GEMM (the GEMV holds at most 16 tokens per pass)
+constexpr int PROJ_GEMM_MIN_ROWS = 17;      // prompt rows from which a step's projections run them
+                                            // on the tensor-core GEMM (the GEMV holds 16 per pass)
+constexpr int GEMM_MIN_PROMPT_ROUTES = 33;  // decode step: prompt-row routes from which an expert's
+                                            // prompt routes take the GEMM (fewer join its GEMV pass)
 constexpr int NCOL = 10;            // input columns per row: 9 audio codebooks + text
 constexpr int PAGE = 256;           // KV page length (tokens)
 
@@ -54,6 +58,7 @@ struct GemvParams {
     // activations
     const __half* X; int ldx;       // GM_PROJ / GM_GATEUP: [T][ldx]; GM_DOWN: y [routes][ldx]
     int T;                          // GM_PROJ token count
+    int tok0;                       // GM_PROJ on the tensor-core GEMM: first token of the range
     float* out; int ldo;            // GM_PROJ / GM_DOWN output (f32)
     __half* yout; int ldy;          // GM_GATEUP output y (f16)
     int out_rows;                   // valid rows per expert (GM_GATEUP / GM_DOWN)
@@ -124,6 +129,9 @@ struct StepBufs {
     __half* qh;                     // [T][nh][hd]
     float* apart; int max_split;    // [T][nh][max_split][hd+2]
     int* attn_ticket;               // [T][nkv] split arrivals (zero between steps)
+    int2* attn_items;               // [T * max_split] attention work list: (token, split), token order
+    int* attn_n_items;              // [1] entries of the work list
+    int split_keys;                 // keys per attention split
     __half* o;                      // [T][nh*hd]
     float* rstate;                  // [T][rd]
     float* rpart; int rpart_T;      // [4][rpart_T][rd] router down-projection partial sums

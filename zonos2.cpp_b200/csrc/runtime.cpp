@@ -127,6 +127,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
     acc((MAX_EXPERTS + 1) * 4);
     acc(4);
     acc(MAX_EXPERTS * 4);
+    acc((size_t)T * c->max_split * 8); acc(4);
     uint8_t* base = (uint8_t*)dal(need);
     if (!base) { set_error("step buffer allocation failed"); return Z2B_ERR_OOM; }
     CK(cudaMemset(base, 0, need));
@@ -158,6 +159,9 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
     B.tile_off = carve<int>(p, MAX_EXPERTS + 1);
     B.n_small = carve<int>(p, 1);
     B.seg_mid = carve<int>(p, MAX_EXPERTS);
+    B.attn_items = carve<int2>(p, (size_t)T * c->max_split);
+    B.attn_n_items = carve<int>(p, 1);
+    B.split_keys = c->split_keys;
 
     c->kv.pool = c->kv_pool;
     c->kv.page_table = (const int*)(c->d_stage + c->st_pt);
@@ -199,6 +203,11 @@ int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp) {
     for (int pg : c->slot_pages[slot]) c->free_pages.push_back(pg);
     c->slot_pages[slot].clear();
     for (int i = 0; i < c->pages_per_slot; ++i) c->h_pt[(size_t)slot * c->pages_per_slot + i] = -1;
+    return ctx_set_sampling(c, slot, sp);
+}
+
+int ctx_set_sampling(Ctx* c, int slot, const z2b_sampling* sp) {
+    if (slot < 0 || slot >= c->n_slots) { set_error("slot out of range"); return Z2B_ERR_ARG; }
     SampDev& s = c->h_samp[slot];
     if (sp) {
         if (sp->rep_window < 0 || sp->rep_window > Z2B_MAX_REP_WINDOW) { set_error("rep_window out of range"); return Z2B_ERR_ARG; }
@@ -240,9 +249,16 @@ struct ProfScope {
 
 int ctas_per_sm(int smem) { return std::max(1, std::min(4, 233472 / (smem + 1024))); }
 
+// Projection of T rows (tokens or output rows). With t_dec >= 0 the rows are a step's
+// tokens, decode rows [0, t_dec) first: when the prompt rows [t_dec, T) are many, they run
+// on the tensor-core GEMM and the tile GEMV keeps the decode rows, so a decode row's result
+// never depends on what else the step carries.
 void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int T, const __half* X, int ldx,
-               float* out, int ldo, int epi, float cap, int cls) {
+               float* out, int ldo, int epi, float cap, int cls, int t_dec = -1) {
     ProfScope ps(c, cls);
+    bool gemm_ok = t_dec >= 0 && T - t_dec >= PROJ_GEMM_MIN_ROWS;
+    for (int i = 0; i < nmat; ++i) gemm_ok = gemm_ok && moe_gemm_supported(*mats[i]);
+    const int T_gemv = gemm_ok ? t_dec : T;
     GemvParams p{};
     p.mode = GM_PROJ; p.epi = epi;
     p.type = mats[0]->type; p.K = mats[0]->K; p.chunks = mats[0]->chunks;
@@ -254,12 +270,20 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
         items += mats[i]->n_row_tiles;
     }
     p.total_items = items;
-    p.X = X; p.ldx = ldx; p.T = T; p.out = out; p.ldo = ldo; p.cap = cap; p.err = c->B.err;
-    int nw, smem;
-    gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps, &p.x_rs);
-    const int grid = std::min(items, c->m->n_sm * ctas_per_sm(smem));
-    launch_gemv(p, nw, grid, smem, c->stream);
-    c->launches++;
+    p.X = X; p.ldx = ldx; p.T = T_gemv; p.out = out; p.ldo = ldo; p.cap = cap; p.err = c->B.err;
+    if (T_gemv > 0) {
+        int nw, smem;
+        gemv_geometry(*mats[0], 1, 2, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps, &p.x_rs);
+        const int grid = std::min(items, c->m->n_sm * ctas_per_sm(smem));
+        launch_gemv(p, nw, grid, smem, c->stream);
+        c->launches++;
+    }
+    if (gemm_ok) {
+        p.tok0 = t_dec;
+        p.T = T - t_dec;
+        launch_moe_gemm(p, c->m->n_sm, c->stream);
+        c->launches++;
+    }
 }
 
 // Expert pass (gate/up + SwiGLU, or down x route weight) over the routes of the step:
@@ -289,7 +313,8 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
     }
     p.err = c->B.err;
     int nw, smem;
-    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, 1, &nw, &p.n_stages, &p.stage_bytes, &smem, &p.cps);
+    gemv_geometry(w0, mode == GM_GATEUP ? 2 : 1, mode == GM_GATEUP ? 2 : 1, &nw, &p.n_stages, &p.stage_bytes, &smem,
+                  &p.cps);
     // blocks per SM the kernel is built for: two for gate/up, three for down
     const int grid = c->m->n_sm * std::min(mode == GM_GATEUP ? 2 : 3, ctas_per_sm(smem));
     launch_gemv(p, nw, grid, smem, c->stream);
@@ -325,19 +350,20 @@ void enqueue_step(Ctx* c, int T, int n_out) {
         if (ly.qkvg_fused) {
             const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
             const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
-            gemv_proj(c, mats, offs, 4, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV);
+            gemv_proj(c, mats, offs, 4, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV, c->cur_t_dec);
         } else {
             const DevMat* mats[4] = {&ly.wq, &ly.wk, &ly.wv, &ly.wgate};
             const int offs[4] = {0, nh * hd, nh * hd + nkv * hd, nh * hd + 2 * nkv * hd};
             for (int i = 0; i < 4; ++i)
-                gemv_proj(c, &mats[i], &offs[i], 1, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV);
+                gemv_proj(c, &mats[i], &offs[i], 1, T, B.cur, D.n_embd, B.qkvg, B.ldq, EPI_STORE, 0.0f, PC_QKV,
+                          c->cur_t_dec);
         }
         { ProfScope ps(c, PC_ROPE); launch_rope_append(B, c->kv, ly.small.attn_temp, D, L, T, c->stream); c->launches++; }
         { ProfScope ps(c, PC_ATTN); launch_attention(B, c->kv, D, L, T, c->split_keys, c->max_split, c->stream); c->launches++; }
         {
             const DevMat* mats[1] = {&ly.wo};
             const int offs[1] = {0};
-            gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f, PC_WO);
+            gemv_proj(c, mats, offs, 1, T, B.o, nh * hd, B.res, D.n_embd, EPI_ADD, 0.0f, PC_WO, c->cur_t_dec);
         }
         if (c->rcap_on && c->d_rcap && ly.is_moe) {
             const size_t per = (size_t)D.n_embd + D.rd;
@@ -371,12 +397,20 @@ void enqueue_step(Ctx* c, int T, int n_out) {
 }
 
 int run_step(Ctx* c, int T, int n_out) {
-    // graphs for decode-only shapes (T == streams); steps carrying prompt rows run eagerly
-    const bool use_graph = c->graphs_enabled && !c->profiling && !c->rcap_on && T == c->cur_n_desc && c->spk_t < 0;
-    if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
-    const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48);
+    // Every launch of a step is fixed by (rows, output rows, descriptors, decode rows): steps
+    // replay a CUDA graph per such shape. Decode-only shapes are captured at once; a shape
+    // carrying prompt rows on its second occurrence (repeated refill shapes replay, one-off
+    // prompt lengths run eagerly), up to kMaxPromptGraphs of them.
+    constexpr int kMaxPromptGraphs = 32;
+    bool use_graph = c->graphs_enabled && !c->profiling && !c->rcap_on && c->spk_t < 0;
+    const uint64_t key = ((uint64_t)T << 32) | (uint32_t)n_out | ((uint64_t)c->cur_n_desc << 48) |
+                         ((uint64_t)c->cur_t_dec << 16);
     auto it = c->graphs.find(key);
+    if (use_graph && T != c->cur_n_desc && it == c->graphs.end())
+        use_graph = ++c->shape_seen[key] >= 2 && c->prompt_graphs < kMaxPromptGraphs;
+    if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
     if (it == c->graphs.end()) {
+        if (T != c->cur_n_desc) c->prompt_graphs++;
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
         enqueue_step(c, T, n_out);
@@ -398,7 +432,7 @@ int run_step(Ctx* c, int T, int n_out) {
 int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_desc, int* T_out, int* n_out_out) {
     const Dims& D = c->m->dims;
     if (n < 1 || n > c->D_max) { set_error("number of descs out of range"); return Z2B_ERR_ARG; }
-    int T = 0, n_out = 0;
+    int T = 0, n_out = 0, t_dec = 0;
     std::vector<char> seen(c->n_slots, 0);
     for (int i = 0; i < n; ++i) {
         const z2b_slot_desc& d = descs[i];
@@ -409,6 +443,7 @@ int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_de
         if (d.n_past + d.n_new + extra_rows_per_desc > c->slot_cap) { set_error("stream exceeds slot capacity"); return Z2B_ERR_ARG; }
         if (d.cfg_twin >= n || d.cfg_twin == i) { set_error("bad cfg_twin"); return Z2B_ERR_ARG; }
         T += d.n_new;
+        t_dec += d.n_new == 1 ? 1 : 0;
         if (d.flags & Z2B_WANT_LOGITS) n_out += c->all_rows ? d.n_new : 1;
     }
     if (T > c->T_max) { set_error("rows per step exceed capacity (" + std::to_string(c->T_max) + ")"); return Z2B_ERR_ARG; }
@@ -443,6 +478,7 @@ int ctx_prepare(Ctx* c, const z2b_slot_desc* descs, int n, int extra_rows_per_de
     }
     (void)D;
     c->cur_n_desc = n;
+    c->cur_t_dec = t_dec;
     *T_out = T;
     *n_out_out = n_out;
     return Z2B_OK;
@@ -662,7 +698,7 @@ int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, con
     const int ncb = D.n_codebooks;
     if (n_steps < 1 || n < 1 || n > c->D_max || n > c->O_max || !descs || !row_src) { set_error("bad schedule arguments"); return Z2B_ERR_ARG; }
     std::vector<int> need(c->n_slots, 0);
-    std::vector<int> T(n_steps, 0);
+    std::vector<int> T(n_steps, 0), T_dec(n_steps, 0);
     for (int s = 0; s < n_steps; ++s) {
         std::vector<char> seen(c->n_slots, 0);
         for (int i = 0; i < n; ++i) {
@@ -679,6 +715,7 @@ int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, con
             seen[d.slot] = 1;
             need[d.slot] = std::max(need[d.slot], d.n_past + d.n_new);
             T[s] += d.n_new;
+            T_dec[s] += d.n_new == 1 ? 1 : 0;
         }
         if (T[s] > c->T_max) { set_error("schedule step exceeds rows per step"); return Z2B_ERR_ARG; }
     }
@@ -745,6 +782,7 @@ int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, con
                               c->B.codes, c->d_sched_rows, c->d_canon_all + per * s, d_canon, ncb, D.text_vocab,
                               c->stream);
         }
+        c->cur_t_dec = T_dec[s];
         const int rc = run_step(c, T[s], n);
         if (rc) return rc;
         total_launches += c->launches + 1;

@@ -49,6 +49,8 @@ struct Ctx {
     std::vector<char> step_has_logits;
     std::vector<int> desc_out_host;
     int cur_n_desc = 0;
+    int cur_t_dec = 0;                       // single-row (decode) descriptors of the current step:
+                                             // tokens [0, cur_t_dec), prompt rows after them
     int last_T = 0;                          // tokens of the last z2b_step
     size_t last_h2d = 0, last_d2h = 0;       // bytes copied by the last z2b_step
     bool keep_logits = true;                 // read logits back even without out_logits
@@ -62,6 +64,8 @@ struct Ctx {
     bool graphs_enabled = true;
     std::map<uint64_t, cudaGraphExec_t> graphs;
     std::map<uint64_t, int> graph_launches;
+    std::map<uint64_t, int> shape_seen;      // occurrences of step shapes carrying prompt rows
+    int prompt_graphs = 0;
     int launches = 0, loop_launches = 0;
     // decode-loop uniforms
     double* d_canon_all = nullptr;
@@ -98,6 +102,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
 // Teacher-forced logits of every row of one sequence (zonos2_logits): out [n][ncb][av].
 int model_logits(Model* m, const int32_t* ids, int n, const float* spk, int spk_pos, const float* delta, float* out);
 int ctx_slot_reset(Ctx* c, int slot, const z2b_sampling* sp);
+int ctx_set_sampling(Ctx* c, int slot, const z2b_sampling* sp);
 int ctx_step(Ctx* c, const z2b_slot_desc* descs, int n, const int32_t* ids, int32_t* out_codes, float* out_logits);
 int ctx_prefill(Ctx* c, int slot, const int32_t* ids, int n0, float* out_logits);
 // Prefill with an optional speaker embedding replacing the embedding of prompt row spk_pos

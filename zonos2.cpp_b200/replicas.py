@@ -16,9 +16,8 @@ another; the only collective is one reduction of the totals after serving.
 """
 from __future__ import annotations
 
-import heapq
 from collections import deque
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 
@@ -28,17 +27,19 @@ class Request:
     rid: int
     prompt_len: int
     gen_frames: int
-    arrival_tick: int = 0
+    arrival_tick: float = 0                           # tick, or seconds for wall-clock arrivals
 
 
-def poisson_requests(n, rate_per_tick, prompt_range, gen_range, seed=0):
+def poisson_requests(n, rate_per_tick, prompt_range, gen_range, seed=0, whole_ticks=True):
     """n requests with exponential inter-arrival times (Poisson arrivals at
     rate_per_tick), prompt lengths and generation lengths uniform in the given
-    inclusive ranges."""
+    inclusive ranges. Arrival times are whole ticks, or (whole_ticks=False) real
+    values, e.g. seconds for a rate per second."""
     g = np.random.default_rng(seed)
     t = np.cumsum(g.exponential(1.0 / rate_per_tick, n))
     return [Request(i, int(g.integers(prompt_range[0], prompt_range[1] + 1)),
-                    int(g.integers(gen_range[0], gen_range[1] + 1)), int(t[i])) for i in range(n)]
+                    int(g.integers(gen_range[0], gen_range[1] + 1)), int(t[i]) if whole_ticks else float(t[i]))
+            for i in range(n)]
 
 
 class SlotTable:
@@ -132,11 +133,12 @@ class Z2BEngine:
     as prompt rows (synthetic ids: the prompt builder is not on this path), decode
     streams feed back their sampled frame, greedy sampling on the device."""
 
-    def __init__(self, ctx, hp, n_slots: int, seed: int = 0):
+    def __init__(self, ctx, hp, n_slots: int, seed: int = 0, max_rows: int = 4096):
         self.ctx, self.hp, self.n_slots = ctx, hp, n_slots
         self.g = np.random.default_rng(seed)
         self.streams = {}                              # rid -> dict(slot, n_past, left, rows)
         self.frames = 0
+        self.max_rows = max_rows                       # rows one step may carry (prompts wait beyond it)
 
     def admit(self, rid, slot, prompt_len, gen_frames):
         from . import runtime as R
@@ -149,12 +151,15 @@ class Z2BEngine:
         from . import runtime as R
         if not self.streams:
             return []
-        rids = sorted(self.streams, key=lambda r: self.streams[r]["slot"])
-        descs, rows = [], []
-        for rid in rids:
+        rids, descs, rows, n_rows = [], [], [], 0
+        for rid in sorted(self.streams, key=lambda r: self.streams[r]["slot"]):
             s = self.streams[rid]
+            if n_rows > 0 and n_rows + len(s["rows"]) > self.max_rows and len(s["rows"]) > 1:
+                continue                               # this prompt waits for a later step
+            rids.append(rid)
             descs.append((s["slot"], s["n_past"], len(s["rows"]), R.WANT_SAMPLE))
             rows.append(s["rows"])
+            n_rows += len(s["rows"])
         codes, _ = self.ctx.step(descs, np.concatenate(rows), want_logits=False)
         fin = []
         for i, rid in enumerate(rids):
@@ -175,22 +180,34 @@ def dispatch(requests, n_replicas: int, replica: int):
     return [r for i, r in enumerate(order) if i % n_replicas == replica]
 
 
-def serve_local(engine, requests, slots, clock=None, max_ticks=1_000_000, on_tick=None):
-    """Serve `requests` on one replica until all are done: per tick, admit the arrived
-    requests into free slots (FIFO, lowest slot first), step the engine, retire the
-    finished streams. clock(tick) gives the arrival time a tick has reached (default: the
-    tick itself). Returns (ticks, frames, rids in retirement order)."""
-    router = Router(requests, 1, slots)
-    tick = 0
-    clock = clock or (lambda t: t)
-    while tick < max_ticks and not router.all_done():
-        for a in router.tick(clock(tick))[0]:
-            engine.admit(*a)
-        router.retire([engine.step()])
-        if on_tick:
-            on_tick(tick)
-        tick += 1
-    return tick, engine.frames, router.done
+class Replica:
+    """One replica's serving loop: per tick, admit the arrived requests into free slots
+    (FIFO, lowest slot first), step the engine, retire the finished streams. clock(tick)
+    gives the arrival time a tick has reached (default: the tick itself)."""
+
+    def __init__(self, engine, requests, slots, clock=None):
+        self.engine = engine
+        self.router = Router(requests, 1, slots)
+        self.clock = clock or (lambda t: t)
+        self.ticks = 0
+
+    def tick(self):
+        for a in self.router.tick(self.clock(self.ticks))[0]:
+            self.engine.admit(*a)
+        self.router.retire([self.engine.step()])
+        self.ticks += 1
+
+    def done(self) -> bool:
+        return self.router.all_done()
+
+
+def serve_local(engine, requests, slots, clock=None, max_ticks=1_000_000):
+    """Serve `requests` on one replica until all are done. Returns (ticks, frames, rids in
+    retirement order)."""
+    rep = Replica(engine, requests, slots, clock)
+    while rep.ticks < max_ticks and not rep.done():
+        rep.tick()
+    return rep.ticks, engine.frames, rep.router.done
 
 
 def serve(engine, requests, slots_per_replica, max_ticks=1_000_000):

@@ -74,6 +74,7 @@ def lib():
             "z2b_ctx_create": ([P, I, I, ctypes.POINTER(P)], I),
             "z2b_ctx_destroy": ([P], I),
             "z2b_slot_reset": ([P, I, ctypes.POINTER(Sampling)], I),
+            "z2b_set_slot_sampling": ([P, I, ctypes.POINTER(Sampling)], I),
             "z2b_slot_prefill": ([P, I, V, I, V], I),
             "z2b_slot_prefill_spk": ([P, I, V, I, V, I, V, V], I),
             "z2b_logits": ([P, V, I, V, V, I, V], I),
@@ -201,6 +202,10 @@ class BatchCtx:
 
     def slot_reset(self, slot: int, sampling: Sampling | None = None):
         _check(lib().z2b_slot_reset(self.h, slot, ctypes.byref(sampling) if sampling else None))
+
+    def set_sampling(self, slot: int, sampling: Sampling | None = None):
+        """The stream's sampler (parameters, seed, empty history), keeping its KV."""
+        _check(lib().z2b_set_slot_sampling(self.h, slot, ctypes.byref(sampling) if sampling else None))
 
     def slot_prefill(self, slot: int, ids, spk=None, spk_pos: int = 0, spk_emotion_delta=None) -> np.ndarray:
         """zonos2_batch_slot_prefill: returns the last prompt row's logits [ncb, av]. With
