@@ -578,7 +578,8 @@ def main():
                      "frac": achieved / hbm, "traffic": traffic,
                      "algorithmic_bytes_per_launch": gu_iso_bytes, "avg_launch_ms": gu_iso_ms,
                      "timing": f"CUDA events on the launching stream around {reps} back-to-back launches "
-                               "cycling over the 28 layers' weights, routing of the last timed step"},
+                               "cycling over the 28 layers, each on its own weights and its own routing of "
+                               "the last decode step"},
         "expert_down_roofline": {"achieved": dn_iso_bytes / (dn_iso_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                                  "frac": dn_iso_bytes / (dn_iso_ms * 1e-3) / 1e9 / hbm,
                                  "algorithmic_bytes_per_launch": dn_iso_bytes, "avg_launch_ms": dn_iso_ms},

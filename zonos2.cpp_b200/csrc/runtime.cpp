@@ -290,8 +290,19 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
 // the tile GEMV takes each expert's routes [seg_off, seg_mid); when the step can have
 // routes for the tcgen05 GEMM (bulk: prompt rows, or a large expert-op batch) the GEMM
 // takes [seg_mid, seg_off + 1).
-void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
+// Expert segment arrays a pass reads (the step buffers' own, or a saved copy).
+struct SegSet {
+    const int *n_active, *n_small, *active, *seg_off, *seg_mid, *tile_off, *route_tok;
+    const float* route_w;
+};
+
+SegSet step_segs(const StepBufs& B) {
+    return SegSet{B.n_active, B.n_small, B.active, B.seg_off, B.seg_mid, B.tile_off, B.route_tok, B.route_w};
+}
+
+void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk, const SegSet* segs = nullptr) {
     ProfScope ps(c, mode == GM_GATEUP ? PC_GATEUP : PC_DOWN);
+    const SegSet sg = segs ? *segs : step_segs(c->B);
     const Dims& D = c->m->dims;
     GemvParams p{};
     const DevMat& w0 = mode == GM_GATEUP ? ly.gate_exps : ly.down_exps;
@@ -302,10 +313,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
     p.w1 = mode == GM_GATEUP ? ly.up_exps.tiles : nullptr;
     p.expert_stride = w0.expert_stride;
     const bool split = bulk && ly.small.gemm_ok;
-    p.n_active = c->B.n_small;
-    p.n_small = c->B.n_small;
-    p.active = c->B.active; p.seg_off = c->B.seg_off; p.seg_mid = c->B.seg_mid; p.tile_off = c->B.tile_off;
-    p.route_tok = c->B.route_tok; p.route_w = c->B.route_w;
+    p.n_active = sg.n_small;
+    p.n_small = sg.n_small;
+    p.active = sg.active; p.seg_off = sg.seg_off; p.seg_mid = sg.seg_mid; p.tile_off = sg.tile_off;
+    p.route_tok = sg.route_tok; p.route_w = sg.route_w;
     if (mode == GM_GATEUP) {
         p.X = c->B.cur; p.ldx = D.n_embd; p.yout = c->B.y; p.ldy = D.n_ff; p.out_rows = D.n_ff;
     } else {
@@ -320,7 +331,7 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
     launch_gemv(p, nw, grid, smem, c->stream);
     c->launches++;
     if (split) {
-        p.n_active = c->B.n_active;
+        p.n_active = sg.n_active;
         launch_moe_gemm(p, c->m->n_sm, c->stream);
         c->launches++;
     }
@@ -328,7 +339,6 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk) {
 
 }  // namespace
 
-void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode) { gemv_moe(c, ly, mode, false); }
 
 void enqueue_step(Ctx* c, int T, int n_out) {
     Model* m = c->m;
@@ -851,35 +861,64 @@ int ctx_sync(Ctx* c) {
 
 namespace z2b {
 
-// Re-launches one expert GEMV class (0 = gate/up, 1 = down) `reps` times, cycling over
-// the MoE layers so every launch streams a different layer's weights, on the routing
-// state the last step left in the step buffers (its final MoE layer). Back-to-back
-// launches with CUDA events on the context's stream around the whole loop; returns the average
-// duration per launch and the algorithmic bytes per launch (routed experts' weights +
-// activations in + results out).
+// Times one expert GEMV class (0 = gate/up, 1 = down) over the MoE layers, each on its own
+// weights and its own routing of the last step: the router ids every layer chose (the
+// step's router log) are turned into that layer's expert segments and kept, then `reps`
+// launches cycle over the layers back to back between CUDA events on the context's
+// stream. Returns the average duration per launch and the average algorithmic bytes per
+// launch (routed experts' weights + activations in + results out).
 int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch) {
     Model* m = c->m;
+    const Dims& D = m->dims;
     std::vector<int> moe;
     for (int L = 0; L < (int)m->layers.size(); ++L)
         if (m->layers[L].is_moe) moe.push_back(L);
     if (moe.empty() || reps < 1 || c->last_T < 1) { set_error("time_expert_gemv: needs a MoE model and a previous step"); return Z2B_ERR_ARG; }
-    int n_active = 0, routes = 0;
-    CK(cudaMemcpyAsync(&n_active, c->B.n_active, 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
-    const LayerDev& l0 = m->layers[moe.back()];
-    CK(cudaMemcpy(&routes, c->B.seg_off + l0.n_expert, 4, cudaMemcpyDeviceToHost));
-    const Dims& D = m->dims;
-    const DevMat& w = which == 0 ? l0.gate_exps : l0.down_exps;
-    const uint64_t per_expert = (uint64_t)w.n_row_tiles * w.chunks * w.tile_bytes * (which == 0 ? 2 : 1);
-    const uint64_t act = which == 0 ? (uint64_t)routes * D.n_embd * 2 + (uint64_t)routes * D.n_ff * 2
-                                    : (uint64_t)routes * D.n_ff * 2 + (uint64_t)routes * D.n_embd * 4;
+    const int T = c->last_T, km = c->kmax, R = T * km, E = MAX_EXPERTS;
+    const int nl = (int)moe.size();
+    // per layer: n_active, n_small | active[E] | seg_off[E+1] | seg_mid[E] | tile_off[E+1] | route_tok[R] | route_w[R]
+    const size_t per = 2 + E + (E + 1) + E + (E + 1) + 2 * (size_t)R;
+    int* save = nullptr;
+    CK(cudaMalloc(&save, per * nl * 4));
+    std::unique_ptr<int, decltype(&cudaFree)> own(save, cudaFree);
+    std::vector<SegSet> sets(nl);
+    std::vector<float> ones((size_t)R, 1.0f);
+    StepBufs B = c->B;
+    CK(cudaMemcpyAsync(B.selw, ones.data(), (size_t)R * 4, cudaMemcpyHostToDevice, c->stream));
+    uint64_t bytes = 0;
+    for (int i = 0; i < nl; ++i) {
+        const LayerDev& ly = m->layers[moe[i]];
+        CK(cudaMemcpyAsync(B.sel, B.sel_log + (size_t)moe[i] * B.sel_log_T * km, (size_t)R * 4, cudaMemcpyDeviceToDevice,
+                           c->stream));
+        launch_segments(B, T, ly.top_k, ly.n_expert, 0, c->stream);
+        int* q = save + per * i;
+        int *na = q, *ns = q + 1, *act = q + 2, *so = act + E, *sm = so + E + 1, *to = sm + E, *rt = to + E + 1;
+        float* rw = reinterpret_cast<float*>(rt + R);
+        auto d2d = [&](void* dst, const void* src, size_t n) {
+            return cudaMemcpyAsync(dst, src, n, cudaMemcpyDeviceToDevice, c->stream);
+        };
+        CK(d2d(na, B.n_active, 4)); CK(d2d(ns, B.n_small, 4)); CK(d2d(act, B.active, E * 4));
+        CK(d2d(so, B.seg_off, (E + 1) * 4)); CK(d2d(sm, B.seg_mid, E * 4)); CK(d2d(to, B.tile_off, (E + 1) * 4));
+        CK(d2d(rt, B.route_tok, (size_t)R * 4)); CK(d2d(rw, B.route_w, (size_t)R * 4));
+        sets[i] = SegSet{na, ns, act, so, sm, to, rt, rw};
+        int n_active = 0, routes = 0;
+        CK(cudaMemcpyAsync(&n_active, B.n_active, 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaMemcpyAsync(&routes, B.seg_off + ly.n_expert, 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        const DevMat& w = which == 0 ? ly.gate_exps : ly.down_exps;
+        const uint64_t per_expert = (uint64_t)w.n_row_tiles * w.chunks * w.tile_bytes * (which == 0 ? 2 : 1);
+        const uint64_t act_bytes = which == 0 ? (uint64_t)routes * D.n_embd * 2 + (uint64_t)routes * D.n_ff * 2
+                                              : (uint64_t)routes * D.n_ff * 2 + (uint64_t)routes * D.n_embd * 4;
+        bytes += (uint64_t)n_active * per_expert + act_bytes;
+    }
     cudaEvent_t e0, e1;
     CK(cudaEventCreate(&e0));
     CK(cudaEventCreate(&e1));
     const bool prof = c->profiling;
     c->profiling = false;
     CK(cudaEventRecord(e0, c->stream));
-    for (int r = 0; r < reps; ++r) gemv_moe_public(c, m->layers[moe[r % moe.size()]], which == 0 ? GM_GATEUP : GM_DOWN);
+    for (int r = 0; r < reps; ++r)
+        gemv_moe(c, m->layers[moe[r % nl]], which == 0 ? GM_GATEUP : GM_DOWN, false, &sets[r % nl]);
     CK(cudaEventRecord(e1, c->stream));
     CK(cudaEventSynchronize(e1));
     c->profiling = prof;
@@ -888,7 +927,7 @@ int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uin
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     *ms_per_launch = ms / reps;
-    *bytes_per_launch = (uint64_t)n_active * per_expert + act;
+    *bytes_per_launch = bytes / nl;
     return Z2B_OK;
 }
 

@@ -117,7 +117,6 @@ int ctx_run_schedule(Ctx* c, int n_steps, int n, const z2b_slot_desc* descs, con
 enum ProfClass { PC_PACK, PC_EMBED, PC_QKV, PC_ROPE, PC_ATTN, PC_ATTN_COMB, PC_WO, PC_ROUTER, PC_GATEUP, PC_DOWN,
                  PC_COMBINE, PC_HEAD, PC_SAMPLER, PC_FEED, PC_N };
 void account(Ctx* c, const z2b_slot_desc* descs, int n, int T);
-void gemv_moe_public(Ctx* c, const LayerDev& ly, int mode);
 int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uint64_t* bytes_per_launch);
 int ctx_debug_fill_kv(Ctx* c, int slot, int n, uint32_t seed);
 int ctx_debug_router_capture(Ctx* c, int enable);
