@@ -278,7 +278,18 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     float* rn = rh + rd;             // [rd]
     float* h0 = rn + rd;             // [rd]
     float* pr = h0 + rd;             // [MAX_EXPERTS]
-    float* wst = pr + MAX_EXPERTS;   // staged m0 [rd][rd], m2 [rd][rd], m4 [E][rd]
+    // static vectors, copied before the wait so no load of them sits on the critical path:
+    // router_down bias | eda scale | router norm | mlp0 bias | mlp2 bias ([rd] each),
+    // balancing bias | mask ([MAX_EXPERTS] each), ffn_norm [d]
+    float* v_rdb = pr + MAX_EXPERTS;
+    float* v_eda = v_rdb + rd;
+    float* v_rnorm = v_eda + rd;
+    float* v_m0b = v_rnorm + rd;
+    float* v_m2b = v_m0b + rd;
+    float* v_rbias = v_m2b + rd;
+    float* v_rmask = v_rbias + MAX_EXPERTS;
+    float* v_fn = v_rmask + MAX_EXPERTS;
+    float* wst = v_fn + d;           // staged m0 [rd][rd], m2 [rd][rd], m4 [E][rd]
     const bool staged = ly.is_moe && stage;
     if (staged) {
         if (threadIdx.x == 0) {
@@ -294,28 +305,42 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
         W2 = wst + rd * rd;
         W4 = wst + 2 * rd * rd;
     }
+    for (int j = threadIdx.x; j < d / 4; j += blockDim.x)
+        reinterpret_cast<float4*>(v_fn)[j] = reinterpret_cast<const float4*>(ly.ffn_norm)[j];
+    if (ly.is_moe) {
+        for (int i = threadIdx.x; i < rd; i += blockDim.x) {
+            v_rdb[i] = ly.rdown_b[i];
+            v_eda[i] = ly.eda ? ly.eda[i] : 0.0f;
+            v_rnorm[i] = ly.rnorm[i];
+            v_m0b[i] = ly.m0_b[i];
+            v_m2b[i] = ly.m2_b[i];
+        }
+        for (int e = threadIdx.x; e < E; e += blockDim.x) {
+            v_rbias[e] = ly.rbias[e];
+            v_rmask[e] = ly.rmask ? ly.rmask[e] : 0.0f;
+        }
+    }
     const bool active = __ldcg(b.tok_slot + t) >= 0;        // packer output, complete before the predecessor
     pdl_wait();
     // the router projection's inputs load with the residual row: partial sums over the K
-    // slices, bias, and the previous MoE layer's state
-    float pa = 0.0f, pb = 0.0f, pst = 0.0f, ped = 0.0f;
+    // slices and the previous MoE layer's state
+    float pa = 0.0f, pst = 0.0f;
     const bool eda_on = ly.is_moe && ly.eda && !first_moe;
     if (ly.is_moe && threadIdx.x < rd) {
         const int i = threadIdx.x;
         for (int ks = 0; ks < router_kslices(d); ++ks) pa += b.rpart[((size_t)ks * b.rpart_T + t) * rd + i];
-        pb = ly.rdown_b[i];
-        if (eda_on) { pst = b.rstate[(size_t)t * rd + i]; ped = ly.eda[i]; }
+        if (eda_on) pst = b.rstate[(size_t)t * rd + i];
     }
 
     // ffn_norm -> cur (f16)
     const float4* r4 = reinterpret_cast<const float4*>(b.res + (size_t)t * d);
     float ss = 0.0f;
     for (int j = threadIdx.x; j < d / 4; j += blockDim.x) { const float4 v = r4[j]; ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
-    ss = block_sum(ss, red);
+    ss = block_sum(ss, red);                                  // its barriers also publish the staged vectors
     const float sc = 1.0f / sqrtf(ss / (float)d + dm.rms_eps);
     for (int j = threadIdx.x; j < d / 4; j += blockDim.x) {
         const float4 r = r4[j];
-        const float4 f = reinterpret_cast<const float4*>(ly.ffn_norm)[j];
+        const float4 f = reinterpret_cast<const float4*>(v_fn)[j];
         __half2* o = reinterpret_cast<__half2*>(b.cur + (size_t)t * d) + 2 * j;
         o[0] = __floats2half2_rn((r.x * sc) * f.x, (r.y * sc) * f.y);
         o[1] = __floats2half2_rn((r.z * sc) * f.z, (r.w * sc) * f.w);
@@ -326,8 +351,8 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     if (ly.is_moe) {
         if (threadIdx.x < rd) {
             const int i = threadIdx.x;
-            float v = pa * sc + pb;
-            if (eda_on) v = v + pst * ped;
+            float v = pa * sc + v_rdb[i];
+            if (eda_on) v = v + pst * v_eda[i];
             rh[i] = v;
             b.rstate[(size_t)t * rd + i] = v;
         }
@@ -336,37 +361,35 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
         for (int i = threadIdx.x; i < rd; i += blockDim.x) s2 += rh[i] * rh[i];
         s2 = block_sum(s2, red);
         const float sc2 = 1.0f / sqrtf(s2 / (float)rd + dm.rms_eps);
-        for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = (rh[i] * sc2) * ly.rnorm[i];
+        for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = (rh[i] * sc2) * v_rnorm[i];
         if (staged) ok = mbar_wait(&bar, 0, b.err);
         __syncthreads();
         if (ok) {
             block_matvec(W0, rn, h0, rd, rd);
             __syncthreads();
-            for (int i = threadIdx.x; i < rd; i += blockDim.x) h0[i] = gelu_erf(h0[i] + ly.m0_b[i]);
+            for (int i = threadIdx.x; i < rd; i += blockDim.x) h0[i] = gelu_erf(h0[i] + v_m0b[i]);
             __syncthreads();
             block_matvec(W2, h0, rn, rd, rd);        // rn reused as h2
             __syncthreads();
-            for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = gelu_erf(rn[i] + ly.m2_b[i]);
+            for (int i = threadIdx.x; i < rd; i += blockDim.x) rn[i] = gelu_erf(rn[i] + v_m2b[i]);
             __syncthreads();
             block_matvec(W4, rn, pr, E, rd);
         }
         __syncthreads();
         if (w == 0 && ok) {
-            // softmax (ggml: sum in double, scale by the rounded reciprocal), one warp
+            // softmax (ggml: sum in double, scale by the rounded reciprocal), one warp: exp per
+            // lane, the double sum over a fixed lane tree
             float mx = -INFINITY;
             for (int e = lane; e < E; e += 32) {
-                if (ly.rmask) pr[e] = pr[e] + ly.rmask[e];
+                if (ly.rmask) pr[e] = pr[e] + v_rmask[e];
                 mx = fmaxf(mx, pr[e]);
             }
             mx = warp_max(mx);
-            __syncwarp();
-            if (lane == 0) {
-                double sum = 0.0;
-                for (int e = 0; e < E; ++e) { const float v = expf(pr[e] - mx); pr[e] = v; sum += (double)v; }
-                red[0] = (float)(1.0 / sum);
-            }
-            __syncwarp();
-            const float inv = red[0];
+            double sum = 0.0;
+            for (int e = lane; e < E; e += 32) { const float v = expf(pr[e] - mx); pr[e] = v; sum += (double)v; }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            const float inv = (float)(1.0 / sum);
             for (int e = lane; e < E; e += 32) pr[e] = pr[e] * inv;
             __syncwarp();
             // top-k over probs + bias (+ mask), ties to the lower expert id: k rounds of
@@ -377,8 +400,8 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
                 const int e = lane + 32 * i;
                 float v = -INFINITY;
                 if (e < E) {
-                    v = pr[e] + ly.rbias[e];
-                    if (ly.rmask) v = v + ly.rmask[e];
+                    v = pr[e] + v_rbias[e];
+                    if (ly.rmask) v = v + v_rmask[e];
                 }
                 sv[i] = v;
             }
@@ -457,9 +480,9 @@ __global__ void route_test_kernel(const int* sel, const float* selw, int T, int 
 constexpr int kMaxRouterDevices = 64;
 
 size_t router_mlp_smem(const Dims& d, int E, bool* stage) {
-    const size_t base = (size_t)(3 * d.rd + MAX_EXPERTS) * sizeof(float);
+    const size_t base = (size_t)(8 * d.rd + 3 * MAX_EXPERTS + d.n_embd) * sizeof(float);
     const size_t w = (size_t)(2 * d.rd * d.rd + E * d.rd) * sizeof(float);
-    *stage = base + w <= 160 * 1024;
+    *stage = base + w <= 190 * 1024;
     return *stage ? base + w : base;
 }
 
