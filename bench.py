@@ -249,7 +249,7 @@ def expert_sweep(args):
     tflops_peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))).get("bf16_tflops", 1590.0) \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
     E, k, d, ff = m.hp.n_expert, 4, m.hp.n_embd, m.hp.n_ff
-    for T in (16, 64, 256, 1024, 4096):
+    for T in (args.sweep_t or (16, 64, 256, 1024, 4096)):
         g = np.random.default_rng(T)
         x = g.standard_normal((T, d)).astype(np.float32)
         bias = np.log(1.0 / np.arange(1, E + 1) ** 1.1)[g.permutation(E)]
@@ -398,6 +398,8 @@ def main():
                     help="fewer layers for small ncu captures (the headline run uses 28)")
     ap.add_argument("--expert-sweep", action="store_true",
                     help="config 4: the isolated expert op over T in {16, 64, 256, 1024, 4096}, one JSON line each")
+    ap.add_argument("--sweep-t", type=int, nargs="*", default=None,
+                    help="with --expert-sweep: only these token counts (small ncu captures)")
     ap.add_argument("--config5", action="store_true",
                     help="config 5: whole-box serving of Poisson arrivals through the replica dispatcher")
     args = ap.parse_args()

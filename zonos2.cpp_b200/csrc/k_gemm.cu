@@ -4,18 +4,29 @@
 // Replaces ggml_mul_mat_id (src/zonos2-graph.cpp:223-231) for those experts; the tile
 // GEMV in k_gemv.cu keeps the experts with few tokens. The same kernel runs the attention
 // projections (ggml_mul_mat, :107-111, 175) over the prompt rows of a step (GM_PROJ: the
-// segments' weights over a contiguous token range, store / add / softcap epilogue). Tile = (expert, 128 weight rows,
-// 64 routed tokens). Per 256-wide K group the four warps dequantise the block's eight
-// 16-row weight tiles (the same in-register decoders as the GEMV, so the weight values
-// are identical) into shared memory in the UMMA K-major interleaved layout, gather the
-// tokens' activation rows next to them, and one thread issues tcgen05.mma (M 128, N 64,
-// K 16, f16 x f16 -> f32) into tensor-memory accumulators; a tcgen05.commit on an
-// mbarrier tells the block when the operands may be overwritten. The epilogue reads the
-// accumulators with tcgen05.ld: SwiGLU to f16 y (gate/up), or x route weight (down).
+// segments' weights over a contiguous token range, store / add / softcap epilogue).
+//
+// Tile = (expert, 128 weight rows, up to 256 routed tokens); the MMA is M 128 x N (the
+// tile's token count rounded up to 16) x K 16, f16 x f16 -> f32 in tensor memory (TMEM:
+// gate at columns [0, 256), up at [256, 512)). A persistent block walks its tiles with
+// warp-specialised roles that hand over through mbarriers, never a block-wide barrier:
+//   - 8 decode warps, one per 16-row weight tile of the block. Each lane-0 streams its
+//     row tile's quantised chunks (cp.async.bulk, one chunk of one matrix per ring slot,
+//     continuing into the block's next tile); the warp decodes a 64-wide K stage of a
+//     chunk with the same in-register decoders as the GEMV (so the weight values are
+//     identical) and stores it into an A ring slot in the UMMA K-major layout with
+//     conflict-free 16-byte stores. The same warps gather the tiles' activation rows
+//     (cp.async, two stages ahead) into a B ring and run the epilogue.
+//   - 1 MMA warp: one lane waits for each stage's A and B, issues four tcgen05.mma and
+//     releases the slots with tcgen05.commit; after a tile's last stage it commits to the
+//     accumulator barrier the epilogue waits on.
+// A stage covers, per lane quarter q of the decoders, k = chunk*KC + q*KC/4 + 16j + [0,16):
+// four 16-wide runs of the chunk (the tile layout's fragment order); B gathers the same k
+// runs in the same order, so the contraction is over the same 64 k values.
 //
 // Shared-memory operand layout (K-major, no swizzle): 8x8 core matrices of 16-byte rows;
-// element (m, k) of a block at (k / 8) * LBO + (m / 8) * 128 + (m % 8) * 16 + (k % 8) * 2
-// with LBO = 128 * rows / 8 (2048 B for 128 weight rows, 1024 B for 64 tokens).
+// element (m, k) of a slot at (k / 8) * LBO + (m / 8) * 128 + (m % 8) * 16 + (k % 8) * 2
+// with LBO = 128 * rows / 8 (2048 B for the 128 weight rows, 4096 B for 256 tokens).
 #include "common.cuh"
 #include "gguf.h"
 #include "kernels.h"
@@ -30,25 +41,66 @@ namespace z2b {
 namespace {
 
 constexpr int GT_M = 128;                        // weight rows per tile
-constexpr int GT_N = 64;                         // routed tokens per tile
-constexpr int GT_K = 256;                        // k per dequantised group
-constexpr int GT_WARPS_ROWS = GT_M / 16;         // 16-row weight tiles per 128-row block
-constexpr int A_BYTES = GT_M * GT_K * 2;         // 64 KB per matrix
-constexpr int B_BYTES = GT_N * GT_K * 2;         // 32 KB
-constexpr uint32_t A_LBO = GT_M / 8 * 128, B_LBO = GT_N / 8 * 128, CORE_SBO = 128;
-// instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, N, M
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(GT_N >> 3) << 17) | ((uint32_t)(GT_M >> 4) << 24);
+constexpr int NT_MAX = 256;                      // routed tokens per tile (MMA N <= 256)
+constexpr int KG = 64;                           // K per stage
+constexpr int DQW = 8;                           // decode warps (16 weight rows each)
+constexpr int BQW = 2;                           // activation (B) producer warps (alternate stages)
+constexpr int GM_THREADS = 32 * (DQW + 1 + BQW); // + the MMA warp + the B producers
+constexpr int NA = 2;                            // A ring slots (one stage of one matrix)
+constexpr int NB = 4;                            // B ring slots (one stage of activations)
+constexpr int MAX_RR = 6;                        // raw chunk ring slots per decode warp
+// A (decoded weights, no swizzle): K-direction stride between 8-wide core-matrix columns,
+// padded by 16 bytes so that the 8 lanes of a quarter-warp storing one 16-byte row each
+// (two rows x four k-columns) hit 8 distinct bank groups.
+constexpr uint32_t A_LBO = GT_M / 8 * 128 + 16, CORE_SBO = 128;
+constexpr int A_SLOT = (int)A_LBO * (KG / 8);    // 16.1 KB
+// B (activations, 128-byte swizzle): token n's 64 k values are one 128-byte row at n * 128,
+// its 16-byte chunk c stored at chunk c ^ (n % 8); 8-token atoms of 1024 B.
+constexpr int B_SLOT = NT_MAX * KG * 2;          // 32 KB
+
+// instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, N, M 128
+__device__ __forceinline__ uint32_t idesc_n(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GT_M >> 4) << 24);
+}
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(CORE_SBO >> 4) << 32) |
            (1ull << 46);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+// K-major, 128-byte swizzle: leading offset unused (1), 1024 B between 8-row atoms; the
+// K16 slices of a 64-wide stage start 32 B apart inside the 128-byte rows.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Activation rows [r0, r1) of X (row stride ldx) copied to Xp (row stride K) in stage
+// order: within each KC-wide chunk, stage j's 64 values k = q*KC/4 + 16j + [0, 16) for
+// q = 0..3 become the contiguous run [64j, 64j + 64), so a GEMM stage of one token is one
+// 128-byte line. 16-byte pieces, one per thread.
+template <int KC>
+__global__ void gemm_x_stage_order_kernel(const __half* __restrict__ X, int ldx, int r0, int r1, int K,
+                                          __half* __restrict__ Xp) {
+    pdl_wait();
+    const int ppr = K / 8;                           // pieces per row
+    const long total = (long)(r1 - r0) * ppr;
+    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int row = r0 + (int)(i / ppr), pc = (int)(i % ppr);
+        const int kd = pc * 8, c = kd / KC, rem = kd % KC;
+        const int j = rem / 64, q = (rem % 64) / 16, h = (rem % 16) / 8;
+        const int ks = c * KC + q * (KC / 4) + 16 * j + 8 * h;
+        *reinterpret_cast<uint4*>(Xp + (size_t)row * K + kd) = *reinterpret_cast<const uint4*>(X + (size_t)row * ldx + ks);
+    }
+    pdl_release();
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-        :: "r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate) : "memory");
+        :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate) : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -58,6 +110,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -71,68 +127,140 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Decode k-steps s..KS-1 of one 16-row tile chunk into the A block: lane (r, q) holds
-// rows r and r + 8 at k = kq + 4s with kq = kofs + q * KC / 4 a multiple of 8, so each
-// store lands at a compile-time offset from the lane's two base pointers:
-// (s / 2) * A_LBO + (s % 2) * 8 bytes.
-template <class D, int s, int KS> struct DqLoop {
-    __device__ __forceinline__ static void run(const D& dec, const uint8_t* T, int lane, uint8_t* b0, uint8_t* b1) {
-        uint32_t a[4];
-        dec.template frag<s>(T, lane, a);
-        *reinterpret_cast<uint2*>(b0 + (s >> 1) * A_LBO + (s & 1) * 8) = make_uint2(a[0], a[2]);
-        *reinterpret_cast<uint2*>(b1 + (s >> 1) * A_LBO + (s & 1) * 8) = make_uint2(a[1], a[3]);
-        DqLoop<D, s + 1, KS>::run(dec, T, lane, b0, b1);
+// Bounded wait that also gives up as soon as another role of the block has given up.
+__device__ __forceinline__ bool wait_ab(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* ab) {
+    for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*ab) return false;
     }
-};
-template <class D, int KS> struct DqLoop<D, KS, KS> {
-    __device__ __forceinline__ static void run(const D&, const uint8_t*, int, uint8_t*, uint8_t*) {}
-};
-
-// The lane's two base pointers into A for a chunk at k offset kofs (rows row0 + r, + 8).
-template <int KC>
-__device__ __forceinline__ void dq_bases(uint8_t* A, int lane, int row0, int kofs, uint8_t** b0, uint8_t** b1) {
-    const int r = lane >> 2, q = lane & 3;
-    const int kq8 = (kofs + q * (KC / 4)) >> 3;
-    *b0 = A + kq8 * A_LBO + ((row0 + r) >> 3) * 128 + ((row0 + r) & 7) * 16;
-    *b1 = A + kq8 * A_LBO + ((row0 + r + 8) >> 3) * 128 + ((row0 + r + 8) & 7) * 16;
+    if (err) atomicOr(err, (uint32_t)DERR_WAIT_TIMEOUT);
+    *ab = 1;
+    return false;
 }
 
-constexpr int GM_WARPS = 8;                      // one 16-row weight tile per warp
-constexpr int RAW_NS = 3;                        // raw weight stages per warp (K groups ahead)
+__device__ __forceinline__ void st16(uint8_t* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(a, b, c, d);
+}
 
-// Per tile: the (K group g, matrix m) stages stream in order s = g * NMAT + m. Each warp
-// bulk-copies its own 16-row tile's chunks of stage s into a ring up to RAW_NS stages
-// ahead; the activation rows of group g are gathered with cp.async into one of two B
-// buffers a group ahead; the single A buffer is rewritten once the MMAs of the previous
-// stage have released it (tcgen05.commit -> mma_bar), then one thread issues the stage's
-// MMAs.
+// Decode k-steps S0..S0+3 of this warp's 16-row tile chunk into an A slot. Lane (r, q)
+// holds rows r and r + 8 at chunk k = q*KC/4 + 4s + [0, 4); in the slot they go to local
+// k = 16q + 4(s - S0) + [0, 4), two k-steps per 16-byte core-matrix row. The 32 lanes of
+// one store cover 32 distinct 16-byte rows (4 per bank group), the minimum 4 wavefronts.
+template <class D, int S0>
+__device__ __forceinline__ void dq_stage(const D& dec, const uint8_t* T, int lane, uint8_t* As, int warp) {
+    uint32_t a0[4], a1[4], a2[4], a3[4];
+    dec.template frag<S0 + 0>(T, lane, a0);
+    dec.template frag<S0 + 1>(T, lane, a1);
+    dec.template frag<S0 + 2>(T, lane, a2);
+    dec.template frag<S0 + 3>(T, lane, a3);
+    uint8_t* p0 = As + 2 * (lane & 3) * A_LBO + 2 * warp * 128 + (lane >> 2) * 16;
+    st16(p0, a0[0], a0[2], a1[0], a1[2]);
+    st16(p0 + 128, a0[1], a0[3], a1[1], a1[3]);
+    st16(p0 + A_LBO, a2[0], a2[2], a3[0], a3[2]);
+    st16(p0 + A_LBO + 128, a2[1], a2[3], a3[1], a3[3]);
+}
+
+template <class D>
+__device__ __forceinline__ void dq_stage_j(int j, const D& dec, const uint8_t* T, int lane, uint8_t* As, int warp) {
+    if constexpr (D::KS >= 16) {
+        switch (j) {
+            case 0: dq_stage<D, 0>(dec, T, lane, As, warp); break;
+            case 1: dq_stage<D, 4>(dec, T, lane, As, warp); break;
+            case 2: dq_stage<D, 8>(dec, T, lane, As, warp); break;
+            default: dq_stage<D, 12>(dec, T, lane, As, warp); break;
+        }
+    } else if constexpr (D::KS >= 8) {
+        if (j == 0) dq_stage<D, 0>(dec, T, lane, As, warp);
+        else dq_stage<D, 4>(dec, T, lane, As, warp);
+    } else {
+        dq_stage<D, 0>(dec, T, lane, As, warp);
+    }
+}
+
+// rows past the matrix: zeros
+__device__ __forceinline__ void dq_zero(int lane, uint8_t* As, int warp) {
+    uint8_t* p0 = As + 2 * (lane & 3) * A_LBO + 2 * warp * 128 + (lane >> 2) * 16;
+    st16(p0, 0u, 0u, 0u, 0u);
+    st16(p0 + 128, 0u, 0u, 0u, 0u);
+    st16(p0 + A_LBO, 0u, 0u, 0u, 0u);
+    st16(p0 + A_LBO + 128, 0u, 0u, 0u, 0u);
+}
+
+// Tile t of a launch: the full token tiles of every expert (or projection segment) first,
+// then each one's remainder tile, so that a static round-robin over the blocks spreads the
+// heavy tiles evenly. Row blocks vary fastest. e < 0: past the end. The per-expert
+// entries (id, first route, routes, row blocks) sit in a shared-memory table filled once
+// per launch, so a lookup is a scan of shared memory, not a chain of dependent loads.
+struct GTile { int e, rb, tok0, nv; };
+struct ExTab { int e[MAX_EXPERTS], tb0[MAX_EXPERTS], ne[MAX_EXPERTS], nrb[MAX_EXPERTS]; };
+
+template <int MODE>
+__device__ __forceinline__ void gm_expert(const GemvParams& p, int a, int n_rb, int* e, int* tok_base, int* ne,
+                                          int* nrb) {
+    if constexpr (MODE == GM_PROJ) {
+        *e = a; *tok_base = p.tok0; *ne = p.T; *nrb = (p.seg[a].rows + GT_M - 1) / GT_M;
+    } else {
+        *e = p.active[a]; *tok_base = p.seg_mid[*e]; *ne = p.seg_off[*e + 1] - *tok_base; *nrb = n_rb;
+    }
+}
+
+__device__ GTile gm_tile(const ExTab& x, int n_ex, int t, int nt, int n_full) {
+    const bool full = t < n_full;
+    if (!full) t -= n_full;
+    int base = 0;
+    for (int a = 0; a < n_ex; ++a) {
+        const int ne = x.ne[a], nrb = x.nrb[a];
+        const int cnt = full ? (ne / nt) * nrb : ((ne % nt) ? nrb : 0);
+        if (t < base + cnt) {
+            const int i = t - base;
+            if (full) return GTile{x.e[a], i % nrb, x.tb0[a] + (i / nrb) * nt, nt};
+            return GTile{x.e[a], i, x.tb0[a] + (ne / nt) * nt, ne % nt};
+        }
+        base += cnt;
+    }
+    return GTile{-1, 0, 0, 0};
+}
+
 template <int WT, int KSF, int MODE>
-__global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParams p) {
     using D = typename DecSel<WT, KSF>::T;
     constexpr int KC = D::KC, KS = D::KS;
-    constexpr int CPG = GT_K / KC;                   // tile chunks per K group
+    static_assert(KS % 4 == 0, "a stage is four k-steps");
+    constexpr int CPS = KS / 4;                      // stages per chunk
     constexpr int NMAT = (MODE == GM_GATEUP) ? 2 : 1;
-    constexpr uint32_t NCOLS = NMAT == 2 ? 128u : 64u;
-    extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t* A = smem;                               // [A_BYTES]
-    uint8_t* Bb = smem + A_BYTES;                    // [2][B_BYTES]
-    uint8_t* raw = Bb + 2 * B_BYTES;                 // [GM_WARPS][RAW_NS][CPG * tile_bytes]
-    __shared__ __align__(8) uint64_t mma_bar;
-    __shared__ __align__(8) uint64_t raw_bar[GM_WARPS][RAW_NS];
+    constexpr uint32_t NCOLS = NMAT * NT_MAX;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the B atoms need 1024-byte alignment (the swizzle pattern follows address bits 7..9)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* Bring = smem;                           // [NB][B_SLOT]
+    uint8_t* Aring = smem + NB * B_SLOT;             // [NA][A_SLOT]
+    uint8_t* raw = Aring + NA * A_SLOT;              // [DQW][RR][tile_bytes]
+    __shared__ __align__(8) uint64_t a_full[NA], a_empty[NA], b_full[NB], b_empty[NB];
+    __shared__ __align__(8) uint64_t acc_full, acc_empty, fin_bar;
+    __shared__ __align__(8) uint64_t raw_bar[DQW][MAX_RR];
     __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag;
+    __shared__ ExTab xt;
+    __shared__ int brow[BQW][NT_MAX];                // B producers: activation row of each token of their tile
+    volatile int* ab = &abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t stage_bytes = (uint32_t)(CPG * p.tile_bytes);
-    const int ns = p.n_stages;                       // raw ring depth per warp (1..RAW_NS)
-    uint8_t* myraw = raw + (size_t)warp * ns * stage_bytes;
+    const int RR = p.n_stages, NT = p.gm_nt;
 
-    if (warp == 0) {
+    if (warp == DQW) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(&tmem_base)), "r"(NCOLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (tid == 0) mbar_init(&mma_bar, 1);
-    if (lane == 0)
-        for (int i = 0; i < RAW_NS; ++i) mbar_init(&raw_bar[warp][i], 1);
+    if (tid == 0) {
+        for (int i = 0; i < NA; ++i) { mbar_init(&a_full[i], DQW); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < NB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }   // one producer per stage
+        mbar_init(&acc_full, 1);
+        mbar_init(&acc_empty, DQW);
+        mbar_init(&fin_bar, 1);
+        abort_flag = 0;
+    }
+    if (warp < DQW && lane == 0)
+        for (int i = 0; i < RR; ++i) mbar_init(&raw_bar[warp][i], 1);
     fence_mbar_init();
     tc_fence_before();
     __syncthreads();
@@ -143,240 +271,299 @@ __global__ void __launch_bounds__(256, 1) moe_gemm_kernel(const GemvParams p) {
 
     // experts with GEMM routes: active[n_small .. n_active), routes [seg_mid[e], seg_off[e + 1]);
     // projections (GM_PROJ): the segments' rows over tokens [tok0, tok0 + T)
-    const int n_groups = (p.chunks + CPG - 1) / CPG;
-    const int n_st = n_groups * NMAT;
-    int e_lo = 0, e_hi = 0, n_rb = 0, n_tiles = 0;
+    int e_lo = 0, e_hi = 0, n_rb = 0;
     if constexpr (MODE == GM_PROJ) {
         e_hi = p.n_seg;
-        for (int a = 0; a < e_hi; ++a)
-            n_tiles += (p.T + GT_N - 1) / GT_N * ((p.seg[a].rows + GT_M - 1) / GT_M);
     } else {
         e_lo = *p.n_small;
         e_hi = *p.n_active;
-        n_rb = (p.out_rows + GT_M - 1) / GT_M;   // 128-row blocks per expert
-        for (int a = e_lo; a < e_hi; ++a) {
-            const int e = p.active[a];
-            n_tiles += (p.seg_off[e + 1] - p.seg_mid[e] + GT_N - 1) / GT_N * n_rb;
-        }
+        n_rb = (p.out_rows + GT_M - 1) / GT_M;
     }
-    uint32_t mma_phase = 0;
-    int mma_pending = 0;                             // commits not yet waited for
-    uint32_t raw_phase[RAW_NS];
-#pragma unroll
-    for (int i = 0; i < RAW_NS; ++i) raw_phase[i] = 0;
-    bool failed = false;
-    auto wait_mma = [&]() {
-        if (mma_pending) {
-            failed = __syncthreads_or(mbar_wait(&mma_bar, mma_phase, p.err) ? 0 : 1) != 0 || failed;
-            mma_phase ^= 1u;
-            mma_pending = 0;
-        }
-    };
+    const int n_ex = min(e_hi - e_lo, MAX_EXPERTS);
+    for (int i = tid; i < n_ex; i += blockDim.x) {
+        int e, tb0, ne, nrb;
+        gm_expert<MODE>(p, e_lo + i, n_rb, &e, &tb0, &ne, &nrb);
+        xt.e[i] = e; xt.tb0[i] = tb0; xt.ne[i] = ne; xt.nrb[i] = nrb;
+    }
+    __syncthreads();
+    int n_full = 0, n_tiles = 0;
+    for (int a = 0; a < n_ex; ++a) {
+        n_full += (xt.ne[a] / NT) * xt.nrb[a];
+        n_tiles += (xt.ne[a] + NT - 1) / NT * xt.nrb[a];
+    }
+    const int n_groups = p.chunks * CPS;             // stages per matrix per tile
 
-    for (int t = blockIdx.x; t < n_tiles && !failed; t += gridDim.x) {
-        int a = e_lo, base = 0, e = 0, ne = 0, nrb = n_rb;
-        for (; a < e_hi; ++a) {
-            if constexpr (MODE == GM_PROJ) {
-                e = a;
-                ne = p.T;
-                nrb = (p.seg[a].rows + GT_M - 1) / GT_M;
-            } else {
-                e = p.active[a];
-                ne = p.seg_off[e + 1] - p.seg_mid[e];
-            }
-            const int nt = (ne + GT_N - 1) / GT_N * nrb;
-            if (t < base + nt) break;
-            base += nt;
-        }
-        const int tb = (t - base) / nrb, rb = (t - base) % nrb;
-        int tok0;
-        if constexpr (MODE == GM_PROJ) tok0 = p.tok0 + tb * GT_N;
-        else tok0 = p.seg_mid[e] + tb * GT_N;
-        const int nv = min(GT_N, ne - tb * GT_N);
-        const int rt = rb * GT_WARPS_ROWS + warp;        // this warp's row tile
-        int n_row_tiles = p.n_row_tiles;
-        const uint8_t* wsrc0 = p.w0 + (size_t)e * p.expert_stride;
-        const uint8_t* wsrc1 = p.w1 + (size_t)e * p.expert_stride;
-        if constexpr (MODE == GM_PROJ) {
-            n_row_tiles = p.seg[e].n_row_tiles;
-            wsrc0 = p.seg[e].tiles;
-        }
-        const bool rt_ok = rt < n_row_tiles;
-
-        // raw stage s -> this warp's ring slot s % RAW_NS
-        auto issue_raw = [&](int s) {
-            if (lane == 0 && rt_ok) {
-                const int g = s / NMAT, m = s % NMAT, c0 = g * CPG, nc = min(CPG, p.chunks - c0);
-                uint64_t* bar = &raw_bar[warp][s % ns];
-                const uint8_t* src = (m == 0 ? wsrc0 : wsrc1) + ((size_t)rt * p.chunks + c0) * p.tile_bytes;
-                mbar_expect_tx(bar, (uint32_t)(nc * p.tile_bytes));
-                bulk_g2s(myraw + (size_t)(s % ns) * stage_bytes, src, (uint32_t)(nc * p.tile_bytes), bar);
-            }
-        };
-        // B group g -> buffer g & 1 (token rows, 16 bytes per (token, 8-wide k chunk))
-        // this thread's token column of B (fixed for the tile) and its first 8-wide k chunk
-        constexpr int B_TPK = 32 * GM_WARPS / GT_N;     // threads per token (k chunks step by this)
-        const int bn = tid % GT_N, bkc0 = tid / GT_N;
-        const bool bn_ok = bn < nv;
-        int brow = tok0 + (bn_ok ? bn : 0);
-        if constexpr (MODE == GM_GATEUP) brow = p.route_tok[brow];
-        const __half* bsrc = p.X + (size_t)brow * p.ldx;
-        auto issue_b = [&](int g) {
-            uint8_t* bdst = Bb + (g & 1) * B_BYTES + (bn >> 3) * 128 + (bn & 7) * 16;
-            const int kg = g * CPG * KC, klim = min(GT_K, p.K - kg);
-#pragma unroll
-            for (int j = 0; j < GT_K / 8 / B_TPK; ++j) {
-                const int kc = bkc0 + j * B_TPK;
-                const bool ok = bn_ok && kc * 8 < klim;
-                cp_async16(bdst + kc * B_LBO, bsrc + kg + (ok ? kc * 8 : 0), ok);
-            }
-            cp_async_commit();
-        };
-
-        for (int s = 0; s < ns && s < n_st; ++s) issue_raw(s);
-        issue_b(0);
-        for (int s = 0; s < n_st && !failed; ++s) {
-            const int g = s / NMAT, m = s % NMAT, c0 = g * CPG, nc = min(CPG, p.chunks - c0);
-            // raw weights of this stage have landed (warp-local); the A buffer (and at a new
-            // group, the other B buffer) is free once the previous stage's MMAs completed.
-            // One block-wide vote per stage keeps every thread on the same path.
-            const int slot = s % ns;
-            bool f = false;
-            if (rt_ok) {
-                f = !mbar_wait(&raw_bar[warp][slot], raw_phase[slot], p.err);
-                raw_phase[slot] ^= 1u;
-            }
-            if (mma_pending) {
-                f = !mbar_wait(&mma_bar, mma_phase, p.err) || f;
-                mma_phase ^= 1u;
-                mma_pending = 0;
-            }
-            failed = __syncthreads_or(f ? 1 : 0) != 0;
-            if (failed) break;
-            if (m == 0 && g + 1 < n_groups) issue_b(g + 1);
-            // dequantise this warp's row tile into A
-            const uint8_t* T0 = myraw + (size_t)slot * stage_bytes;
-#pragma unroll
-            for (int cc = 0; cc < CPG; ++cc) {
-                uint8_t *b0, *b1;
-                dq_bases<KC>(A, lane, 16 * warp, cc * KC, &b0, &b1);
-                if (rt_ok && cc < nc) {
-                    const uint8_t* T = T0 + cc * p.tile_bytes;
-                    D dec;
-                    dec.prep(T, lane);
-                    DqLoop<D, 0, KS>::run(dec, T, lane, b0, b1);
-                } else {
-                    // rows past the matrix or k past K: zeros
-#pragma unroll
-                    for (int s2 = 0; s2 < KS; ++s2) {
-                        *reinterpret_cast<uint2*>(b0 + (s2 >> 1) * A_LBO + (s2 & 1) * 8) = make_uint2(0u, 0u);
-                        *reinterpret_cast<uint2*>(b1 + (s2 >> 1) * A_LBO + (s2 & 1) * 8) = make_uint2(0u, 0u);
-                    }
-                }
-            }
-            __syncwarp();
-            if (s + ns < n_st) { fence_proxy_async(); issue_raw(s + ns); }
-            // activation rows of group g complete (the newest group may still be in flight)
-            if (m == 0) { if (g + 1 < n_groups) cp_async_wait_1(); else cp_async_wait_0(); }
-            fence_proxy_async();                     // generic-proxy writes -> tensor core reads
-            tc_fence_before();
-            __syncthreads();
-            if (tid == 0) {
+    bool ok = true;
+    if (warp == DQW) {
+        // ---- MMA warp: one lane issues ----
+        if (lane == 0) {
+            int aslot = 0, bslot = 0;
+            uint32_t aph = 0, bph = 0, accph = 0;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
+                const uint32_t idesc = idesc_n((ti.nv + 15) & ~15);
+                ok = wait_ab(&acc_empty, accph ^ 1u, p.err, ab);   // previous tile's accumulators read
+                accph ^= 1u;
+                if (!ok) break;
                 tc_fence_after();
-                const uint8_t* Bs = Bb + (g & 1) * B_BYTES;
-                const int kblocks = nc * KC / 16;
-                for (int kb = 0; kb < kblocks; ++kb) {
-                    const uint64_t da = umma_desc(smem_u32(A) + 2 * kb * A_LBO, A_LBO);
-                    const uint64_t db = umma_desc(smem_u32(Bs) + 2 * kb * B_LBO, B_LBO);
-                    umma_f16(tm + m * GT_N, da, db, (g > 0 || kb > 0) ? 1u : 0u);
+                for (int g = 0; g < n_groups && ok; ++g) {
+                    ok = wait_ab(&b_full[bslot], bph, p.err, ab);
+                    if (!ok) break;
+#pragma unroll
+                    for (int m = 0; m < NMAT; ++m) {
+                        if (!ok) break;
+                        ok = wait_ab(&a_full[aslot], aph, p.err, ab);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(Aring + aslot * A_SLOT), sb = smem_u32(Bring + bslot * B_SLOT);
+#pragma unroll
+                        for (int kb = 0; kb < KG / 16; ++kb)
+                            umma_f16(tm + m * NT_MAX, umma_desc(sa + 2 * kb * A_LBO, A_LBO),
+                                     umma_desc_sw128(sb + 32 * kb), idesc, (g > 0 || kb > 0) ? 1u : 0u);
+                        umma_commit(&a_empty[aslot]);            // A slot free once these MMAs complete
+                        if (++aslot == NA) { aslot = 0; aph ^= 1u; }
+                    }
+                    if (!ok) break;
+                    umma_commit(&b_empty[bslot]);
+                    if (++bslot == NB) { bslot = 0; bph ^= 1u; }
                 }
-                umma_commit(&mma_bar);
+                if (!ok) break;
+                umma_commit(&acc_full);
             }
-            mma_pending = 1;
+            if (!ok) *ab = 1;
+            // every MMA issued completes before the block releases its memory
+            umma_commit(&fin_bar);
+            (void)mbar_wait(&fin_bar, 0, nullptr, 1u << 16);
         }
-        wait_mma();
-        cp_async_wait_0();
-        tc_fence_after();
-        if (!failed) {
-            // epilogue: warp w reads TMEM lanes 32 (w % 4).., token columns 32 (w / 4) ..
-            const int row = rb * GT_M + 32 * (warp & 3) + lane;
-            const int row_lim = MODE == GM_PROJ ? p.seg[e].rows : p.out_rows;
-            const uint32_t lane_addr = tm + ((uint32_t)(32 * (warp & 3)) << 16);
+        __syncwarp();
+    } else if (warp < DQW) {
+        // ---- decode warps ----
+        const uint8_t* myraw = raw + (size_t)warp * RR * p.tile_bytes;
+        // raw chunk stream (this warp's row tile of each of the block's tiles, chunk-major,
+        // gate then up): issue cursor (tile, chunk index) and counts
+        int is_t = blockIdx.x, is_q = 0, n_issued = 0, n_waited = 0;
+        GTile is_ti = is_t < n_tiles ? gm_tile(xt, n_ex, is_t, NT, n_full) : GTile{-1, 0, 0, 0};
+        auto issue_chunk = [&]() {
+            if (is_t >= n_tiles) return;
+            const int slot = n_issued % RR, c = is_q / NMAT, m = is_q % NMAT;
+            const int rt = is_ti.rb * DQW + warp;
+            if (lane == 0) {
+                uint64_t* bar = &raw_bar[warp][slot];
+                const uint8_t* src;
+                int nrt;
+                if constexpr (MODE == GM_PROJ) {
+                    src = p.seg[is_ti.e].tiles;
+                    nrt = p.seg[is_ti.e].n_row_tiles;
+                } else {
+                    src = (m == 0 ? p.w0 : p.w1) + (size_t)is_ti.e * p.expert_stride;
+                    nrt = p.n_row_tiles;
+                }
+                if (rt < nrt) {
+                    mbar_expect_tx(bar, (uint32_t)p.tile_bytes);
+                    bulk_g2s(const_cast<uint8_t*>(myraw) + (size_t)slot * p.tile_bytes,
+                             src + ((size_t)rt * p.chunks + c) * p.tile_bytes, (uint32_t)p.tile_bytes, bar);
+                } else {
+                    mbar_expect_tx(bar, 0u);                 // no rows here: the phase completes empty
+                }
+            }
+            ++n_issued;
+            if (++is_q == p.chunks * NMAT) {
+                is_q = 0;
+                is_t += gridDim.x;
+                if (is_t < n_tiles) is_ti = gm_tile(xt, n_ex, is_t, NT, n_full);
+            }
+        };
+        for (int i = 0; i < RR; ++i) issue_chunk();
+        int aslot = 0;
+        uint32_t aph = 0, accph = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
+            const int rt = ti.rb * DQW + warp;
+            const bool rt_ok = rt < (MODE == GM_PROJ ? p.seg[ti.e].n_row_tiles : p.n_row_tiles);
+            D dec[NMAT];
+            int rslot[NMAT];
+            for (int g = 0; g < n_groups && ok; ++g) {
+                const int j = g % CPS;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    if (!ok) break;
+                    if (j == 0) {
+                        // first stage of chunk (c, m): wait for its bytes, read its scales
+                        rslot[m] = n_waited % RR;
+                        bool w = wait_ab(&raw_bar[warp][rslot[m]], (uint32_t)((n_waited / RR) & 1), p.err, ab);
+                        ok = __all_sync(0xffffffffu, w);
+                        if (!ok) break;
+                        ++n_waited;
+                        if (rt_ok) dec[m].prep(myraw + (size_t)rslot[m] * p.tile_bytes, lane);
+                    }
+                    bool w = wait_ab(&a_empty[aslot], aph ^ 1u, p.err, ab);
+                    ok = __all_sync(0xffffffffu, w);
+                    if (!ok) break;
+                    uint8_t* As = Aring + aslot * A_SLOT;
+                    if (rt_ok) dq_stage_j<D>(j, dec[m], myraw + (size_t)rslot[m] * p.tile_bytes, lane, As, warp);
+                    else dq_zero(lane, As, warp);
+                    fence_proxy_async();                     // generic-proxy writes -> tensor core reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[aslot]);
+                    if (++aslot == NA) { aslot = 0; aph ^= 1u; }
+                    if (j == CPS - 1) issue_chunk();         // chunk (c, m) decoded: its slot refills
+                }
+            }
+            if (!ok) break;
+            // epilogue: warp w reads TMEM lanes 32 (w % 4).. (its rows), token columns in
+            // 16-wide chunks alternating between the two warps of a lane quarter
+            {
+                bool w = wait_ab(&acc_full, accph, p.err, ab);
+                accph ^= 1u;
+                ok = __all_sync(0xffffffffu, w);
+                if (!ok) break;
+            }
+            tc_fence_after();
+            const int qd = warp & 3;
+            const int row = ti.rb * GT_M + 32 * qd + lane;
+            const int row_lim = MODE == GM_PROJ ? p.seg[ti.e].rows : p.out_rows;
+            const uint32_t lane_addr = tm + ((uint32_t)(32 * qd) << 16);
+            const int ncc = (ti.nv + 15) >> 4;
 #pragma unroll 1
-            for (int c = 32 * (warp >> 2); c < 32 * (warp >> 2) + 32; c += 16) {
+            for (int cc = warp >> 2; cc < ncc; cc += 2) {
                 float v0[16], v1[16];
-                tmem_ld16(lane_addr + c, v0);
-                if constexpr (NMAT == 2) tmem_ld16(lane_addr + GT_N + c, v1);
+                tmem_ld16(lane_addr + cc * 16, v0);
+                if constexpr (NMAT == 2) tmem_ld16(lane_addr + NT_MAX + cc * 16, v1);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int n = c + i;
-                    if (n >= nv || row >= row_lim) continue;
+                    const int n = cc * 16 + i;
+                    if (n >= ti.nv || row >= row_lim) continue;
                     if constexpr (MODE == GM_GATEUP) {
                         const float gt = v0[i], up = v1[i];
                         const float si = gt / (1.0f + expf(-gt));
-                        p.yout[(size_t)(tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
+                        p.yout[(size_t)(ti.tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
                     } else if constexpr (MODE == GM_PROJ) {
-                        float* o = p.out + (size_t)(tok0 + n) * p.ldo + p.seg[e].out_off + row;
+                        float* o = p.out + (size_t)(ti.tok0 + n) * p.ldo + p.seg[ti.e].out_off + row;
                         if (p.epi == EPI_ADD) *o = v0[i] + *o;
                         else if (p.epi == EPI_SOFTCAP) *o = tanhf(v0[i] * (1.0f / p.cap)) * p.cap;
                         else *o = v0[i];
                     } else {
-                        p.out[(size_t)(tok0 + n) * p.ldo + row] = v0[i] * p.route_w[tok0 + n];
+                        p.out[(size_t)(ti.tok0 + n) * p.ldo + row] = v0[i] * p.route_w[ti.tok0 + n];
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty);
         }
-        tc_fence_before();
-        __syncthreads();                                 // accumulators read before the next tile
-        tc_fence_after();
-    }
-    // after a failure: copies and MMAs still in flight finish (bounded) before release
-    if (failed) {
-        if (lane == 0)
-            for (int i = 0; i < ns; ++i) (void)mbar_wait(&raw_bar[warp][i], raw_phase[i], nullptr, 1u << 12);
-        (void)mbar_wait(&mma_bar, mma_phase, nullptr, 1u << 12);
+        if (!ok) *ab = 1;
         cp_async_wait_0();
+        // after a failure: chunk copies still in flight land (bounded) before release
+        if (!ok && lane == 0)
+            for (int J = n_waited; J < n_issued; ++J)
+                (void)mbar_wait(&raw_bar[warp][J % RR], (uint32_t)((J / RR) & 1), nullptr, 1u << 16);
+        __syncwarp();
+    } else {
+        // ---- activation (B) producers: warp wb copies the stages G with G % 2 == wb (G counts
+        // the block's stages over its tiles). Stage g of a tile holds, for every token n, the
+        // same 64 k values the decoders put in A (k = chunk*KC + q*KC/4 + 16j + [0, 16) for
+        // q = 0..3), one 128-byte line of the stage-ordered copy of X, stored as token n's
+        // row with the 128-byte swizzle. Lane (token n % 4, piece c): a quarter-warp copies
+        // one line. A stage is published once the warp's next stage is in flight (its copies,
+        // a proxy fence, the arrive). Rows past the tile's tokens (up to the next 16) copy
+        // zeros. ----
+        const int wb = warp - DQW - 1, pc = lane & 7, tq = lane >> 3;
+        int* myrow = brow[wb];
+        int G = 0, pend = -1;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
+            const int n16 = (ti.nv + 15) & ~15;
+            for (int i = lane; i < n16; i += 32) {
+                int row = ti.tok0 + (i < ti.nv ? i : 0);
+                if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
+                myrow[i] = row;
+            }
+            __syncwarp();
+            for (int g = 0; g < n_groups && ok; ++g, ++G) {
+                if ((G & 1) != wb) continue;
+                const int slot = G % NB;
+                bool w = wait_ab(&b_empty[slot], (uint32_t)(((G / NB) & 1) ^ 1), p.err, ab);
+                ok = __all_sync(0xffffffffu, w);
+                if (!ok) break;
+                const int k0 = (g / CPS) * KC + 64 * (g % CPS) + 8 * pc;
+                uint8_t* dst = Bring + slot * B_SLOT;
+                for (int n = tq; n < n16; n += 4)
+                    cp_async16(dst + n * 128 + ((pc ^ (n & 7)) << 4), p.xperm + (size_t)myrow[n] * p.K + k0, n < ti.nv);
+                cp_async_commit();
+                if (pend >= 0) {
+                    cp_async_wait_1();                   // this warp's previous stage landed
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&b_full[pend % NB]);
+                }
+                pend = G;
+            }
+        }
+        cp_async_wait_0();
+        if (pend >= 0 && ok) {
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&b_full[pend % NB]);
+        }
+        if (!ok) *ab = 1;
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0)
+    if (warp == DQW) {
+        tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tm), "r"(NCOLS) : "memory");
+    }
+}
+
+// Raw ring depth (chunks per decode warp) that fits next to the A and B rings (static
+// shared memory: barriers and the expert table; 1 KB of slack for the B alignment).
+int gemm_raw_slots(int tile_bytes) {
+    const int budget = 232448 - 7168 - 1024 - NA * A_SLOT - NB * B_SLOT;
+    return std::min(MAX_RR, budget / (DQW * tile_bytes));
 }
 
 template <int WT, int KSF>
-void gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
+bool gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
     void (*k)(const GemvParams) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
                                   : p.mode == GM_PROJ ? moe_gemm_kernel<WT, KSF, GM_PROJ>
                                                       : moe_gemm_kernel<WT, KSF, GM_DOWN>;
-    constexpr int CPG = GT_K / DecSel<WT, KSF>::T::KC;
-    // deepest raw ring (up to RAW_NS stages) that fits next to A and the two B buffers
-    const int per_stage = GM_WARPS * CPG * p.tile_bytes;
-    const int budget = 227 * 1024 - 1024 - A_BYTES - 2 * B_BYTES;
     GemvParams q = p;
-    q.n_stages = std::max(1, std::min(RAW_NS, budget / per_stage));
-    const int smem = A_BYTES + 2 * B_BYTES + q.n_stages * per_stage;
+    q.n_stages = gemm_raw_slots(p.tile_bytes);
+    if (q.n_stages < (p.mode == GM_GATEUP ? 2 : 1)) return false;   // moe_gemm_supported excludes this
+    if (q.gm_nt <= 0 || q.gm_nt > NT_MAX || q.gm_nt % 16) q.gm_nt = NT_MAX;
+    constexpr int KC = DecSel<WT, KSF>::T::KC;
+    if (!q.xperm || q.K % KC || q.x_row0 < 0 || q.x_row0 >= q.x_rows || ((uintptr_t)q.xperm & 15u)) return false;
+    {
+        const long pieces = (long)(q.x_rows - q.x_row0) * (q.K / 8);
+        const int blocks = (int)std::min<long>((pieces + 255) / 256, 4L * grid);
+        launch_pdl(gemm_x_stage_order_kernel<KC>, dim3(blocks), dim3(256), 0, s, q.X, q.ldx, q.x_row0, q.x_rows, q.K,
+                   q.xperm);
+    }
+    const int smem = 1024 + NB * B_SLOT + NA * A_SLOT + q.n_stages * DQW * p.tile_bytes;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    launch_pdl(k, dim3(grid), dim3(32 * GM_WARPS), (size_t)smem, s, q);
+    launch_pdl(k, dim3(grid), dim3(GM_THREADS), (size_t)smem, s, q);
+    return true;
 }
 
 }  // namespace
 
 bool moe_gemm_supported(const DevMat& m) {
     switch (m.type) {
-        case GT_Q4_K: case GT_Q6_K: return true;              // 256-wide chunks
-        case GT_Q8_0: return true;                            // 128-wide chunks, two per group
-        case GT_F16: return m.steps == 4;                     // 64-wide chunks, four per group
+        case GT_Q4_K: case GT_Q6_K: return true;              // 256-wide chunks, four stages each
+        case GT_Q8_0: return true;                            // 128-wide chunks, two stages each
+        case GT_F16: return m.steps == 4;                     // 64-wide chunks, one stage each
         default: return false;
     }
 }
 
-void launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s) {
+bool launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s) {
     switch (p.type) {
-        case GT_Q4_K: gemm_typed<GT_Q4_K, 16>(p, grid, s); break;
-        case GT_Q6_K: gemm_typed<GT_Q6_K, 16>(p, grid, s); break;
-        case GT_Q8_0: gemm_typed<GT_Q8_0, 8>(p, grid, s); break;
-        case GT_F16: gemm_typed<GT_F16, 4>(p, grid, s); break;
-        default: break;
+        case GT_Q4_K: return gemm_typed<GT_Q4_K, 16>(p, grid, s);
+        case GT_Q6_K: return gemm_typed<GT_Q6_K, 16>(p, grid, s);
+        case GT_Q8_0: return gemm_typed<GT_Q8_0, 8>(p, grid, s);
+        case GT_F16: return gemm_typed<GT_F16, 4>(p, grid, s);
+        default: return false;
     }
 }
 

@@ -94,8 +94,13 @@ __device__ __forceinline__ void item_next(const GemvParams& p, ItemPos& q) {
     if (++q.rt == nrt) { q.rt = 0; ++q.s; }
 }
 
+// The active expert of the last item resolved (expert id, first route, route count): a
+// CTA's items change expert once per n_row_tiles items, so the dependent loads of
+// active[] and the segment offsets are issued once per expert, not once per item.
+struct ExpCache { int s = -1, expert = 0, tok0 = 0, n_tok = 0; };
+
 template <int MODE>
-__device__ __forceinline__ ItemRef item_ref(const GemvParams& p, ItemPos q, int c0) {
+__device__ __forceinline__ ItemRef item_ref(const GemvParams& p, ItemPos q, int c0, ExpCache& ec) {
     ItemRef r{};
     r.rt = q.rt;
     if constexpr (MODE == GM_PROJ) {
@@ -104,13 +109,19 @@ __device__ __forceinline__ ItemRef item_ref(const GemvParams& p, ItemPos q, int 
         r.src[1] = nullptr;
         r.n_tok = p.T; r.tok0 = 0;
     } else {
-        r.expert = p.active[q.s];
+        if (q.s != ec.s) {
+            ec.s = q.s;
+            ec.expert = p.active[q.s];
+            ec.tok0 = p.seg_off[ec.expert];
+            ec.n_tok = (p.seg_mid ? p.seg_mid[ec.expert] : p.seg_off[ec.expert + 1]) - ec.tok0;
+        }
+        r.expert = ec.expert;
         r.seg = 0;
         const size_t off = (size_t)r.expert * p.expert_stride + ((size_t)q.rt * p.chunks + c0) * p.tile_bytes;
         r.src[0] = p.w0 + off;
         r.src[1] = (MODE == GM_GATEUP) ? p.w1 + off : nullptr;
-        r.tok0 = p.seg_off[r.expert];
-        r.n_tok = (p.seg_mid ? p.seg_mid[r.expert] : p.seg_off[r.expert + 1]) - r.tok0;
+        r.tok0 = ec.tok0;
+        r.n_tok = ec.n_tok;
     }
     return r;
 }
@@ -152,6 +163,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     __syncwarp();
 
     int it0 = 0, it1 = 0;
+    ExpCache ec_issue, ec_use;                   // expert resolved by the copy issuer / the consumer
     int issued_upto = -1;                        // last item whose copy was issued
     ItemPos ipos{0, 0};                          // position of the next item to issue
     auto issue = [&](int item, int slot) {
@@ -159,7 +171,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
         const ItemPos q = ipos;
         item_next<MODE>(p, ipos);
         if (lane == 0 && ncw > 0) {
-            const ItemRef it = item_ref<MODE>(p, q, c0);
+            const ItemRef it = item_ref<MODE>(p, q, c0, ec_issue);
             mbar_expect_tx(&mybar[slot], wbytes * NMAT);
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
@@ -192,7 +204,7 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
     int slot = 0;
     uint32_t parity = 0;
     for (int item = it0; item < it1; ++item) {
-        const ItemRef it = item_ref<MODE>(p, cpos, c0);
+        const ItemRef it = item_ref<MODE>(p, cpos, c0, ec_use);
         item_next<MODE>(p, cpos);
         // the item's weights are waited for after the first activation loads are issued
         const bool need_wait = !failed && ncw > 0 && item <= issued_upto;

@@ -67,6 +67,11 @@ struct GemvParams {
     // launch geometry (host-filled)
     int n_stages, stage_bytes, cps;  // ring depth per warp, bytes per stage, chunks per stage
     int x_rs;                       // GM_PROJ: bytes per token row of a warp's shared activation slice (0: none)
+    int gm_nt;                      // tensor-core GEMM: routed tokens per tile (multiple of 16, <= 256);
+                                    // 0 lets launch_moe_gemm choose
+    int x_rows;                     // tensor-core GEMM: rows [x_row0, x_rows) of X that it reads
+    int x_row0;
+    __half* xperm;                  // tensor-core GEMM: scratch [x_rows][K] for X in stage order
 };
 
 // Chooses warps/stages for a weight matrix and fills the launch geometry.
@@ -75,7 +80,8 @@ void gemv_geometry(const DevMat& m, int nmat, int ntg, int* nwarps, int* n_stage
 void launch_gemv(const GemvParams& p, int nwarps, int grid, int smem, cudaStream_t s);
 // tcgen05 grouped GEMM over the experts active[n_small, n_active) (k_gemm.cu)
 bool moe_gemm_supported(const DevMat& m);
-void launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s);
+// Returns false (nothing launched) when the activation buffer's TMA view cannot be built.
+bool launch_moe_gemm(const GemvParams& p, int grid, cudaStream_t s);
 
 // ---- decode-step kernels -----------------------------------------------------------
 struct Dims {
@@ -139,6 +145,7 @@ struct StepBufs {
     int* n_active; int* active; int* seg_off; int* route_tok; float* route_w; int* route_pos;
     int* tile_off;                  // [MAX_EXPERTS + 1] prefix of 8-token tiles over active experts
     int* n_small;                   // active[0, n_small): experts with GEMV routes; then GEMM experts
+    __half* gemm_x;                 // tensor-core GEMM: activations in stage order (k permuted per chunk)
     int* seg_mid;                   // [MAX_EXPERTS] first GEMM route of each expert
     int* ticket;
     __half* y;                      // [R][ff]

@@ -124,6 +124,8 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
     acc((size_t)D.n_layer * T * c->kmax * 4);
     acc((size_t)4 * T * std::max(D.rd, 1) * 4);
     acc((size_t)T * nkv * 4);
+    const size_t gx = std::max((size_t)T * std::max((size_t)d, (size_t)nh * hd), (size_t)R * D.n_ff);
+    acc(gx * 2);
     acc((MAX_EXPERTS + 1) * 4);
     acc(4);
     acc(MAX_EXPERTS * 4);
@@ -156,6 +158,7 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
     B.err = carve<uint32_t>(p, 1);
     B.sel_log = carve<int>(p, (size_t)D.n_layer * T * c->kmax); B.sel_log_T = T;
     B.attn_ticket = carve<int>(p, (size_t)T * nkv);
+    B.gemm_x = carve<__half>(p, gx);
     B.tile_off = carve<int>(p, MAX_EXPERTS + 1);
     B.n_small = carve<int>(p, 1);
     B.seg_mid = carve<int>(p, MAX_EXPERTS);
@@ -247,6 +250,13 @@ struct ProfScope {
     ~ProfScope() { if (c->profiling) cudaEventRecord(e1, c->stream); }
 };
 
+// The tensor-core GEMM could not be set up (its activation TMA view was rejected): the
+// step's results would be incomplete, so the call that enqueued it fails.
+void gemm_setup_failed(Ctx* c) {
+    set_error("tensor-core GEMM: activation tensor map could not be encoded");
+    c->enq_failed = true;
+}
+
 int ctas_per_sm(int smem) { return std::max(1, std::min(4, 233472 / (smem + 1024))); }
 
 // Projection of T rows (tokens or output rows). With t_dec >= 0 the rows are a step's
@@ -281,7 +291,10 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
     if (gemm_ok) {
         p.tok0 = t_dec;
         p.T = T - t_dec;
-        launch_moe_gemm(p, c->m->n_sm, c->stream);
+        p.x_rows = T;
+        p.x_row0 = t_dec;
+        p.xperm = c->B.gemm_x;
+        if (!launch_moe_gemm(p, c->m->n_sm, c->stream)) gemm_setup_failed(c);
         c->launches++;
     }
 }
@@ -332,7 +345,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk, const SegSet* seg
     c->launches++;
     if (split) {
         p.n_active = sg.n_active;
-        launch_moe_gemm(p, c->m->n_sm, c->stream);
+        p.x_rows = mode == GM_GATEUP ? c->cur_T : c->cur_T * c->kmax;
+        p.x_row0 = 0;
+        p.xperm = c->B.gemm_x;
+        if (!launch_moe_gemm(p, c->m->n_sm, c->stream)) gemm_setup_failed(c);
         c->launches++;
     }
 }
@@ -341,6 +357,7 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk, const SegSet* seg
 
 
 void enqueue_step(Ctx* c, int T, int n_out) {
+    c->cur_T = T;
     Model* m = c->m;
     const Dims& D = m->dims;
     StepBufs B = c->B;
@@ -418,13 +435,18 @@ int run_step(Ctx* c, int T, int n_out) {
     auto it = c->graphs.find(key);
     if (use_graph && T != c->cur_n_desc && it == c->graphs.end())
         use_graph = ++c->shape_seen[key] >= 2 && c->prompt_graphs < kMaxPromptGraphs;
-    if (!use_graph) { enqueue_step(c, T, n_out); return Z2B_OK; }
+    c->enq_failed = false;
+    if (!use_graph) {
+        enqueue_step(c, T, n_out);
+        return c->enq_failed ? Z2B_ERR_CUDA : Z2B_OK;
+    }
     if (it == c->graphs.end()) {
         if (T != c->cur_n_desc) c->prompt_graphs++;
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
         enqueue_step(c, T, n_out);
         CK(cudaStreamEndCapture(c->stream, &g));
+        if (c->enq_failed) { cudaGraphDestroy(g); return Z2B_ERR_CUDA; }
         cudaGraphExec_t ge;
         const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
         cudaGraphDestroy(g);
@@ -962,10 +984,13 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
     launch_segments(B, T, k, ly.n_expert, bulk ? 1 : 0, c->stream);
     const bool prof = c->profiling;
     c->profiling = false;
+    c->enq_failed = false;
+    c->cur_T = T;
     gemv_moe(c, ly, GM_GATEUP, bulk);
     gemv_moe(c, ly, GM_DOWN, bulk);
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaGetLastError());
+    if (c->enq_failed) { c->profiling = prof; return Z2B_ERR_CUDA; }
     if (reps > 0 && ms) {
         cudaEvent_t e0, e1;
         CK(cudaEventCreate(&e0));

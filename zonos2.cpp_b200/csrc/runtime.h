@@ -66,6 +66,8 @@ struct Ctx {
     std::map<uint64_t, int> graph_launches;
     std::map<uint64_t, int> shape_seen;      // occurrences of step shapes carrying prompt rows
     int prompt_graphs = 0;
+    bool enq_failed = false;
+    int cur_T = 0;                           // rows of the step (or expert op) being enqueued                 // a launch could not be set up while enqueuing (error set)
     int launches = 0, loop_launches = 0;
     // decode-loop uniforms
     double* d_canon_all = nullptr;
