@@ -34,6 +34,8 @@
 #include "tile_layout.h"
 #include "k_decode.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <algorithm>
 
 namespace z2b {
@@ -41,11 +43,12 @@ namespace z2b {
 namespace {
 
 constexpr int GT_M = 128;                        // weight rows per tile
-constexpr int NT_MAX = 256;                      // routed tokens per tile (MMA N <= 256)
+constexpr int NT_MAX = 256;                      // MMA N / B rows per stage (a tile's rows start
+                                                 // 8-aligned at or before its first route)
+constexpr int NT_TILE_MAX = 248;                 // routes per tile, so that the aligned rows fit
 constexpr int KG = 64;                           // K per stage
 constexpr int DQW = 8;                           // decode warps (16 weight rows each)
-constexpr int BQW = 2;                           // activation (B) producer warps (alternate stages)
-constexpr int GM_THREADS = 32 * (DQW + 1 + BQW); // + the MMA warp + the B producers
+constexpr int GM_THREADS = 32 * (DQW + 2);       // + the MMA warp + the activation (B) producer
 constexpr int NA = 2;                            // A ring slots (one stage of one matrix)
 constexpr int NB = 4;                            // B ring slots (one stage of activations)
 constexpr int MAX_RR = 6;                        // raw chunk ring slots per decode warp
@@ -54,8 +57,9 @@ constexpr int MAX_RR = 6;                        // raw chunk ring slots per dec
 // (two rows x four k-columns) hit 8 distinct bank groups.
 constexpr uint32_t A_LBO = GT_M / 8 * 128 + 16, CORE_SBO = 128;
 constexpr int A_SLOT = (int)A_LBO * (KG / 8);    // 16.1 KB
-// B (activations, 128-byte swizzle): token n's 64 k values are one 128-byte row at n * 128,
-// its 16-byte chunk c stored at chunk c ^ (n % 8); 8-token atoms of 1024 B.
+// B (activations, 128-byte swizzle): stage row n (route or token row0 + n) is one 128-byte
+// row at n * 128, its 16-byte chunk c at chunk c ^ (n % 8), as one TMA box writes it; 8-row
+// atoms of 1024 B.
 constexpr int B_SLOT = NT_MAX * KG * 2;          // 32 KB
 
 // instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, N, M 128
@@ -75,22 +79,36 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
            (2ull << 61);
 }
 
-// Activation rows [r0, r1) of X (row stride ldx) copied to Xp (row stride K) in stage
-// order: within each KC-wide chunk, stage j's 64 values k = q*KC/4 + 16j + [0, 16) for
-// q = 0..3 become the contiguous run [64j, 64j + 64), so a GEMM stage of one token is one
-// 128-byte line. 16-byte pieces, one per thread.
+// One tiled TMA load (no multicast) of a 2-D box completing on `bar`; x is a multiple of 64
+// elements (128 bytes).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+
+// Activation rows copied to Xp (row stride K) in stage order: within each KC-wide chunk,
+// stage j's 64 values k = q*KC/4 + 16j + [0, 16) for q = 0..3 become the contiguous run
+// [64j, 64j + 64), so a GEMM stage of a row is one 128-byte line and a tile's stage is one
+// TMA box over consecutive rows. Row r of Xp is X row rowmap[r] (the gate/up pass: one row
+// per route, in expert order) or X row r; rows [r0, r1), clipped to *n_rows when given.
+// 16-byte pieces, one per thread.
 template <int KC>
-__global__ void gemm_x_stage_order_kernel(const __half* __restrict__ X, int ldx, int r0, int r1, int K,
+__global__ void gemm_x_stage_order_kernel(const __half* __restrict__ X, int ldx, const int* __restrict__ rowmap,
+                                          const int* __restrict__ n_rows, int r0, int r1, int K,
                                           __half* __restrict__ Xp) {
     pdl_wait();
+    if (n_rows) r1 = min(r1, *n_rows);
     const int ppr = K / 8;                           // pieces per row
-    const long total = (long)(r1 - r0) * ppr;
+    const long total = (long)max(r1 - r0, 0) * ppr;
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int row = r0 + (int)(i / ppr), pc = (int)(i % ppr);
+        const int src_row = rowmap ? rowmap[row] : row;
         const int kd = pc * 8, c = kd / KC, rem = kd % KC;
         const int j = rem / 64, q = (rem % 64) / 16, h = (rem % 16) / 8;
         const int ks = c * KC + q * (KC / 4) + 16 * j + 8 * h;
-        *reinterpret_cast<uint4*>(Xp + (size_t)row * K + kd) = *reinterpret_cast<const uint4*>(X + (size_t)row * ldx + ks);
+        *reinterpret_cast<uint4*>(Xp + (size_t)row * K + kd) =
+            *reinterpret_cast<const uint4*>(X + (size_t)src_row * ldx + ks);
     }
     pdl_release();
 }
@@ -187,12 +205,18 @@ __device__ __forceinline__ void dq_zero(int lane, uint8_t* As, int warp) {
 }
 
 // Tile t of a launch: the full token tiles of every expert (or projection segment) first,
-// then each one's remainder tile, so that a static round-robin over the blocks spreads the
-// heavy tiles evenly. Row blocks vary fastest. e < 0: past the end. The per-expert
-// entries (id, first route, routes, row blocks) sit in a shared-memory table filled once
-// per launch, so a lookup is a scan of shared memory, not a chain of dependent loads.
+// then each one's remainder tile, largest remainder first (xord: experts by remainder,
+// descending). Row blocks vary fastest. Blocks take tiles in serpentine order (round r:
+// block b, or gridDim - 1 - b on odd rounds), so with tiles in decreasing size the load per
+// block stays within about one small tile of the mean. The per-expert entries (id, first
+// route, routes, row blocks) sit in a shared-memory table filled once per launch, so a
+// lookup is a scan of shared memory, not a chain of dependent loads. e < 0: past the end.
 struct GTile { int e, rb, tok0, nv; };
-struct ExTab { int e[MAX_EXPERTS], tb0[MAX_EXPERTS], ne[MAX_EXPERTS], nrb[MAX_EXPERTS]; };
+struct ExTab { int e[MAX_EXPERTS], tb0[MAX_EXPERTS], ne[MAX_EXPERTS], nrb[MAX_EXPERTS], ord[MAX_EXPERTS]; };
+
+__device__ __forceinline__ int snake_tile(int r) {
+    return r * (int)gridDim.x + ((r & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x);
+}
 
 template <int MODE>
 __device__ __forceinline__ void gm_expert(const GemvParams& p, int a, int n_rb, int* e, int* tok_base, int* ne,
@@ -208,13 +232,14 @@ __device__ GTile gm_tile(const ExTab& x, int n_ex, int t, int nt, int n_full) {
     const bool full = t < n_full;
     if (!full) t -= n_full;
     int base = 0;
-    for (int a = 0; a < n_ex; ++a) {
+    for (int i = 0; i < n_ex; ++i) {
+        const int a = full ? i : x.ord[i];
         const int ne = x.ne[a], nrb = x.nrb[a];
         const int cnt = full ? (ne / nt) * nrb : ((ne % nt) ? nrb : 0);
         if (t < base + cnt) {
-            const int i = t - base;
-            if (full) return GTile{x.e[a], i % nrb, x.tb0[a] + (i / nrb) * nt, nt};
-            return GTile{x.e[a], i, x.tb0[a] + (ne / nt) * nt, ne % nt};
+            const int j = t - base;
+            if (full) return GTile{x.e[a], j % nrb, x.tb0[a] + (j / nrb) * nt, nt};
+            return GTile{x.e[a], j, x.tb0[a] + (ne / nt) * nt, ne % nt};
         }
         base += cnt;
     }
@@ -222,7 +247,7 @@ __device__ GTile gm_tile(const ExTab& x, int n_ex, int t, int nt, int n_full) {
 }
 
 template <int WT, int KSF, int MODE>
-__global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParams p, const __grid_constant__ CUtensorMap tmx) {
     using D = typename DecSel<WT, KSF>::T;
     constexpr int KC = D::KC, KS = D::KS;
     static_assert(KS % 4 == 0, "a stage is four k-steps");
@@ -241,7 +266,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     __shared__ ExTab xt;
-    __shared__ int brow[BQW][NT_MAX];                // B producers: activation row of each token of their tile
     volatile int* ab = &abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int RR = p.n_stages, NT = p.gm_nt;
@@ -286,6 +310,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
         xt.e[i] = e; xt.tb0[i] = tb0; xt.ne[i] = ne; xt.nrb[i] = nrb;
     }
     __syncthreads();
+    for (int i = tid; i < n_ex; i += blockDim.x) {     // remainder tiles, largest first
+        const int ri = xt.ne[i] % NT;
+        int rank = 0;
+        for (int j = 0; j < n_ex; ++j) {
+            const int rj = xt.ne[j] % NT;
+            rank += (rj > ri || (rj == ri && j < i)) ? 1 : 0;
+        }
+        xt.ord[rank] = i;
+    }
+    __syncthreads();
     int n_full = 0, n_tiles = 0;
     for (int a = 0; a < n_ex; ++a) {
         n_full += (xt.ne[a] / NT) * xt.nrb[a];
@@ -299,9 +333,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
         if (lane == 0) {
             int aslot = 0, bslot = 0;
             uint32_t aph = 0, bph = 0, accph = 0;
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            for (int r = 0, t = snake_tile(0); t < n_tiles && ok; t = snake_tile(++r)) {
                 const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
-                const uint32_t idesc = idesc_n((ti.nv + 15) & ~15);
+                const uint32_t idesc = idesc_n((ti.tok0 % 8 + ti.nv + 15) & ~15);   // rows from tok0 & ~7
                 ok = wait_ab(&acc_empty, accph ^ 1u, p.err, ab);   // previous tile's accumulators read
                 accph ^= 1u;
                 if (!ok) break;
@@ -341,7 +375,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
         const uint8_t* myraw = raw + (size_t)warp * RR * p.tile_bytes;
         // raw chunk stream (this warp's row tile of each of the block's tiles, chunk-major,
         // gate then up): issue cursor (tile, chunk index) and counts
-        int is_t = blockIdx.x, is_q = 0, n_issued = 0, n_waited = 0;
+        int is_r = 0, is_t = snake_tile(0), is_q = 0, n_issued = 0, n_waited = 0;
         GTile is_ti = is_t < n_tiles ? gm_tile(xt, n_ex, is_t, NT, n_full) : GTile{-1, 0, 0, 0};
         auto issue_chunk = [&]() {
             if (is_t >= n_tiles) return;
@@ -369,14 +403,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
             ++n_issued;
             if (++is_q == p.chunks * NMAT) {
                 is_q = 0;
-                is_t += gridDim.x;
+                is_t = snake_tile(++is_r);
                 if (is_t < n_tiles) is_ti = gm_tile(xt, n_ex, is_t, NT, n_full);
             }
         };
         for (int i = 0; i < RR; ++i) issue_chunk();
         int aslot = 0;
         uint32_t aph = 0, accph = 0;
-        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        for (int r = 0, t = snake_tile(0); t < n_tiles && ok; t = snake_tile(++r)) {
             const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
             const int rt = ti.rb * DQW + warp;
             const bool rt_ok = rt < (MODE == GM_PROJ ? p.seg[ti.e].n_row_tiles : p.n_row_tiles);
@@ -423,7 +457,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
             const int row = ti.rb * GT_M + 32 * qd + lane;
             const int row_lim = MODE == GM_PROJ ? p.seg[ti.e].rows : p.out_rows;
             const uint32_t lane_addr = tm + ((uint32_t)(32 * qd) << 16);
-            const int ncc = (ti.nv + 15) >> 4;
+            const int n_off = ti.tok0 % 8;             // column n holds row (tok0 & ~7) + n
+            const int ncc = (n_off + ti.nv + 15) >> 4;
 #pragma unroll 1
             for (int cc = warp >> 2; cc < ncc; cc += 2) {
                 float v0[16], v1[16];
@@ -431,11 +466,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
                 if constexpr (NMAT == 2) tmem_ld16(lane_addr + NT_MAX + cc * 16, v1);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int n = cc * 16 + i;
-                    if (n >= ti.nv || row >= row_lim) continue;
+                    const int n = cc * 16 + i - n_off;
+                    if (n < 0 || n >= ti.nv || row >= row_lim) continue;
                     if constexpr (MODE == GM_GATEUP) {
+                        // SiLU with the fast exponential and division (about 1e-6 relative): a
+                        // tile's 32K outputs would otherwise cost as much as its last stages
                         const float gt = v0[i], up = v1[i];
-                        const float si = gt / (1.0f + expf(-gt));
+                        const float si = __fdividef(gt, 1.0f + __expf(-gt));
                         p.yout[(size_t)(ti.tok0 + n) * p.ldy + row] = __float2half_rn(up * si);
                     } else if constexpr (MODE == GM_PROJ) {
                         float* o = p.out + (size_t)(ti.tok0 + n) * p.ldo + p.seg[ti.e].out_off + row;
@@ -459,53 +496,34 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
                 (void)mbar_wait(&raw_bar[warp][J % RR], (uint32_t)((J / RR) & 1), nullptr, 1u << 16);
         __syncwarp();
     } else {
-        // ---- activation (B) producers: warp wb copies the stages G with G % 2 == wb (G counts
-        // the block's stages over its tiles). Stage g of a tile holds, for every token n, the
-        // same 64 k values the decoders put in A (k = chunk*KC + q*KC/4 + 16j + [0, 16) for
-        // q = 0..3), one 128-byte line of the stage-ordered copy of X, stored as token n's
-        // row with the 128-byte swizzle. Lane (token n % 4, piece c): a quarter-warp copies
-        // one line. A stage is published once the warp's next stage is in flight (its copies,
-        // a proxy fence, the arrive). Rows past the tile's tokens (up to the next 16) copy
-        // zeros. ----
-        const int wb = warp - DQW - 1, pc = lane & 7, tq = lane >> 3;
-        int* myrow = brow[wb];
-        int G = 0, pend = -1;
-        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        // ---- activation (B) producer warp: stage g of a tile is the 64-wide stage-ordered
+        // column block (chunk*KC + 64j) of the 256 consecutive rows from tok0 & ~7 of Xp (the
+        // tile's routes, then rows of the next routes or zero fill past the end, in columns
+        // the epilogue never reads): one TMA box with the 128-byte swizzle. ----
+        int slot = 0, issued = 0;
+        uint32_t ph = 0;
+        for (int r = 0, t = snake_tile(0); t < n_tiles && ok; t = snake_tile(++r)) {
             const GTile ti = gm_tile(xt, n_ex, t, NT, n_full);
-            const int n16 = (ti.nv + 15) & ~15;
-            for (int i = lane; i < n16; i += 32) {
-                int row = ti.tok0 + (i < ti.nv ? i : 0);
-                if constexpr (MODE == GM_GATEUP) row = p.route_tok[row];
-                myrow[i] = row;
-            }
-            __syncwarp();
-            for (int g = 0; g < n_groups && ok; ++g, ++G) {
-                if ((G & 1) != wb) continue;
-                const int slot = G % NB;
-                bool w = wait_ab(&b_empty[slot], (uint32_t)(((G / NB) & 1) ^ 1), p.err, ab);
+            for (int g = 0; g < n_groups && ok; ++g) {
+                bool w = wait_ab(&b_empty[slot], ph ^ 1u, p.err, ab);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
-                const int k0 = (g / CPS) * KC + 64 * (g % CPS) + 8 * pc;
-                uint8_t* dst = Bring + slot * B_SLOT;
-                for (int n = tq; n < n16; n += 4)
-                    cp_async16(dst + n * 128 + ((pc ^ (n & 7)) << 4), p.xperm + (size_t)myrow[n] * p.K + k0, n < ti.nv);
-                cp_async_commit();
-                if (pend >= 0) {
-                    cp_async_wait_1();                   // this warp's previous stage landed
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&b_full[pend % NB]);
+                if (lane == 0) {
+                    mbar_expect_tx(&b_full[slot], (uint32_t)B_SLOT);
+                    tma_load_2d(Bring + slot * B_SLOT, &tmx, (g / CPS) * KC + 64 * (g % CPS), ti.tok0 & ~7, &b_full[slot]);
                 }
-                pend = G;
+                __syncwarp();
+                ++issued;
+                if (++slot == NB) { slot = 0; ph ^= 1u; }
             }
         }
-        cp_async_wait_0();
-        if (pend >= 0 && ok) {
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&b_full[pend % NB]);
+        if (!ok) {
+            *ab = 1;
+            // loads still in flight land (bounded) before the block releases its memory
+            if (lane == 0)
+                for (int G = max(0, issued - NB); G < issued; ++G)
+                    (void)mbar_wait(&b_full[G % NB], (uint32_t)((G / NB) & 1), nullptr, 1u << 16);
         }
-        if (!ok) *ab = 1;
         __syncwarp();
     }
     tc_fence_before();
@@ -519,30 +537,62 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
 // Raw ring depth (chunks per decode warp) that fits next to the A and B rings (static
 // shared memory: barriers and the expert table; 1 KB of slack for the B alignment).
 int gemm_raw_slots(int tile_bytes) {
-    const int budget = 232448 - 7168 - 1024 - NA * A_SLOT - NB * B_SLOT;
+    const int budget = 232448 - 6144 - 1024 - NA * A_SLOT - NB * B_SLOT;
     return std::min(MAX_RR, budget / (DQW * tile_bytes));
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// The stage-ordered activations Xp[x_rows][K]: box {64, 256} at (chunk*KC + 64j, row) is one
+// GEMM stage of 256 consecutive rows, 32 KB written with the 128-byte swizzle (rows past
+// x_rows read as zeros).
+bool make_x_map(const GemvParams& p, CUtensorMap* map) {
+    auto enc = tensor_map_encoder();
+    if (!enc || p.x_rows <= 0 || ((uintptr_t)p.xperm & 15u) || p.K % 64) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)p.x_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)p.K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)NT_MAX};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.xperm, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int WT, int KSF>
 bool gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
-    void (*k)(const GemvParams) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
+    void (*k)(const GemvParams, const CUtensorMap) = p.mode == GM_GATEUP ? moe_gemm_kernel<WT, KSF, GM_GATEUP>
                                   : p.mode == GM_PROJ ? moe_gemm_kernel<WT, KSF, GM_PROJ>
                                                       : moe_gemm_kernel<WT, KSF, GM_DOWN>;
     GemvParams q = p;
     q.n_stages = gemm_raw_slots(p.tile_bytes);
     if (q.n_stages < (p.mode == GM_GATEUP ? 2 : 1)) return false;   // moe_gemm_supported excludes this
-    if (q.gm_nt <= 0 || q.gm_nt > NT_MAX || q.gm_nt % 16) q.gm_nt = NT_MAX;
+    if (q.gm_nt <= 0 || q.gm_nt > NT_TILE_MAX || q.gm_nt % 8) q.gm_nt = NT_TILE_MAX;
     constexpr int KC = DecSel<WT, KSF>::T::KC;
-    if (!q.xperm || q.K % KC || q.x_row0 < 0 || q.x_row0 >= q.x_rows || ((uintptr_t)q.xperm & 15u)) return false;
+    alignas(64) CUtensorMap tmx;
+    if (!q.xperm || q.K % KC || q.x_row0 < 0 || q.x_row0 >= q.x_rows || !make_x_map(q, &tmx)) return false;
     {
+        // gate/up: one row per route (expert order, up to the step's route count); else X's rows
+        const bool per_route = q.mode == GM_GATEUP;
         const long pieces = (long)(q.x_rows - q.x_row0) * (q.K / 8);
         const int blocks = (int)std::min<long>((pieces + 255) / 256, 4L * grid);
-        launch_pdl(gemm_x_stage_order_kernel<KC>, dim3(blocks), dim3(256), 0, s, q.X, q.ldx, q.x_row0, q.x_rows, q.K,
-                   q.xperm);
+        launch_pdl(gemm_x_stage_order_kernel<KC>, dim3(blocks), dim3(256), 0, s, q.X, q.ldx,
+                   per_route ? q.route_tok : (const int*)nullptr, per_route ? q.n_routes : (const int*)nullptr,
+                   q.x_row0, q.x_rows, q.K, q.xperm);
     }
     const int smem = 1024 + NB * B_SLOT + NA * A_SLOT + q.n_stages * DQW * p.tile_bytes;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    launch_pdl(k, dim3(grid), dim3(GM_THREADS), (size_t)smem, s, q);
+    launch_pdl(k, dim3(grid), dim3(GM_THREADS), (size_t)smem, s, q, tmx);
     return true;
 }
 

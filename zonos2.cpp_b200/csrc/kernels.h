@@ -72,6 +72,7 @@ struct GemvParams {
     int x_rows;                     // tensor-core GEMM: rows [x_row0, x_rows) of X that it reads
     int x_row0;
     __half* xperm;                  // tensor-core GEMM: scratch [x_rows][K] for X in stage order
+    const int* n_routes;            // device: routes of the step (gate/up gathers one row per route)
 };
 
 // Chooses warps/stages for a weight matrix and fills the launch geometry.

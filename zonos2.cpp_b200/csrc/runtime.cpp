@@ -124,7 +124,8 @@ int ctx_create(Model* m, int n_slots, int slot_cap_frames, Ctx** out, int out_ro
     acc((size_t)D.n_layer * T * c->kmax * 4);
     acc((size_t)4 * T * std::max(D.rd, 1) * 4);
     acc((size_t)T * nkv * 4);
-    const size_t gx = std::max((size_t)T * std::max((size_t)d, (size_t)nh * hd), (size_t)R * D.n_ff);
+    // tensor-core GEMM activations in stage order: projection rows, or one row per route
+    const size_t gx = std::max((size_t)T * std::max((size_t)d, (size_t)nh * hd), (size_t)R * std::max(D.n_ff, d));
     acc(gx * 2);
     acc((MAX_EXPERTS + 1) * 4);
     acc(4);
@@ -257,6 +258,13 @@ void gemm_setup_failed(Ctx* c) {
     c->enq_failed = true;
 }
 
+// Tensor-core GEMM token tile (routes or rows per tile, a multiple of 8 up to 248) for a
+// launch over `rows` token rows (for the expert passes, routes / 4): 248 from 1024 rows,
+// where each dequantised weight block then serves the most tokens and the tiles still
+// outnumber the blocks; else 120, whose smaller, more numerous tiles keep the 148 blocks
+// evenly loaded.
+int gemm_token_tile(int rows) { return rows >= 1024 ? 248 : 120; }
+
 int ctas_per_sm(int smem) { return std::max(1, std::min(4, 233472 / (smem + 1024))); }
 
 // Projection of T rows (tokens or output rows). With t_dec >= 0 the rows are a step's
@@ -293,6 +301,7 @@ void gemv_proj(Ctx* c, const DevMat* const* mats, const int* offs, int nmat, int
         p.T = T - t_dec;
         p.x_rows = T;
         p.x_row0 = t_dec;
+        p.gm_nt = gemm_token_tile(T - t_dec);
         p.xperm = c->B.gemm_x;
         if (!launch_moe_gemm(p, c->m->n_sm, c->stream)) gemm_setup_failed(c);
         c->launches++;
@@ -345,8 +354,10 @@ void gemv_moe(Ctx* c, const LayerDev& ly, int mode, bool bulk, const SegSet* seg
     c->launches++;
     if (split) {
         p.n_active = sg.n_active;
-        p.x_rows = mode == GM_GATEUP ? c->cur_T : c->cur_T * c->kmax;
+        p.x_rows = c->cur_T * c->kmax;                 // one row per route
         p.x_row0 = 0;
+        p.gm_nt = gemm_token_tile(c->cur_T * c->kmax / 4);
+        p.n_routes = sg.seg_off + ly.n_expert;
         p.xperm = c->B.gemm_x;
         if (!launch_moe_gemm(p, c->m->n_sm, c->stream)) gemm_setup_failed(c);
         c->launches++;
