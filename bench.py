@@ -20,6 +20,7 @@ schedule (steps W .. W+K-1), so they see the same refills.
 Weights streamed per step (~6-8 GB) exceed the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --config3                    Q6_K / Q8_0 mixed prefill + decode (config 3), see config3()
     python bench.py --config5 [--gpus N] ...    whole-box serving (config 5), see config5()
     python bench.py --expert-sweep               the isolated expert op (config 4)
 Under torchrun each rank runs an independent replica on its GPU (replicas only: the
@@ -271,6 +272,90 @@ def expert_sweep(args):
     m.close()
 
 
+C3_DECODE, C3_PROMPTS, C3_PROMPT, C3_CTX = 60, 4, (32, 512), (128, 4096)
+
+
+def config3(args):
+    """Config 3: the ZONOS2-scale backbone at Q6_K and at Q8_0 (Q4_K's shapes), batch 64 per
+    step: 60 streams decode one frame each and 4 new prompts of U[32, 512] rows are prefilled
+    in the same step (their last rows give 4 more frames); decode contexts U[128, 4096] with
+    f16 KV in 256-token pages. Slots 0..59 decode throughout (their seeded contexts come from
+    the KV hash fill, so no 100k-row prefill precedes the run); slots 60..63 take a new
+    prompt every step (reset to position 0). Device-resident schedule (z2b_run_schedule),
+    greedy sampling on the device. One JSON line per quantisation: frames/s (64 per step)
+    and rows/s (decode + prompt rows)."""
+    import torch
+    load_pkg()
+    import z2b.runtime as R
+    import z2b.synth as S
+    n_slots = C3_DECODE + C3_PROMPTS
+    for preset, quant in (("zonos2_q6k", "Q6_K"), ("zonos2_q8", "Q8_0")):
+        path = S.cached(preset, directory=model_dir())
+        model = R.Model(path)
+        hp = model.hp
+        g = np.random.default_rng(3)
+        ctx0 = g.integers(C3_CTX[0], C3_CTX[1] + 1, C3_DECODE)
+        ctx = R.BatchCtx(model, n_slots, C3_CTX[1] + args.warmup + args.steps + 8)
+        ctx.set_logits_readback(False)
+        for i in range(n_slots):
+            ctx.slot_reset(i, R.Sampling(greedy=True))
+        for i in range(C3_DECODE):
+            ctx.fill_kv(i, int(ctx0[i]), seed=100 + i)
+
+        def schedule(n_steps, s0):
+            descs = np.zeros((n_steps, n_slots, 6))
+            src = np.full((n_steps, n_slots), -1, np.int32)
+            rows, nrow, prompt_rows = [], 0, 0
+            for s in range(n_steps):
+                for i in range(C3_DECODE):
+                    descs[s, i] = (i, ctx0[i] + s0 + s, 1, 3, -1, 1.0)
+                    if s0 + s == 0:                      # the first frame of each decode stream
+                        src[s, i] = nrow
+                        rows.append(random_rows(g, 1))
+                        nrow += 1
+                for j in range(C3_PROMPTS):
+                    L = int(g.integers(C3_PROMPT[0], C3_PROMPT[1] + 1))
+                    descs[s, C3_DECODE + j] = (C3_DECODE + j, 0, L, 3, -1, 1.0)
+                    src[s, C3_DECODE + j] = nrow
+                    rows.append(random_rows(g, L))
+                    nrow += L
+                    prompt_rows += L
+            return descs, np.concatenate(rows), src, prompt_rows
+
+        d, rows, src, _ = schedule(args.warmup, 0)
+        ctx.run_schedule(d, rows, src)
+        ctx.sync()
+        d, rows, src, prompt_rows = schedule(args.steps, args.warmup)
+        stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", 0))
+        clocks = ClockSampler(0)
+        clocks.start()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.run_schedule(d, rows, src)
+        e1.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        ck = clocks.stop()
+        frames = args.steps * n_slots
+        line = {"metric": f"codec frames/sec/GPU, config 3 ({quant}, batch 64 = 60 decode + 4 prompts U[32,512])",
+                "value": frames / (ms * 1e-3), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 (weights decoded in registers; prompt rows on the tcgen05 GEMM)",
+                "data": "synthetic",
+                "config": {"workload": f"config3: ZONOS2-scale {quant} backbone, 60 decode streams ctx U[128,4096] "
+                                       f"+ 4 prompts U[32,512] per step", "global_batch": n_slots,
+                           "seq_len": "ctx U[128,4096]", "parallelism": "replicas x1", "sampling": "greedy",
+                           "l2": "weights streamed per step exceed L2; no flush needed"},
+                "rows_per_s": (args.steps * C3_DECODE + prompt_rows) / (ms * 1e-3),
+                "prompt_rows_per_step": prompt_rows / args.steps, "gpu_launches": ctx.last_run_launches(),
+                "clocks": ck}
+        print(json.dumps(line), flush=True)
+        ctx.close()
+        model.close()
+
+
 C5_SLOTS, C5_RATE, C5_PROMPT, C5_GEN, C5_REQUESTS = 32, 50.0, (32, 256), (300, 1500), 8192
 
 
@@ -400,12 +485,16 @@ def main():
                     help="config 4: the isolated expert op over T in {16, 64, 256, 1024, 4096}, one JSON line each")
     ap.add_argument("--sweep-t", type=int, nargs="*", default=None,
                     help="with --expert-sweep: only these token counts (small ncu captures)")
+    ap.add_argument("--config3", action="store_true",
+                    help="config 3: Q6_K and Q8_0 backbones, 60 decode + 4 prompt streams per step, one JSON line each")
     ap.add_argument("--config5", action="store_true",
                     help="config 5: whole-box serving of Poisson arrivals through the replica dispatcher")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.expert_sweep:
         return expert_sweep(args)
+    if args.config3:
+        return config3(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

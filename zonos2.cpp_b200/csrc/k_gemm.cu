@@ -6,27 +6,32 @@
 // projections (ggml_mul_mat, :107-111, 175) over the prompt rows of a step (GM_PROJ: the
 // segments' weights over a contiguous token range, store / add / softcap epilogue).
 //
-// Tile = (expert, 128 weight rows, up to 256 routed tokens); the MMA is M 128 x N (the
-// tile's token count rounded up to 16) x K 16, f16 x f16 -> f32 in tensor memory (TMEM:
-// gate at columns [0, 256), up at [256, 512)). A persistent block walks its tiles with
+// Tile = (expert, 128 weight rows, up to 248 routes); the MMA is M 128 x N (the tile's
+// activation rows, which start 8-aligned at or before its first route, rounded up to 16)
+// x K 16, f16 x f16 -> f32 in tensor memory (TMEM: gate at columns [0, 256), up at [256,
+// 512)). Before the GEMM a small kernel copies the activations in stage order (a stage's
+// 64 k values contiguous; for gate/up one row per route, in expert order), so a tile's
+// stage of activations is one TMA box. A persistent block walks its tiles with
 // warp-specialised roles that hand over through mbarriers, never a block-wide barrier:
-//   - 8 decode warps, one per 16-row weight tile of the block. Each lane-0 streams its
-//     row tile's quantised chunks (cp.async.bulk, one chunk of one matrix per ring slot,
-//     continuing into the block's next tile); the warp decodes a 64-wide K stage of a
-//     chunk with the same in-register decoders as the GEMV (so the weight values are
-//     identical) and stores it into an A ring slot in the UMMA K-major layout with
-//     conflict-free 16-byte stores. The same warps gather the tiles' activation rows
-//     (cp.async, two stages ahead) into a B ring and run the epilogue.
+//   - 8 decode warps, one per 16-row weight tile. Lane 0 of each streams its tile's
+//     quantised chunks (cp.async.bulk, one chunk of one matrix per ring slot, continuing
+//     into the block's next tile); the warp decodes each 64-wide K stage with the same
+//     in-register decoders as the GEMV (so the weight values are identical) into an A ring
+//     slot in the UMMA K-major layout, with conflict-free 16-byte stores. The same warps
+//     run the epilogue.
 //   - 1 MMA warp: one lane waits for each stage's A and B, issues four tcgen05.mma and
 //     releases the slots with tcgen05.commit; after a tile's last stage it commits to the
 //     accumulator barrier the epilogue waits on.
+//   - 1 activation producer: one TMA box (no multicast) per stage into a B ring slot.
 // A stage covers, per lane quarter q of the decoders, k = chunk*KC + q*KC/4 + 16j + [0,16):
-// four 16-wide runs of the chunk (the tile layout's fragment order); B gathers the same k
-// runs in the same order, so the contraction is over the same 64 k values.
+// four 16-wide runs of the chunk (the tile layout's fragment order); the stage-ordered
+// activations hold the same k values in the same order, so the contraction is over the
+// same 64 k values.
 //
-// Shared-memory operand layout (K-major, no swizzle): 8x8 core matrices of 16-byte rows;
-// element (m, k) of a slot at (k / 8) * LBO + (m / 8) * 128 + (m % 8) * 16 + (k % 8) * 2
-// with LBO = 128 * rows / 8 (2048 B for the 128 weight rows, 4096 B for 256 tokens).
+// Shared-memory operand layouts (K-major): A without swizzle, 8x8 core matrices of 16-byte
+// rows, element (m, k) at (k / 8) * LBO + (m / 8) * 128 + (m % 8) * 16 + (k % 8) * 2 with
+// LBO = 2048 + 16 (padded for the decoders' stores); B with the 128-byte swizzle, row n at
+// n * 128 with its 16-byte chunk c at chunk c ^ (n % 8), 8-row atoms 1024 bytes apart.
 #include "common.cuh"
 #include "gguf.h"
 #include "kernels.h"
@@ -497,7 +502,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
         __syncwarp();
     } else {
         // ---- activation (B) producer warp: stage g of a tile is the 64-wide stage-ordered
-        // column block (chunk*KC + 64j) of the 256 consecutive rows from tok0 & ~7 of Xp (the
+        // column block (chunk*KC + 64j) of the NT + 8 consecutive rows from tok0 & ~7 of Xp (the
         // tile's routes, then rows of the next routes or zero fill past the end, in columns
         // the epilogue never reads): one TMA box with the 128-byte swizzle. ----
         int slot = 0, issued = 0;
@@ -509,7 +514,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) moe_gemm_kernel(const GemvParam
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) break;
                 if (lane == 0) {
-                    mbar_expect_tx(&b_full[slot], (uint32_t)B_SLOT);
+                    mbar_expect_tx(&b_full[slot], (uint32_t)((NT + 8) * 128));
                     tma_load_2d(Bring + slot * B_SLOT, &tmx, (g / CPS) * KC + 64 * (g % CPS), ti.tok0 & ~7, &b_full[slot]);
                 }
                 __syncwarp();
@@ -554,15 +559,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// The stage-ordered activations Xp[x_rows][K]: box {64, 256} at (chunk*KC + 64j, row) is one
-// GEMM stage of 256 consecutive rows, 32 KB written with the 128-byte swizzle (rows past
-// x_rows read as zeros).
+// The stage-ordered activations Xp[x_rows][K]: box {64, gm_nt + 8} at (chunk*KC + 64j, row)
+// is one GEMM stage of a tile's rows (its routes start at most 7 rows in), written with the
+// 128-byte swizzle (rows past x_rows read as zeros).
 bool make_x_map(const GemvParams& p, CUtensorMap* map) {
     auto enc = tensor_map_encoder();
     if (!enc || p.x_rows <= 0 || ((uintptr_t)p.xperm & 15u) || p.K % 64) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)p.K, (cuuint64_t)p.x_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)p.K * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)NT_MAX};
+    const cuuint32_t box[2] = {64, (cuuint32_t)(p.gm_nt + 8)};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.xperm, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
