@@ -68,22 +68,21 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 // active[0, n_small) lists the experts with GEMV routes, active[n_small, n_active) those
 // with GEMM routes (an expert can be in both). tile_off (optional): prefix over the GEMV
 // list of ceil(routes / 8).
-// Up to SEG_STAGE routes are read from global memory once, in one pass, and placed from
-// shared memory; larger steps read them per expert.
-constexpr int SEG_STAGE = 2048;
+// Up to st_cap routes (the caller's shared-memory staging area: st_se / st_sw, 8 bytes per
+// route) are read from global memory once, in one pass, and placed from shared memory;
+// larger steps read them again per expert, which costs a dependent global round trip per
+// 32 routes and expert.
 __device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
                                int* seg_off, int* seg_mid, int* active, int* n_active, int* route_tok,
                                float* route_w, int* route_pos, int* tile_off, int* n_small, int bulk_mode,
-                               const int* tok_desc, const SlotDesc* descs) {
+                               const int* tok_desc, const SlotDesc* descs, int* s_se, float* s_sw, int st_cap) {
     __shared__ int cntb[MAX_EXPERTS];
     __shared__ int s_off[MAX_EXPERTS];
-    __shared__ int s_se[SEG_STAGE];              // expert | GEMM-part flag << 16, or -1
-    __shared__ float s_sw[SEG_STAGE];
     auto tok_bulk = [&](int t) -> bool {
         return bulk_mode == 2 && descs[tok_desc[t]].n_new > 1;
     };
     const int R = T * k;
-    const bool staged = R <= SEG_STAGE;
+    const bool staged = R <= st_cap;                 // s_se: expert | GEMM-part flag << 16, or -1
     for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; cntb[e] = 0; }
     __syncthreads();
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
@@ -262,7 +261,7 @@ __global__ void __launch_bounds__(256) router_proj_kernel(const StepBufs b, cons
 // them into shared memory before the wait on router_proj. The last block to finish
 // builds the expert segments.
 __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const LayerSmall ly, const Dims dm,
-                                                         int first_moe, int T, int layer, int stage) {
+                                                         int first_moe, int T, int layer, int stage, int seg_cap) {
     extern __shared__ __align__(128) float sh[];
     __shared__ __align__(8) uint64_t bar;
     __shared__ float red[32];
@@ -450,29 +449,36 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // the block's dynamic shared memory (MLP weights, vectors) is free now: it stages the routes
     build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.seg_mid, b.active, b.n_active, b.route_tok,
-                   b.route_w, b.route_pos, b.tile_off, b.n_small, ly.gemm_ok ? 2 : 0, b.tok_desc, b.descs);
+                   b.route_w, b.route_pos, b.tile_off, b.n_small, ly.gemm_ok ? 2 : 0, b.tok_desc, b.descs,
+                   reinterpret_cast<int*>(sh), sh + seg_cap, seg_cap);
     if (threadIdx.x == 0) {
         if (b.layer_active) b.layer_active[layer] = *b.n_active;
         *b.ticket = 0;
     }
 }
 
-__global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_mode) {
+__global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_mode, int seg_cap) {
+    extern __shared__ __align__(16) float seg_st[];  // [seg_cap] ids, then [seg_cap] weights
     __shared__ int cnt[MAX_EXPERTS];
     pdl_wait();
     pdl_release();
     for (int j = threadIdx.x; j < T * b.kmax; j += blockDim.x) b.route_pos[j] = -1;
     __syncthreads();
     build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.seg_mid, b.active, b.n_active, b.route_tok,
-                   b.route_w, b.route_pos, b.tile_off, b.n_small, bulk_mode, nullptr, nullptr);
+                   b.route_w, b.route_pos, b.tile_off, b.n_small, bulk_mode, nullptr, nullptr,
+                   reinterpret_cast<int*>(seg_st), seg_st + seg_cap, seg_cap);
 }
 
 __global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
                                   int* n_active, int* route_tok, float* route_w, int* route_pos) {
+    constexpr int kStage = 2048;                     // routes staged in shared memory (static)
     __shared__ int cnt[MAX_EXPERTS];
+    __shared__ int st_se[kStage];
+    __shared__ float st_sw[kStage];
     build_segments(sel, selw, T, k, k, E, cnt, seg_off, nullptr, active, n_active, route_tok, route_w, route_pos,
-                   nullptr, nullptr, 0, nullptr, nullptr);
+                   nullptr, nullptr, 0, nullptr, nullptr, st_se, st_sw, kStage);
 }
 
 }  // namespace
@@ -486,18 +492,23 @@ size_t router_mlp_smem(const Dims& d, int E, bool* stage) {
     return *stage ? base + w : base;
 }
 
-void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
-                   cudaStream_t s) {
-    // the dynamic shared memory opt-in is a per-device function attribute: set it once on
-    // every device a context runs on (one process may drive several GPUs)
+// The dynamic shared memory opt-in is a per-device function attribute: set it once on
+// every device a context runs on (one process may drive several GPUs).
+void router_attributes() {
     static std::atomic<bool> configured[kMaxRouterDevices];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= kMaxRouterDevices || !configured[dev].load(std::memory_order_acquire)) {
         cudaFuncSetAttribute(router_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         cudaFuncSetAttribute(router_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(segments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (dev >= 0 && dev < kMaxRouterDevices) configured[dev].store(true, std::memory_order_release);
     }
+}
+
+void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T, int first_moe, int layer,
+                   cudaStream_t s) {
+    router_attributes();
     if (ly.is_moe) {
         const int nks = router_kslices(d.n_embd), L = d.n_embd / nks, S = L + 4;
         const size_t smem = (size_t)((RP_TOK + RP_ROWS) * S + L) * sizeof(float);
@@ -506,13 +517,17 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
     }
     bool stage = false;
     const size_t smem = router_mlp_smem(d, ly.is_moe ? ly.n_expert : 1, &stage);
-    launch_pdl(router_mlp_kernel, dim3(T), dim3(512), smem, s, b, ly, d, first_moe, T, layer, stage ? 1 : 0);
+    launch_pdl(router_mlp_kernel, dim3(T), dim3(512), smem, s, b, ly, d, first_moe, T, layer, stage ? 1 : 0,
+               (int)(smem / 8));
 }
 
 int router_launches(const LayerSmall& ly) { return ly.is_moe ? 2 : 1; }
 
 void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s) {
-    launch_pdl(segments_kernel, dim3(1), dim3(1024), 0, s, b, T, k, E, bulk_mode);
+    // every route staged in shared memory (8 bytes each, up to 24K routes)
+    router_attributes();
+    const int cap = std::min(T * k, 24 * 1024);
+    launch_pdl(segments_kernel, dim3(1), dim3(1024), (size_t)cap * 8, s, b, T, k, E, bulk_mode, cap);
 }
 
 }  // namespace z2b
