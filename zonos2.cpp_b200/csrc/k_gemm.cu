@@ -22,7 +22,7 @@
 //   - 1 MMA warp: one lane waits for each stage's A and B, issues four tcgen05.mma and
 //     releases the slots with tcgen05.commit; after a tile's last stage it commits to the
 //     accumulator barrier the epilogue waits on.
-//   - 1 activation producer: one TMA box (no multicast) per stage into a B ring slot.
+//   - 1 activation producer: one TMA box per stage into a B ring slot (this CTA only).
 // A stage covers, per lane quarter q of the decoders, k = chunk*KC + q*KC/4 + 16j + [0,16):
 // four 16-wide runs of the chunk (the tile layout's fragment order); the stage-ordered
 // activations hold the same k values in the same order, so the contraction is over the
@@ -84,7 +84,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
            (2ull << 61);
 }
 
-// One tiled TMA load (no multicast) of a 2-D box completing on `bar`; x is a multiple of 64
+// One tiled TMA load (this CTA only) of a 2-D box completing on `bar`; x is a multiple of 64
 // elements (128 bytes).
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(

@@ -8,7 +8,7 @@
 // Work item = (matrix or expert, row-tile of 16 output rows). A CTA owns a contiguous
 // run of items; its warps split each item's K range. Each warp streams its K-slice of
 // every item through a private ring of shared-memory stages filled by one-lane
-// cp.async.bulk copies (no multicast), decodes the quantised weights in registers
+// cp.async.bulk copies (this CTA only), decodes the quantised weights in registers
 // straight into mma.sync.m16n8k16 A fragments (tile_layout.h), multiplies them with the
 // activation fragments (f16, 8 tokens per n-tile) and accumulates in f32. Partial sums
 // are reduced across warps in shared memory in a fixed order, so results do not depend
