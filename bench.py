@@ -21,6 +21,7 @@ Weights streamed per step (~6-8 GB) exceed the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --config3                    Q6_K / Q8_0 mixed prefill + decode (config 3), see config3()
+    python bench.py --crossover                  the expert op's GEMV / GEMM crossover (config 4), see crossover()
     python bench.py --config5 [--gpus N] ...    whole-box serving (config 5), see config5()
     python bench.py --expert-sweep               the isolated expert op (config 4)
 Under torchrun each rank runs an independent replica on its GPU (replicas only: the
@@ -47,6 +48,7 @@ STREAMS = 16
 STEPS_PER_STREAM = 256
 REFILL_PROMPT = 96
 CTX_RANGE = (64, 2048)
+PREWARM_STEPS = 64           # untimed schedule steps before the value window (graph shapes seen)
 
 
 def load_pkg():
@@ -272,6 +274,44 @@ def expert_sweep(args):
     m.close()
 
 
+def crossover(args):
+    """Config 4's GEMV / GEMM crossover: the expert FFN of one ZONOS2 MoE layer with every
+    expert given exactly n routes (T = 8n tokens, token t routed to experts 4t..4t+3 mod 32,
+    x ~ N(0, 1)), timed with every expert on the tile GEMV and with every expert on the
+    tcgen05 GEMM (z2b_set_expert_gemm_min). One JSON line per n; the last line names the
+    smallest n from which the GEMM is faster."""
+    load_pkg()
+    import z2b.runtime as R
+    import z2b.synth as S
+    path = S.cached("zonos2", directory=model_dir(), n_layer=1, expert_used=[4])
+    m = R.Model(path)
+    ctx = R.BatchCtx(m, 16, 64)
+    E, k, d = m.hp.n_expert, 4, m.hp.n_embd
+    reps = max(args.steps // 8, 10)
+    cross = None
+    for n in (4, 8, 12, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512):
+        T = 8 * n
+        g = np.random.default_rng(n)
+        x = g.standard_normal((T, d)).astype(np.float32)
+        sel = ((4 * np.arange(T)[:, None] + np.arange(k)[None, :]) % E).astype(np.int32)
+        w = np.full((T, k), 0.25, np.float32)
+        ctx.set_expert_gemm_min(1 << 30)
+        _, ms_gemv, nbytes, ng0 = ctx.expert_op(0, x, sel, w, reps=reps, want_out=False)
+        ctx.set_expert_gemm_min(1)
+        _, ms_gemm, _, ng1 = ctx.expert_op(0, x, sel, w, reps=reps, want_out=False)
+        if cross is None and ms_gemm <= ms_gemv:
+            cross = n
+        print(json.dumps({"metric": "expert FFN op, GEMV vs tcgen05 GEMM (config 4 crossover)", "routes_per_expert": n,
+                          "T": T, "ms_gemv": ms_gemv, "ms_gemm": ms_gemm, "experts_on_gemm": [ng0, ng1],
+                          "gemv_weight_gbs": nbytes / (ms_gemv * 1e-3) / 1e9,
+                          "gemm_tflops": 2.0 * T * k * 3 * d * m.hp.n_ff / (ms_gemm * 1e-3) / 1e12}), flush=True)
+    ctx.set_expert_gemm_min(17)
+    print(json.dumps({"metric": "GEMV / GEMM crossover (routes per expert)", "value": cross,
+                      "note": "smallest n of the sweep from which the GEMM is at least as fast"}), flush=True)
+    ctx.close()
+    m.close()
+
+
 C3_DECODE, C3_PROMPTS, C3_PROMPT, C3_CTX = 60, 4, (32, 512), (128, 4096)
 
 
@@ -485,6 +525,8 @@ def main():
                     help="config 4: the isolated expert op over T in {16, 64, 256, 1024, 4096}, one JSON line each")
     ap.add_argument("--sweep-t", type=int, nargs="*", default=None,
                     help="with --expert-sweep: only these token counts (small ncu captures)")
+    ap.add_argument("--crossover", action="store_true",
+                    help="config 4's GEMV / GEMM crossover: n routes per expert on either path, one JSON line per n")
     ap.add_argument("--config3", action="store_true",
                     help="config 3: Q6_K and Q8_0 backbones, 60 decode + 4 prompt streams per step, one JSON line each")
     ap.add_argument("--config5", action="store_true",
@@ -495,6 +537,8 @@ def main():
         return expert_sweep(args)
     if args.config3:
         return config3(args)
+    if args.crossover:
+        return crossover(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -552,8 +596,11 @@ def main():
     stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local if world > 1 else 0))
     frames_per_step = STREAMS
 
-    # ---- value: device-resident scheduled run
-    d, rows, src = build_schedule(args.warmup, first)
+    # ---- value: device-resident scheduled run. The warm-up is W steps of the continuous
+    # schedule and at least PREWARM_STEPS: a step shape carrying prompt rows is graph-captured
+    # on its second occurrence, and with a short warm-up the refill shapes would first repeat
+    # (and be captured, a one-off host cost) inside the timed window.
+    d, rows, src = build_schedule(max(args.warmup, PREWARM_STEPS), first)
     ctx.run_schedule(d, rows, src)
     ctx.sync()
     d, rows, src = build_schedule(args.steps, None)
@@ -658,6 +705,7 @@ def main():
         "value": world * frames_per_step * args.steps / (t_value * 1e-3),
         "unit": "frames/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "warmup_steps_run": max(args.warmup, PREWARM_STEPS),
         "ms_per_step": t_value / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 (mma.sync f16 x f16 -> f32; Q4_K/F16/Q8_0 weights decoded in registers)",

@@ -98,9 +98,16 @@ int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, i
 int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
                                int32_t* route_tok, int32_t* route_pos);
 
+/* No reference counterpart. Tuning of z2b_expert_op (z2b.h): an expert with at least
+ * `routes` routes takes the tcgen05 grouped GEMM, one with fewer the tile GEMV (default 17;
+ * 1 sends every expert to the GEMM, a value above the op's route count none). Used to
+ * measure the GEMV / GEMM crossover; the decode step keeps its own rule. Z2B_ERR_ARG for
+ * routes < 1. */
+struct z2b_ctx;
+int z2b_set_expert_gemm_min(struct z2b_ctx* ctx, int routes);
+
 /* Router ids of every layer for the last z2b_step: writes [n_layer][T][kmax] when cap is
  * large enough; returns the number of entries (or -1). */
-struct z2b_ctx;
 int z2b_debug_last_sel(struct z2b_ctx* ctx, int32_t* out, int cap);
 
 /* Test support, no reference counterpart (need a GPU).

@@ -77,3 +77,31 @@ def test_expert_op_vs_float32(model_dir, T):
     print(f"T {T}: {n_gemm} experts on the tcgen05 GEMM, worst token cos {c.min():.7f}")
     assert c.min() >= 0.9999, (int(c.argmin()), c.min())
     assert np.abs(out - ref).max() / np.abs(ref).max() <= 1e-2
+
+
+@pytest.mark.parametrize("gemm_min", [1, 1 << 30])
+def test_expert_op_forced_path(model_dir, gemm_min):
+    """The threshold of z2b_set_expert_gemm_min: 1 sends every expert (down to 1-route ones,
+    a 16-wide MMA over a single route) to the tcgen05 GEMM, 2^30 every expert to the tile
+    GEMV (up to ~40 routes, three 16-token passes); both match the float32 reference."""
+    path = S.cached("zonos2", directory=model_dir, n_layer=1, expert_used=[4])
+    m = R.Model(path)
+    T = 96
+    try:
+        ctx = R.BatchCtx(m, 16, 64)
+        ctx.set_expert_gemm_min(gemm_min)
+        x = np.random.default_rng(5).standard_normal((T, m.hp.n_embd)).astype(np.float32)
+        sel, w = routing(T, m.hp.n_expert, 4, seed=6)
+        out, _, _, n_gemm = ctx.expert_op(0, x, sel, w)
+        with pytest.raises(RuntimeError):
+            ctx.set_expert_gemm_min(0)
+        ctx.close()
+    finally:
+        m.close()
+    assert n_gemm == (len(np.unique(sel)) if gemm_min == 1 else 0)
+    ref = reference(path, x, sel, w)
+    a, b = out.astype(np.float64), ref.astype(np.float64)
+    c = (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+    print(f"gemm_min {gemm_min}: {n_gemm} experts on the tcgen05 GEMM, worst token cos {c.min():.7f}")
+    assert c.min() >= 0.9999, (int(c.argmin()), c.min())
+    assert np.abs(out - ref).max() / np.abs(ref).max() <= 1e-2

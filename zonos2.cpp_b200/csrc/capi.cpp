@@ -234,6 +234,11 @@ int z2b_expert_op(z2b_ctx* ctx, int layer, const float* x, int T, const int32_t*
     return rc;
 }
 
+int z2b_set_expert_gemm_min(z2b_ctx* ctx, int routes) {
+    if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
+    return ctx_set_expert_gemm_min(ctx->c, routes);
+}
+
 int z2b_debug_fill_kv(z2b_ctx* ctx, int slot, int n, uint32_t seed) {
     if (!ctx) { set_error("null argument"); return Z2B_ERR_ARG; }
     cudaSetDevice(ctx->c->m->device);

@@ -59,7 +59,7 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 // follow (from seg_mid[e]), each part ordered by token, then rank in the token's top-k.
 // Which part a route joins depends on bulk_mode:
 //   0: none take the GEMM;
-//   1: all routes of an expert with >= GEMM_MIN_TOKENS routes (the isolated expert op);
+//   1: all routes of an expert with >= gemm_min routes (the isolated expert op);
 //   2: the routes of prompt rows (tokens whose descriptor feeds more than one row) of
 //      experts with >= GEMM_MIN_PROMPT_ROUTES such routes (the decode step); an expert
 //      with fewer takes them in its GEMV pass, which streams its weights anyway. Decode
@@ -75,7 +75,8 @@ __device__ __forceinline__ void block_matvec(const float* __restrict__ W, const 
 __device__ void build_segments(const int* sel, const float* selw, int T, int k, int kmax, int E, int* cnt,
                                int* seg_off, int* seg_mid, int* active, int* n_active, int* route_tok,
                                float* route_w, int* route_pos, int* tile_off, int* n_small, int bulk_mode,
-                               const int* tok_desc, const SlotDesc* descs, int* s_se, float* s_sw, int st_cap) {
+                               const int* tok_desc, const SlotDesc* descs, int* s_se, float* s_sw, int st_cap,
+                               int gemm_min = GEMM_MIN_TOKENS) {
     __shared__ int cntb[MAX_EXPERTS];
     __shared__ int s_off[MAX_EXPERTS];
     auto tok_bulk = [&](int t) -> bool {
@@ -100,7 +101,7 @@ __device__ void build_segments(const int* sel, const float* selw, int T, int k, 
     }
     __syncthreads();
     if (bulk_mode == 1)
-        for (int e = threadIdx.x; e < E; e += blockDim.x) cntb[e] = cnt[e] >= GEMM_MIN_TOKENS ? cnt[e] : 0;
+        for (int e = threadIdx.x; e < E; e += blockDim.x) cntb[e] = cnt[e] >= gemm_min ? cnt[e] : 0;
     if (bulk_mode == 2)
         for (int e = threadIdx.x; e < E; e += blockDim.x) if (cntb[e] < GEMM_MIN_PROMPT_ROUTES) cntb[e] = 0;
     __syncthreads();
@@ -459,7 +460,7 @@ __global__ void __launch_bounds__(512) router_mlp_kernel(const StepBufs b, const
     }
 }
 
-__global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_mode, int seg_cap) {
+__global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_mode, int seg_cap, int gemm_min) {
     extern __shared__ __align__(16) float seg_st[];  // [seg_cap] ids, then [seg_cap] weights
     __shared__ int cnt[MAX_EXPERTS];
     pdl_wait();
@@ -468,7 +469,7 @@ __global__ void segments_kernel(const StepBufs b, int T, int k, int E, int bulk_
     __syncthreads();
     build_segments(b.sel, b.selw, T, k, b.kmax, E, cnt, b.seg_off, b.seg_mid, b.active, b.n_active, b.route_tok,
                    b.route_w, b.route_pos, b.tile_off, b.n_small, bulk_mode, nullptr, nullptr,
-                   reinterpret_cast<int*>(seg_st), seg_st + seg_cap, seg_cap);
+                   reinterpret_cast<int*>(seg_st), seg_st + seg_cap, seg_cap, gemm_min);
 }
 
 __global__ void route_test_kernel(const int* sel, const float* selw, int T, int k, int E, int* seg_off, int* active,
@@ -523,11 +524,11 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
 
 int router_launches(const LayerSmall& ly) { return ly.is_moe ? 2 : 1; }
 
-void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s) {
+void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s, int gemm_min) {
     // every route staged in shared memory (8 bytes each, up to 24K routes)
     router_attributes();
     const int cap = std::min(T * k, 24 * 1024);
-    launch_pdl(segments_kernel, dim3(1), dim3(1024), (size_t)cap * 8, s, b, T, k, E, bulk_mode, cap);
+    launch_pdl(segments_kernel, dim3(1), dim3(1024), (size_t)cap * 8, s, b, T, k, E, bulk_mode, cap, gemm_min);
 }
 
 }  // namespace z2b

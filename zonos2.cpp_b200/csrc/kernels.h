@@ -193,7 +193,9 @@ void launch_router(const StepBufs& b, const LayerSmall& ly, const Dims& d, int T
                    cudaStream_t s);
 int router_launches(const LayerSmall& ly);
 // Expert segments from given router ids b.sel/b.selw (one block; the router's own last step).
-void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s);
+// bulk_mode 1: experts with >= gemm_min routes take the tensor-core GEMM.
+void launch_segments(const StepBufs& b, int T, int k, int E, int bulk_mode, cudaStream_t s,
+                     int gemm_min = GEMM_MIN_TOKENS);
 // f32 rows -> f16 rows (n values).
 void launch_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 // Device-resident decode loop: feed each stream its sampled frame (+ text pad) as the

@@ -972,6 +972,12 @@ namespace z2b {
 // x -> f16, segments from the given ids, then the decode step's own expert passes
 // (tile GEMV for experts with few routes, tcgen05 GEMM for the rest). out[t] = sum over
 // the token's routes of selw * down(SwiGLU(gate, up)).
+int ctx_set_expert_gemm_min(Ctx* c, int routes) {
+    if (routes < 1) { set_error("expert GEMM threshold must be >= 1 route"); return Z2B_ERR_ARG; }
+    c->expert_gemm_min = routes;
+    return Z2B_OK;
+}
+
 int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k, float* out,
                   int reps, double* ms, uint64_t* weight_bytes, int* n_gemm) {
     Model* m = c->m;
@@ -991,8 +997,8 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
     CK(cudaMemcpyAsync(B.sel, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(B.selw, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice, c->stream));
     launch_to_f16(B.res, B.cur, (size_t)T * d, c->stream);
-    const bool bulk = T >= GEMM_MIN_TOKENS && ly.small.gemm_ok;
-    launch_segments(B, T, k, ly.n_expert, bulk ? 1 : 0, c->stream);
+    const bool bulk = T >= c->expert_gemm_min && ly.small.gemm_ok;   // some expert can reach the threshold
+    launch_segments(B, T, k, ly.n_expert, bulk ? 1 : 0, c->stream, c->expert_gemm_min);
     const bool prof = c->profiling;
     c->profiling = false;
     c->enq_failed = false;

@@ -67,7 +67,8 @@ struct Ctx {
     std::map<uint64_t, int> shape_seen;      // occurrences of step shapes carrying prompt rows
     int prompt_graphs = 0;
     bool enq_failed = false;
-    int cur_T = 0;                           // rows of the step (or expert op) being enqueued                 // a launch could not be set up while enqueuing (error set)
+    int cur_T = 0;                           // rows of the step (or expert op) being enqueued
+    int expert_gemm_min = GEMM_MIN_TOKENS;   // expert op: routes from which an expert takes the GEMM                 // a launch could not be set up while enqueuing (error set)
     int launches = 0, loop_launches = 0;
     // decode-loop uniforms
     double* d_canon_all = nullptr;
@@ -123,6 +124,7 @@ int ctx_time_expert_gemv(Ctx* c, int which, int reps, double* ms_per_launch, uin
 int ctx_debug_fill_kv(Ctx* c, int slot, int n, uint32_t seed);
 int ctx_debug_router_capture(Ctx* c, int enable);
 int ctx_debug_router_inputs(Ctx* c, int layer, float* res, float* state, int* T);
+int ctx_set_expert_gemm_min(Ctx* c, int routes);
 int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k, float* out,
                   int reps, double* ms, uint64_t* weight_bytes, int* n_gemm);
 

@@ -102,6 +102,7 @@ def lib():
             "z2b_host_unpack_tiles": ([ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64, V, V], I),
             "z2b_slot_after_frame": ([ctypes.POINTER(HParams), ctypes.POINTER(SlotState), V, I, I], I),
             "z2b_debug_fill_kv": ([P, I, I, ctypes.c_uint32], I),
+            "z2b_set_expert_gemm_min": ([P, I], I),
             "z2b_debug_router_capture": ([P, I], I),
             "z2b_debug_router_inputs": ([P, I, V, V, ctypes.POINTER(ctypes.c_int)], I),
             "z2b_debug_last_sel": ([P, V, I], I),
@@ -289,6 +290,10 @@ class BatchCtx:
         ms, nb = ctypes.c_double(), ctypes.c_uint64()
         _check(lib().z2b_time_expert_gemv(self.h, int(which), int(reps), ctypes.byref(ms), ctypes.byref(nb)))
         return ms.value, nb.value
+
+    def set_expert_gemm_min(self, routes: int):
+        """Routes from which an expert of the isolated expert op takes the tensor-core GEMM."""
+        _check(lib().z2b_set_expert_gemm_min(self.h, int(routes)))
 
     def expert_op(self, layer: int, x, sel, selw, reps: int = 0, want_out: bool = True):
         """The isolated expert op of a MoE layer: returns (out [T][d] or None, ms per
