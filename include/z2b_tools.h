@@ -91,8 +91,8 @@ int z2b_test_route(const int32_t* sel, const float* selw, int T, int k, int E, i
  * budget of the GPU to its KV page pool, or a latency-critical thread, since allocation
  * can synchronise the whole device and stall decode steps queued by other threads.
  * Runs on the current device and the calling thread's per-thread default stream, and
- * returns when the results are in the host arrays. The first call on each device looks
- * up the scratch address (set-up), so make it before any stream capture begins. Calls
+ * returns when the results are in the host arrays. The first call on each device also
+ * looks up the scratch address (a one-time set-up on that device). Calls
  * that overlap on the GPU share the scratch and race: serialise them. T * k >
  * Z2B_NOALLOC_MAX_ROUTES returns Z2B_ERR_ARG with z2b_last_error() naming the limit. */
 int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int k, int E, int32_t* seg_off,
