@@ -9,8 +9,13 @@
 namespace z2b {
 
 constexpr int MAX_EXPERTS = 256;
-constexpr int GEMM_MIN_TOKENS = 17;  // isolated expert op: routes from which an expert takes the
-                                     // tensor-core GEMM (the GEMV holds at most 16 tokens per pass)
+// Routes from which an expert takes the tensor-core GEMM rather than the tile GEMV. With
+// every expert on one path the crossover is 48 routes (bench.py --crossover), but the two
+// passes run back to back and, once the GEMM launches, its tiles fill one wave of the SMs:
+// an expert added to it costs little, while one moved to the GEMV adds a pass per 16
+// routes. Measured on the skewed config-4 op, 48 instead of 17 took T = 256 from 0.216 to
+// 0.372 ms, so the GEMM takes every expert past the GEMV's single 16-token pass.
+constexpr int GEMM_MIN_TOKENS = 17;  // isolated expert op
 constexpr int PROJ_GEMM_MIN_ROWS = 17;      // prompt rows from which a step's projections run them
                                             // on the tensor-core GEMM (the GEMV holds 16 per pass)
 constexpr int GEMM_MIN_PROMPT_ROUTES = 33;  // decode step: prompt-row routes from which an expert's
