@@ -305,7 +305,7 @@ def crossover(args):
                           "T": T, "ms_gemv": ms_gemv, "ms_gemm": ms_gemm, "experts_on_gemm": [ng0, ng1],
                           "gemv_weight_gbs": nbytes / (ms_gemv * 1e-3) / 1e9,
                           "gemm_tflops": 2.0 * T * k * 3 * d * m.hp.n_ff / (ms_gemm * 1e-3) / 1e12}), flush=True)
-    ctx.set_expert_gemm_min(17)
+    ctx.set_expert_gemm_min(9)
     print(json.dumps({"metric": "GEMV / GEMM crossover (routes per expert)", "value": cross,
                       "note": "smallest n of the sweep from which the GEMM is at least as fast"}), flush=True)
     ctx.close()

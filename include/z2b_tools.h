@@ -99,7 +99,7 @@ int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int
                                int32_t* route_tok, int32_t* route_pos);
 
 /* No reference counterpart. Tuning of z2b_expert_op (z2b.h): an expert with at least
- * `routes` routes takes the tcgen05 grouped GEMM, one with fewer the tile GEMV (default 17;
+ * `routes` routes takes the tcgen05 grouped GEMM, one with fewer the tile GEMV (default 9;
  * 1 sends every expert to the GEMM, a value above the op's route count none). Used to
  * measure the GEMV / GEMM crossover; the decode step keeps its own rule. Z2B_ERR_ARG for
  * routes < 1. */

@@ -13,9 +13,10 @@ constexpr int MAX_EXPERTS = 256;
 // every expert on one path the crossover is 48 routes (bench.py --crossover), but the two
 // passes run back to back and, once the GEMM launches, its tiles fill one wave of the SMs:
 // an expert added to it costs little, while one moved to the GEMV adds a pass per 16
-// routes. Measured on the skewed config-4 op, 48 instead of 17 took T = 256 from 0.216 to
-// 0.372 ms, so the GEMM takes every expert past the GEMV's single 16-token pass.
-constexpr int GEMM_MIN_TOKENS = 17;  // isolated expert op
+// routes, and every expert the GEMV keeps costs it a full weight stream. Measured on the
+// skewed config-4 op (ms at T = 64 / 256): threshold 1: 0.184 / 0.280, 5: 0.140 / 0.222,
+// 9: 0.127 / 0.205, 17: 0.148 / 0.215, 48: 0.266 / 0.372.
+constexpr int GEMM_MIN_TOKENS = 9;   // isolated expert op
 constexpr int PROJ_GEMM_MIN_ROWS = 17;      // prompt rows from which a step's projections run them
                                             // on the tensor-core GEMM (the GEMV holds 16 per pass)
 // Decode step: prompt-row routes from which an expert's prompt routes take the GEMM (fewer
