@@ -188,8 +188,8 @@ int z2b_time_expert_gemv(z2b_ctx* ctx, int which, int reps, double* ms_per_launc
  * expert ids, selw[T][k] route weights -> out[T][n_embd] (out may be NULL). With reps > 0
  * the two expert passes run reps more times between CUDA events and *ms is the time per
  * repetition. *weight_bytes = routed experts' weight bytes; *n_gemm_experts = experts
- * that took the tensor-core GEMM (those with >= 9 routes, or the threshold set by
- * z2b_set_expert_gemm_min). T <= the context's rows per step.
+ * that took the tensor-core GEMM (from T = 64, those with >= 9 routes; or the threshold
+ * set by z2b_set_expert_gemm_min at any T). T <= the context's rows per step.
  * No reference counterpart (the reference's expert op is ggml_mul_mat_id inside its graph). */
 int z2b_expert_op(z2b_ctx* ctx, int layer, const float* x, int T, const int32_t* sel, const float* selw, int k,
                   float* out, int reps, double* ms, uint64_t* weight_bytes, int32_t* n_gemm_experts);

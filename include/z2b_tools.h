@@ -99,8 +99,9 @@ int z2b_route_segments_noalloc(const int32_t* sel, const float* selw, int T, int
                                int32_t* route_tok, int32_t* route_pos);
 
 /* No reference counterpart. Tuning of z2b_expert_op (z2b.h): an expert with at least
- * `routes` routes takes the tcgen05 grouped GEMM, one with fewer the tile GEMV (default 9;
- * 1 sends every expert to the GEMM, a value above the op's route count none). Used to
+ * `routes` routes takes the tcgen05 grouped GEMM, one with fewer the tile GEMV (default 9,
+ * applied from T = 64 rows; once set, at any T: 1 sends every expert to the GEMM, a value
+ * above the op's route count none). Used to
  * measure the GEMV / GEMM crossover; the decode step keeps its own rule. Z2B_ERR_ARG for
  * routes < 1. */
 struct z2b_ctx;

@@ -2,7 +2,7 @@
 gate/up, F16 down, top-4 routing skewed by a Zipf(1.1) bias) through z2b_expert_op,
 against a float32 numpy restatement over gguf-py's dequantised weights, at every token
 count of the config-4 sweep (T = 16, 64, 256, 1024, 4096) plus 320. The experts with >= 9
-routes take the tcgen05 GEMM, the others the tile GEMV;
+routes take the tcgen05 GEMM from T = 64 (T = 16 runs on the tile GEMV only);
 at 1024 and 4096 the most-loaded experts span several token tiles, the last one partial."""
 from __future__ import annotations
 
@@ -70,7 +70,8 @@ def test_expert_op_vs_float32(model_dir, T):
     finally:
         m.close()
     counts = np.bincount(sel.ravel(), minlength=m.hp.n_expert)
-    assert n_gemm == int((counts >= GEMM_MIN).sum())   # the loaded experts took the tensor-core path
+    expected = int((counts >= GEMM_MIN).sum()) if T >= 64 else 0   # the op launches the GEMM from 64 rows
+    assert n_gemm == expected                  # the loaded experts took the tensor-core path
     if T >= 64:
         assert n_gemm > 0
     ref = reference(path, x, sel, w)

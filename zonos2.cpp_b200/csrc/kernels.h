@@ -17,6 +17,10 @@ constexpr int MAX_EXPERTS = 256;
 // skewed config-4 op (ms at T = 64 / 256): threshold 1: 0.184 / 0.280, 5: 0.140 / 0.222,
 // 9: 0.127 / 0.205, 17: 0.148 / 0.215, 48: 0.266 / 0.372.
 constexpr int GEMM_MIN_TOKENS = 9;   // isolated expert op
+// ... and only from 64 rows: a GEMM launch costs a wave of decode-bound tiles (~70 us),
+// which the GEMV's passes undercut when the op carries few routes (T = 16: 0.045 ms on the
+// GEMV alone, 0.112 ms when the experts with >= 9 routes launch the GEMM).
+constexpr int GEMM_OP_MIN_ROWS = 64;
 constexpr int PROJ_GEMM_MIN_ROWS = 17;      // prompt rows from which a step's projections run them
                                             // on the tensor-core GEMM (the GEMV holds 16 per pass)
 // Decode step: prompt-row routes from which an expert's prompt routes take the GEMM (fewer

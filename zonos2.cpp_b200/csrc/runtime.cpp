@@ -975,6 +975,7 @@ namespace z2b {
 int ctx_set_expert_gemm_min(Ctx* c, int routes) {
     if (routes < 1) { set_error("expert GEMM threshold must be >= 1 route"); return Z2B_ERR_ARG; }
     c->expert_gemm_min = routes;
+    c->expert_gemm_set = true;
     return Z2B_OK;
 }
 
@@ -997,7 +998,8 @@ int ctx_expert_op(Ctx* c, int layer, const float* x, int T, const int32_t* sel, 
     CK(cudaMemcpyAsync(B.sel, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(B.selw, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice, c->stream));
     launch_to_f16(B.res, B.cur, (size_t)T * d, c->stream);
-    const bool bulk = T >= c->expert_gemm_min && ly.small.gemm_ok;   // some expert can reach the threshold
+    // some expert can reach the threshold, and (unless set explicitly) the op is large enough
+    const bool bulk = T >= c->expert_gemm_min && ly.small.gemm_ok && (c->expert_gemm_set || T >= GEMM_OP_MIN_ROWS);
     launch_segments(B, T, k, ly.n_expert, bulk ? 1 : 0, c->stream, c->expert_gemm_min);
     const bool prof = c->profiling;
     c->profiling = false;

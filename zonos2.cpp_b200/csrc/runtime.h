@@ -68,7 +68,8 @@ struct Ctx {
     int prompt_graphs = 0;
     bool enq_failed = false;
     int cur_T = 0;                           // rows of the step (or expert op) being enqueued
-    int expert_gemm_min = GEMM_MIN_TOKENS;   // expert op: routes from which an expert takes the GEMM                 // a launch could not be set up while enqueuing (error set)
+    int expert_gemm_min = GEMM_MIN_TOKENS;   // expert op: routes from which an expert takes the GEMM
+    bool expert_gemm_set = false;            // set explicitly: the op's minimum rows no longer apply                 // a launch could not be set up while enqueuing (error set)
     int launches = 0, loop_launches = 0;
     // decode-loop uniforms
     double* d_canon_all = nullptr;
