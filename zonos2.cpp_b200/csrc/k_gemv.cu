@@ -188,9 +188,49 @@ __global__ void __launch_bounds__(MAXT, MINB) gemv_kernel(const GemvParams p) {
         pdl_wait();
     } else {
         pdl_wait();
-        const int n_items = (*p.n_active) * p.n_row_tiles;
+        const int n_act = *p.n_active;
+        const int n_items = n_act * p.n_row_tiles;
         it0 = (int)((int64_t)blockIdx.x * n_items / gridDim.x);
         it1 = (int)((int64_t)(blockIdx.x + 1) * n_items / gridDim.x);
+        if (p.tile_off && n_act <= 32) {
+            // Balanced split: an item of expert a costs W + (its 8-token tiles), fitted to
+            // measured per-block times (an expert past 8 tokens takes a second 8-token pass in
+            // the down GEMV, twice the n-tiles in gate/up); blocks take equal cost ranges, so
+            // the blocks on heavily routed experts get fewer items. Warp 0 scans the experts'
+            // tile prefix (tile_off, from the router) and finds this block's first and last
+            // item; the result only moves items between blocks, never changes one.
+            __shared__ int s_it[2];
+            if (warp == 0) {
+                constexpr int W = (MODE == GM_GATEUP) ? 2 : 1;
+                const int nrt = p.n_row_tiles;
+                const int t_lo = lane <= n_act ? p.tile_off[lane] : 0;
+                int t_hi = __shfl_down_sync(0xffffffffu, t_lo, 1);
+                if (lane == 31 && n_act == 32) t_hi = p.tile_off[32];
+                const int unit = lane < n_act ? W + t_hi - t_lo : 0;   // < 2^16 (tiles of <= 2^19 routes)
+                const int span = unit * nrt;
+                int inc = span;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += v;
+                }
+                const int total = __shfl_sync(0xffffffffu, inc, 31), base = inc - span;
+#pragma unroll
+                for (int which = 0; which < 2; ++which) {
+                    const int c = (int)((long long)(blockIdx.x + which) * total / gridDim.x);
+                    const bool mine = lane < n_act && c >= base && c < base + span;
+                    const unsigned m = __ballot_sync(0xffffffffu, mine);
+                    if (m == 0u) {
+                        if (lane == 0) s_it[which] = n_items;
+                    } else if (lane == __ffs(m) - 1) {
+                        s_it[which] = lane * nrt + (int)((c - base) / unit);
+                    }
+                }
+            }
+            __syncthreads();
+            it0 = s_it[0];
+            it1 = s_it[1];
+        }
         issued_upto = it0 - 1;
         ipos = item_seek<MODE>(p, it0);
         for (int i = 0; i < NS && it0 + i < it1; ++i) issue(it0 + i, i);
