@@ -488,6 +488,76 @@ def config5(args, rank, world, local):
         dist.destroy_process_group()
 
 
+DAC_STREAMS, DAC_BLOCK, DAC_CTX = 16, 40, 24
+
+
+def dac_bench(args):
+    """DAC decode (codes -> waveform) of the streaming server's cadence: 16 streams, each
+    emitting one block of 40 frames decoded with 24 frames of conv context on either side
+    (src/server.cpp:105-106, 976-989), all 16 windows in one z2b_dac_decode_windows call on a
+    synthetic decoder with the real DAC 44 kHz shapes (latent 1024, decoder 1536, rates
+    8/8/4/2). value = kept output frames per second (x 512 samples; 86.1 frames = 1 s of
+    audio). Timed with CUDA events on the decoder's stream around each call (codes H2D and PCM
+    D2H inside); the roofline is the convolutions' algorithmic FLOPs (88 latent frames per
+    window) over the whole call against the measured bf16 dense peak."""
+    import torch
+    load_pkg()
+    import z2b.dac as D
+    import z2b.synth as S
+    path = S.cached_dac("dac44k", 0, model_dir())
+    dac = D.Dac(path)
+    g = np.random.default_rng(9)
+    H = DAC_BLOCK + 2 * DAC_CTX + 200
+    streams = [g.integers(0, 1024, (H, 9)).astype(np.int32) for _ in range(DAC_STREAMS)]
+    f_lo = 100
+    wins = [(c, f_lo, f_lo + DAC_BLOCK, DAC_CTX, DAC_CTX) for c in streams]
+    for _ in range(max(args.warmup, 3)):
+        dac.decode_windows(wins)
+    stream = torch.cuda.ExternalStream(dac.stream())
+    clk = ClockSampler(0)
+    clk.start()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = dac.decode_windows(wins)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    frames = DAC_STREAMS * DAC_BLOCK
+    flops = DAC_STREAMS * dac.conv_flops(DAC_BLOCK + 2 * DAC_CTX)
+    peaks_f = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    tpk = json.load(open(peaks_f)).get("bf16_tflops", 1590.0) if os.path.exists(peaks_f) else 1590.0
+    achieved = flops / (ms * 1e-3) / 1e12
+    line = {"metric": "DAC decode output frames/s (16 streaming windows per call)",
+            "value": frames / (ms * 1e-3), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 (tcgen05 kind::f16, f32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"DAC 44 kHz decoder shapes, {DAC_STREAMS} windows of {DAC_BLOCK} frames "
+                                   f"+ {DAC_CTX} context each side, one call",
+                       "audio_seconds_per_step": frames * 512 / 44100},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tpk, "unit": "TFLOP/s",
+                         "frac": achieved / tpk, "flops_per_step": flops,
+                         "timing": "whole call (all kernels and both copies) per step: a lower bound on the "
+                                   "convolution kernels' own rate"},
+            "e2e": {"value": frames / (ms * 1e-3), "unit": "frames/s",
+                    "h2d_bytes_per_step": DAC_STREAMS * (DAC_BLOCK + 2 * DAC_CTX + 8) * 9 * 4,
+                    "d2h_bytes_per_step": sum(x.nbytes for x in out)},
+            "gpu_launches": dac.last_launches() * args.steps, "clocks": clocks}
+    if args.cpu_seconds > 0:
+        from oracle.dac_oracle import DacOracle
+        o = DacOracle(path)
+        t = time.perf_counter()
+        o.decode_window(*wins[0])
+        dt = time.perf_counter() - t
+        line["cpu_baseline"] = {"value": DAC_BLOCK / dt, "unit": "frames/s", "cores": os.cpu_count(),
+                                "kind": "port", "sample": "one window of the same workload (88 latent frames, "
+                                                          "40 kept) through the CPU oracle"}
+    print(json.dumps(line), flush=True)
+    dac.close()
+
+
 def workload_name():
     return (f"config2: ZONOS2-scale Q4_K backbone, {STREAMS} streams/GPU, ctx U[{CTX_RANGE[0]},{CTX_RANGE[1]}], "
             f"{STEPS_PER_STREAM} frames per stream, continuous refill with {REFILL_PROMPT}-row prompts")
@@ -529,6 +599,8 @@ def main():
                     help="config 4's GEMV / GEMM crossover: n routes per expert on either path, one JSON line per n")
     ap.add_argument("--config3", action="store_true",
                     help="config 3: Q6_K and Q8_0 backbones, 60 decode + 4 prompt streams per step, one JSON line each")
+    ap.add_argument("--dac", action="store_true",
+                    help="DAC decode of 16 streaming windows per call (codes -> PCM on the GPU)")
     ap.add_argument("--config5", action="store_true",
                     help="config 5: whole-box serving of Poisson arrivals through the replica dispatcher")
     args = ap.parse_args()
@@ -539,6 +611,8 @@ def main():
         return config3(args)
     if args.crossover:
         return crossover(args)
+    if args.dac:
+        return dac_bench(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

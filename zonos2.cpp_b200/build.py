@@ -1,7 +1,8 @@
 """Build recipe for the in-tree shared libraries (nvcc / g++, no torch extension machinery).
 
 libz2b.so        the decode-step library: GGUF loader, tile repack, sm_100a kernels,
-                 batch runtime and the C ABI declared in include/z2b.h.
+                 batch runtime and the C ABI declared in include/z2b.h; the DAC decoder
+                 (include/z2b_dac.h).
 libz2b_synth.so  host-only synthetic GGUF writer (include/z2b_tools.h).
 
 Objects go to zonos2.cpp_b200/_build/ and are rebuilt when a source or header is newer.
@@ -25,8 +26,8 @@ LIB = os.path.join(PKG, "libz2b.so")
 SYNTH_LIB = os.path.join(PKG, "libz2b_synth.so")
 
 HOST_COMMON = ["gguf.cpp", "quant.cpp"]
-Z2B_HOST = ["repack.cpp", "model.cpp", "runtime.cpp", "capi.cpp"]
-Z2B_CUDA = ["k_gemv.cu", "k_gemm.cu", "k_attn.cu", "k_router.cu", "k_misc.cu", "k_test.cu"]
+Z2B_HOST = ["repack.cpp", "model.cpp", "runtime.cpp", "capi.cpp", "dac.cpp", "capi_dac.cpp"]
+Z2B_CUDA = ["k_gemv.cu", "k_gemm.cu", "k_attn.cu", "k_router.cu", "k_misc.cu", "k_test.cu", "k_dac.cu"]
 
 
 def _headers():

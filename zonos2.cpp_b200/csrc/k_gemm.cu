@@ -38,9 +38,8 @@
 #include "launch.cuh"
 #include "tile_layout.h"
 #include "k_decode.cuh"
+#include "tc05.cuh"
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
 #include <algorithm>
 
 namespace z2b {
@@ -67,29 +66,12 @@ constexpr int A_SLOT = (int)A_LBO * (KG / 8);    // 16.1 KB
 // atoms of 1024 B.
 constexpr int B_SLOT = NT_MAX * KG * 2;          // 32 KB
 
-// instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both K-major, N, M 128
-__device__ __forceinline__ uint32_t idesc_n(int n) {
-    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GT_M >> 4) << 24);
-}
+// instruction descriptor: M 128 (weight rows) x N (activation rows)
+__device__ __forceinline__ uint32_t idesc_n(int n) { return idesc_f16(GT_M, n); }
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(CORE_SBO >> 4) << 32) |
            (1ull << 46);
-}
-
-// K-major, 128-byte swizzle: leading offset unused (1), 1024 B between 8-row atoms; the
-// K16 slices of a 64-wide stage start 32 B apart inside the 128-byte rows.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
-}
-
-// One tiled TMA load (this CTA only) of a 2-D box completing on `bar`; x is a multiple of 64
-// elements (128 bytes).
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
 }
 
 // Activation rows copied to Xp (row stride K) in stage order: within each KC-wide chunk,
@@ -116,49 +98,6 @@ __global__ void gemm_x_stage_order_kernel(const __half* __restrict__ X, int ldx,
             *reinterpret_cast<const uint4*>(X + (size_t)src_row * ldx + ks);
     }
     pdl_release();
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-        :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate) : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 :: "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Bounded wait that also gives up as soon as another role of the block has given up.
-__device__ __forceinline__ bool wait_ab(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* ab) {
-    for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*ab) return false;
-    }
-    if (err) atomicOr(err, (uint32_t)DERR_WAIT_TIMEOUT);
-    *ab = 1;
-    return false;
 }
 
 __device__ __forceinline__ void st16(uint8_t* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -546,19 +485,6 @@ int gemm_raw_slots(int tile_bytes) {
     return std::min(MAX_RR, budget / (DQW * tile_bytes));
 }
 
-// cuTensorMapEncodeTiled from the driver, looked up once.
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }();
-    return fn;
-}
-
 // The stage-ordered activations Xp[x_rows][K]: box {64, gm_nt + 8} at (chunk*KC + 64j, row)
 // is one GEMM stage of a tile's rows (its routes start at most 7 rows in), written with the
 // 128-byte swizzle (rows past x_rows read as zeros).
@@ -602,6 +528,19 @@ bool gemm_typed(const GemvParams& p, int grid, cudaStream_t s) {
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled from the driver, looked up once.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (PFN_cuTensorMapEncodeTiled_v12000) nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
 
 bool moe_gemm_supported(const DevMat& m) {
     switch (m.type) {

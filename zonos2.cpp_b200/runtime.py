@@ -106,6 +106,15 @@ def lib():
             "z2b_debug_router_capture": ([P, I], I),
             "z2b_debug_router_inputs": ([P, I, V, V, ctypes.POINTER(ctypes.c_int)], I),
             "z2b_debug_last_sel": ([P, V, I], I),
+            "z2b_dac_load": ([ctypes.c_char_p, I, ctypes.POINTER(P)], I),
+            "z2b_dac_free": ([P], I),
+            "z2b_dac_get_hparams": ([P, V], I),
+            "z2b_dac_decode": ([P, V, I, I, I, V, ctypes.c_int64, V], I),
+            "z2b_dac_decode_window": ([P, V, I, I, I, I, I, V, ctypes.c_int64, V], I),
+            "z2b_dac_decode_windows": ([P, V, I, V, ctypes.c_int64, V], I),
+            "z2b_dac_last_launches": ([P], ctypes.c_long),
+            "z2b_dac_stream": ([P], P),
+            "z2b_dac_wav_bytes": ([V, ctypes.c_int64, I, V, ctypes.c_int64], ctypes.c_int64),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)

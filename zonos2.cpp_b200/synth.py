@@ -120,3 +120,86 @@ def cached(preset: str = "tiny", directory: str | None = None, **overrides) -> s
         write(tmp, preset, **overrides)
         os.replace(tmp, path)
     return path
+
+
+# ---------------------------------------------------------------- DAC decoder files
+
+DAC_PRESETS = {
+    # the real decoder's shapes (DAC 44 kHz: latent 1024, decoder 1536, rates 8/8/4/2, hop 512)
+    "dac44k": dict(latent=1024, decoder_dim=1536, rates=(8, 8, 4, 2)),
+    # small shapes for parity tests: every kernel path (channel padding, four blocks, all rates)
+    "dac_small": dict(latent=64, decoder_dim=256, rates=(8, 8, 4, 2)),
+    "dac_tiny": dict(latent=8, decoder_dim=16, rates=(2, 2)),
+}
+
+
+def write_dac(path: str, preset: str = "dac_small", seed: int = 0, n_codebooks: int = 9,
+              codebook_size: int = 1024, sample_rate: int = 44100) -> str:
+    """Write a synthetic DAC decoder GGUF with the tensor names, shapes and f32 storage of the
+    reference's converter (models/convert-dac-to-gguf.py): folded quantizer tables, conv_in,
+    the decoder blocks (snake, transposed conv, three residual units), snake_out, conv_out.
+    Random weights scaled so activations stay O(1) through the residual stack and the
+    pre-tanh output spans tanh's linear and saturated ranges."""
+    import numpy as np
+    from gguf import GGUFWriter
+
+    p = DAC_PRESETS[preset]
+    lat, dd, rates = p["latent"], p["decoder_dim"], list(p["rates"])
+    rng = np.random.default_rng(seed)
+    w = GGUFWriter(path, "dac")
+    w.add_string("general.name", f"DAC-synthetic-{preset}")
+    for k, v in (("n_codebooks", n_codebooks), ("codebook_size", codebook_size), ("latent_dim", lat),
+                 ("decoder_dim", dd), ("sample_rate", sample_rate), ("hop_length", int(np.prod(rates))),
+                 ("audio_pad_id", codebook_size + 1)):
+        w.add_uint32(f"dac.{k}", v)
+    w.add_array("dac.decoder_rates", rates)
+
+    def put(name, a):
+        w.add_tensor(name, np.ascontiguousarray(a, dtype=np.float32))
+
+    def normal(shape, std):
+        return (rng.standard_normal(shape) * std).astype(np.float32)
+
+    def conv(name, oc, ic, k, gain=1.0):
+        put(name + ".weight", normal((oc, ic, k), gain / np.sqrt(ic * k)))
+        put(name + ".bias", normal((oc, 1), 0.1))
+
+    def snake(name, c):
+        a = rng.uniform(0.5, 1.5, (c, 1)).astype(np.float32)
+        put(name + ".alpha", a)
+        put(name + ".inv_alpha", (1.0 / (a + 1e-9)).astype(np.float32))
+
+    for i in range(n_codebooks):
+        put(f"quant.{i}.table", normal((codebook_size, lat), 1.0 / np.sqrt(n_codebooks)))
+    put("quant.bias", normal((lat,), 0.1))
+    conv("dec.conv_in", dd, lat, 7)
+    for b, s in enumerate(rates):
+        ci, co = dd >> b, dd >> (b + 1)
+        snake(f"dec.b{b}.snake", ci)
+        put(f"dec.b{b}.convt.weight", normal((ci, co, 2 * s), 1.0 / np.sqrt(2 * ci)))
+        put(f"dec.b{b}.convt.bias", normal((co, 1), 0.1))
+        for r in range(3):
+            snake(f"dec.b{b}.res{r}.snake1", co)
+            conv(f"dec.b{b}.res{r}.conv1", co, co, 7)
+            snake(f"dec.b{b}.res{r}.snake2", co)
+            conv(f"dec.b{b}.res{r}.conv2", co, co, 1, gain=0.5)
+    cf = dd >> len(rates)
+    snake("dec.snake_out", cf)
+    conv("dec.conv_out", 1, cf, 7, gain=0.3)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file(progress=False)
+    w.close()
+    return path
+
+
+def cached_dac(preset: str = "dac_small", seed: int = 0, directory: str | None = None) -> str:
+    """Path of a synthetic DAC GGUF for (preset, seed), generating it once per directory."""
+    directory = directory or os.environ.get("Z2B_MODEL_DIR", "/tmp/z2b_models")
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{preset}_seed-{seed}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_dac(tmp, preset, seed)
+        os.replace(tmp, path)
+    return path
