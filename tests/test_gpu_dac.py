@@ -82,13 +82,16 @@ def test_windows_batch_exact_and_match_oracle(dacs, paths):
 
 
 def test_window_equals_full_decode_slice(dacs):
-    """With context at least the decoder's receptive field the window's samples equal the
-    full decode's (src/dac.h:37-44); on the GPU bit for bit."""
+    """With context at least the decoder's receptive field, and the right context inside the
+    generated codes, the window's samples equal the full decode's (src/dac.h:37-44); on the
+    GPU bit for bit. (Context frames at or past H read as pad codes, where the full decode
+    ends, so a window whose right context runs past H differs near its end, as in the
+    reference; such a window is checked against the oracle above.)"""
     d = dacs["dac_small"]
     codes = _codes(96, 3)
     full = d.decode(codes)
     spf = d.spf
-    for f_lo, f_hi in ((20, 60), (0, 16), (70, 96)):
+    for f_lo, f_hi in ((20, 60), (0, 16), (56, 72)):
         win = d.decode_window(codes, f_lo, f_hi, 24, 24)
         seg = full[f_lo * spf:f_hi * spf]
         diff = np.abs(win - seg).max()
