@@ -17,7 +17,7 @@
 // the weights' [128 x 64] box and the activations' [64 x 128] box at row offset k*dil - pad
 // (rows before the window or past its allocation read as zeros, the convolution's zero
 // padding). Roles, handing over through mbarriers: warp 0 lane 0 issues the TMA loads, warp
-// 1 lane 0 the tcgen05.mma (accumulator in TMEM), warps 2-5 the epilogue: bias, residual
+// 1 lane 0 the tcgen05.mma (accumulator in TMEM), warps 2-9 the epilogue: bias, residual
 // add, the next snake, f32 residual stream and f16 conv input written time-major.
 //
 // Numerics follow the reference's CPU graph: conv inputs and weights in f16 (its im2col
@@ -43,9 +43,10 @@ constexpr int BK = 64;                      // input channels per stage
 constexpr int NS = 3;                       // stages in flight (two blocks per SM)
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
-constexpr int CONV_THREADS = 192;           // TMA warp, MMA warp, 4 epilogue warps
+constexpr int EPI_WARPS = 8;                // two per TMEM lane quarter, alternating column chunks
+constexpr int CONV_THREADS = 32 * (2 + EPI_WARPS);   // TMA warp, MMA warp, epilogue warps
 constexpr int CONV_SMEM = 1024 + NS * (A_BYTES + B_BYTES);
-constexpr uint32_t TMEM_COLS = BN;
+constexpr uint32_t TMEM_COLS = 2 * BN;       // two accumulator buffers
 constexpr int MAX_CB = 16;                  // codebooks
 constexpr int OUT_TILE = 64;                // samples per conv_out block
 constexpr int MAX_CFIN = 128;               // conv_out input channels (static shared-memory tile)
@@ -61,8 +62,21 @@ struct ConvK {
     uint32_t* err;
     int oc, oc_pad, cin_chunks, ic_pad, taps, dil, pad;
     int m_rows, n_tiles, ostride, ooff, lout, c_out_st;
+    int n_win, n_tiles_total;
 };
 
+// Tile t of a launch: output-channel tile fastest (the CTAs working on one activation tile
+// at the same time share it through L2), then (window, row tile), then phase.
+struct ConvTile { int m0, win, n0, phase; };
+__device__ __forceinline__ ConvTile conv_tile(const ConvK& p, int t) {
+    const int mtc = p.oc_pad / BM, wt = p.n_win * p.n_tiles;
+    const int mt = t % mtc, rest = t / mtc, y = rest % wt;
+    return ConvTile{mt * BM, y / p.n_tiles, (y % p.n_tiles) * BN, rest / wt};
+}
+
+// Persistent: each CTA walks tiles blockIdx.x, + gridDim.x, ...; the accumulator is double
+// buffered in TMEM (columns [0, 128) and [128, 256)), so the epilogue of one tile overlaps
+// the main loop of the next.
 __global__ void __launch_bounds__(CONV_THREADS, 2)
 dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -70,13 +84,12 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* As = smem;
     uint8_t* Bs = smem + NS * A_BYTES;
-    __shared__ __align__(8) uint64_t full[NS], empty[NS], acc_full, fin_bar;
+    __shared__ __align__(8) uint64_t full[NS], empty[NS], acc_full[2], acc_empty[2], fin_bar;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
     volatile int* ab = &abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int win = blockIdx.y / p.n_tiles, nt = blockIdx.y % p.n_tiles, phase = blockIdx.z;
-    const int m0 = blockIdx.x * BM, n0 = nt * BN;
+    const int n_total = p.n_tiles_total;
 
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -85,7 +98,7 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
     }
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        mbar_init(&acc_full, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], EPI_WARPS); }
         mbar_init(&fin_bar, 1);
         abort_flag = 0;
     }
@@ -102,15 +115,19 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
         // ---- TMA producer ----
         if (lane == 0) {
             int issued = 0;
-            for (int s = 0; s < n_stages && ok; ++s) {
-                const int slot = s % NS;
-                ok = wait_ab(&empty[slot], (uint32_t)(((s / NS) & 1) ^ 1), p.err, ab);
-                if (!ok) break;
-                const int k = s / p.cin_chunks, c = s % p.cin_chunks;
-                mbar_expect_tx(&full[slot], (uint32_t)(A_BYTES + B_BYTES));
-                tma_load_2d(As + slot * A_BYTES, &wmap, k * p.ic_pad + c * BK, phase * p.oc_pad + m0, &full[slot]);
-                tma_load_3d(Bs + slot * B_BYTES, &xmap, c * BK, n0 + k * p.dil - p.pad, win, &full[slot]);
-                ++issued;
+            for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x) {
+                const ConvTile ti = conv_tile(p, t);
+                for (int s = 0; s < n_stages && ok; ++s) {
+                    const int slot = issued % NS;
+                    ok = wait_ab(&empty[slot], (uint32_t)(((issued / NS) & 1) ^ 1), p.err, ab);
+                    if (!ok) break;
+                    const int k = s / p.cin_chunks, c = s % p.cin_chunks;
+                    mbar_expect_tx(&full[slot], (uint32_t)(A_BYTES + B_BYTES));
+                    tma_load_2d(As + slot * A_BYTES, &wmap, k * p.ic_pad + c * BK, ti.phase * p.oc_pad + ti.m0,
+                                &full[slot]);
+                    tma_load_3d(Bs + slot * B_BYTES, &xmap, c * BK, ti.n0 + k * p.dil - p.pad, ti.win, &full[slot]);
+                    ++issued;
+                }
             }
             if (!ok) {
                 *ab = 1;
@@ -124,57 +141,84 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
         // ---- MMA issuer ----
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(BM, BN);
-            for (int s = 0; s < n_stages && ok; ++s) {
-                const int slot = s % NS;
-                ok = wait_ab(&full[slot], (uint32_t)((s / NS) & 1), p.err, ab);
+            int consumed = 0, it = 0;
+            for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x, ++it) {
+                const int buf = it & 1;
+                // the epilogue has read this buffer's previous tile
+                ok = wait_ab(&acc_empty[buf], (uint32_t)(((it >> 1) & 1) ^ 1), p.err, ab);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t sa = smem_u32(As + slot * A_BYTES), sb = smem_u32(Bs + slot * B_BYTES);
+                const uint32_t acc = tm + (uint32_t)(buf * BN);
+                for (int s = 0; s < n_stages && ok; ++s) {
+                    const int slot = consumed % NS;
+                    ok = wait_ab(&full[slot], (uint32_t)((consumed / NS) & 1), p.err, ab);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(As + slot * A_BYTES), sb = smem_u32(Bs + slot * B_BYTES);
 #pragma unroll
-                for (int kb = 0; kb < BK / 16; ++kb)
-                    umma_f16(tm, umma_desc_sw128(sa + 32 * kb), umma_desc_sw128(sb + 32 * kb), idesc,
-                             (s > 0 || kb > 0) ? 1u : 0u);
-                umma_commit(&empty[slot]);               // the slot refills once these MMAs complete
+                    for (int kb = 0; kb < BK / 16; ++kb)
+                        umma_f16(acc, umma_desc_sw128(sa + 32 * kb), umma_desc_sw128(sb + 32 * kb), idesc,
+                                 (s > 0 || kb > 0) ? 1u : 0u);
+                    umma_commit(&empty[slot]);           // the slot refills once these MMAs complete
+                    ++consumed;
+                }
+                if (ok) umma_commit(&acc_full[buf]);
             }
-            if (ok) umma_commit(&acc_full);
-            else *ab = 1;
+            if (!ok) *ab = 1;
             // every MMA issued completes before the block releases its memory
             umma_commit(&fin_bar);
             (void)mbar_wait(&fin_bar, 0, nullptr, 1u << 16);
         }
         __syncwarp();
     } else {
-        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = its 32 output channels ----
-        const bool w = wait_ab(&acc_full, 0, p.err, ab);
-        if (__all_sync(0xffffffffu, w)) {
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = its 32 output channels, the
+        // two warps of a lane quarter alternating 16-column chunks ----
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        int it = 0;
+        for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x, ++it) {
+            const int buf = it & 1;
+            const bool w = wait_ab(&acc_full[buf], (uint32_t)((it >> 1) & 1), p.err, ab);
+            ok = __all_sync(0xffffffffu, w);
+            if (!ok) break;
             tc_fence_after();
-            const int q = warp & 3;
-            const int oc = m0 + 32 * q + lane;
+            const ConvTile ti = conv_tile(p, t);
+            const int oc = ti.m0 + 32 * q + lane, n0 = ti.n0, phase = ti.phase;
             const bool ch_ok = oc < p.oc;
             const float bias = ch_ok ? p.bias[oc] : 0.0f;
             const float al = (p.alpha && ch_ok) ? p.alpha[oc] : 0.0f;
             const float iv = (p.inv && ch_ok) ? p.inv[oc] : 0.0f;
-            const int lw = p.lw_out[win];
-            const uint32_t taddr = tm + ((uint32_t)(32 * q) << 16);
-            const size_t wbase = (size_t)win * p.lout;
+            const int lw = p.lw_out[ti.win];
+            const uint32_t taddr = tm + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
+            const size_t wbase = (size_t)ti.win * p.lout;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 16; ++cc) {
+            for (int cc = half; cc < BN / 16; cc += 2) {
                 if (n0 + cc * 16 >= p.m_rows) break;     // warp-uniform
-                float v[16];
+                float v[16], r[16];
                 tmem_ld16(taddr + cc * 16, v);
+                // the residual may alias xout: read the chunk's 16 values before its stores, so
+                // the loads issue together instead of each waiting behind the previous store
+                if (p.xres) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int m = n0 + cc * 16 + i;
+                        const int tt = m * p.ostride + phase - p.ooff;
+                        const bool in = ch_ok && m < p.m_rows && tt >= 0 && tt < p.lout && tt < lw;
+                        r[i] = in ? p.xres[(wbase + tt) * p.c_out_st + oc] : 0.0f;
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int m = n0 + cc * 16 + i;
-                    const int t = m * p.ostride + phase - p.ooff;
-                    if (m >= p.m_rows || t < 0 || t >= p.lout) continue;
-                    const size_t idx = (wbase + t) * p.c_out_st + oc;
-                    if (!ch_ok || t >= lw) {
+                    const int tt = m * p.ostride + phase - p.ooff;
+                    if (m >= p.m_rows || tt < 0 || tt >= p.lout) continue;
+                    const size_t idx = (wbase + tt) * p.c_out_st + oc;
+                    if (!ch_ok || tt >= lw) {
                         if (p.xout) p.xout[idx] = 0.0f;
                         p.sout[idx] = __float2half_rn(0.0f);
                         continue;
                     }
                     float x = v[i] + bias;
-                    if (p.xres) x = p.xres[idx] + x;
+                    if (p.xres) x = r[i] + x;
                     if (p.xout) p.xout[idx] = x;
                     float y = x;
                     if (p.alpha) {
@@ -185,7 +229,11 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
                     p.sout[idx] = __float2half_rn(y);
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);   // the MMA warp may reuse this buffer
         }
+        if (!ok) *ab = 1;
     }
     tc_fence_before();
     __syncthreads();
@@ -269,6 +317,7 @@ __global__ void dac_out_kernel(const __half* __restrict__ in, int lin, int c_st,
 }
 
 bool conv_attr_done[64] = {};
+int conv_sms[64] = {};
 
 }  // namespace
 
@@ -314,7 +363,10 @@ bool launch_dac_conv(const DacConv& c, const DacConvIO& io, cudaStream_t s) {
     p.c_out_st = io.c_out_st;
     p.n_tiles = (p.m_rows + BN - 1) / BN;
     if (convt ? (io.lout != io.lin * c.stride || c.taps != 2) : io.lout != io.lin) return false;
-    if ((long)io.n_win * p.n_tiles > 65535) return false;
+    p.n_win = io.n_win;
+    const long total = (long)(c.oc_pad / BM) * io.n_win * p.n_tiles * c.phases;
+    if (total > 0x7fffffffL) return false;
+    p.n_tiles_total = (int)total;
     alignas(64) CUtensorMap xmap;
     const cuuint64_t dims[3] = {(cuuint64_t)c.ic_pad, (cuuint64_t)io.lin, (cuuint64_t)io.n_win};
     const cuuint64_t strides[2] = {(cuuint64_t)io.c_in_st * 2, (cuuint64_t)io.lin * io.c_in_st * 2};
@@ -328,12 +380,14 @@ bool launch_dac_conv(const DacConv& c, const DacConvIO& io, cudaStream_t s) {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return false;
     if (!conv_attr_done[dev]) {                       // the shared-memory opt-in is per device
-        if (cudaFuncSetAttribute(dac_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CONV_SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(dac_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CONV_SMEM) != cudaSuccess ||
+            cudaDeviceGetAttribute(&conv_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return false;
         conv_attr_done[dev] = true;
     }
-    const dim3 grid(c.oc_pad / BM, io.n_win * p.n_tiles, c.phases);
-    return launch_pdl(dac_conv_kernel, grid, dim3(CONV_THREADS), (size_t)CONV_SMEM, s, p,
+    // two persistent blocks per SM (TMEM: 2 x 256 columns; shared memory: 2 x 97 KB)
+    const int grid = (int)std::min<long>(total, 2L * conv_sms[dev]);
+    return launch_pdl(dac_conv_kernel, dim3(grid), dim3(CONV_THREADS), (size_t)CONV_SMEM, s, p,
                       *reinterpret_cast<const CUtensorMap*>(c.wmap), xmap) == cudaSuccess;
 }
 
