@@ -22,8 +22,9 @@
 //
 // Numerics follow the reference's CPU graph: conv inputs and weights in f16 (its im2col
 // patches are f16 and ggml's f16 dot converts the f32 weights to f16), products summed in
-// f32; bias, residual, snake and tanh in f32. The transposed convs, f32 x f32 in the
-// reference, take f16 operands here too.
+// f32; bias, residual, snake and tanh in f32, the snake's sine from the hardware
+// approximation (its error is far below the f16 rounding of the snake's output). The
+// transposed convs, f32 x f32 in the reference, take f16 operands here too.
 #include "common.cuh"
 #include "dac.h"
 #include "launch.cuh"
@@ -195,23 +196,25 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
                 if (n0 + cc * 16 >= p.m_rows) break;     // warp-uniform
                 float v[16], r[16];
                 tmem_ld16(taddr + cc * 16, v);
+                // column i of the chunk: GEMM row m0c + i, output row tt0 + i * ostride
+                const int m0c = n0 + cc * 16, tt0 = m0c * p.ostride + phase - p.ooff;
+                const long long base = ((long long)wbase + tt0) * p.c_out_st + oc;
+                const long long step = (long long)p.ostride * p.c_out_st;
                 // the residual may alias xout: read the chunk's 16 values before its stores, so
                 // the loads issue together instead of each waiting behind the previous store
                 if (p.xres) {
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int m = n0 + cc * 16 + i;
-                        const int tt = m * p.ostride + phase - p.ooff;
-                        const bool in = ch_ok && m < p.m_rows && tt >= 0 && tt < p.lout && tt < lw;
-                        r[i] = in ? p.xres[(wbase + tt) * p.c_out_st + oc] : 0.0f;
+                        const int tt = tt0 + i * p.ostride;
+                        const bool in = ch_ok && m0c + i < p.m_rows && tt >= 0 && tt < p.lout && tt < lw;
+                        r[i] = in ? p.xres[base + i * step] : 0.0f;
                     }
                 }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int m = n0 + cc * 16 + i;
-                    const int tt = m * p.ostride + phase - p.ooff;
-                    if (m >= p.m_rows || tt < 0 || tt >= p.lout) continue;
-                    const size_t idx = (wbase + tt) * p.c_out_st + oc;
+                    const int tt = tt0 + i * p.ostride;
+                    if (m0c + i >= p.m_rows || tt < 0 || tt >= p.lout) continue;
+                    const long long idx = base + i * step;
                     if (!ch_ok || tt >= lw) {
                         if (p.xout) p.xout[idx] = 0.0f;
                         p.sout[idx] = __float2half_rn(0.0f);
@@ -222,8 +225,10 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
                     if (p.xout) p.xout[idx] = x;
                     float y = x;
                     if (p.alpha) {
-                        // snake: x + sin(alpha x)^2 / alpha (inverse precomputed), each step rounded
-                        const float sn = sinf(__fmul_rn(x, al));
+                        // snake: x + sin(alpha x)^2 / alpha (inverse precomputed). The hardware
+                        // sine's error (about 2^-21 absolute near zero, growing with |alpha x|)
+                        // stays far below the f16 rounding of the result, the next conv's input.
+                        const float sn = __sinf(__fmul_rn(x, al));
                         y = __fadd_rn(x, __fmul_rn(__fmul_rn(sn, sn), iv));
                     }
                     p.sout[idx] = __float2half_rn(y);
