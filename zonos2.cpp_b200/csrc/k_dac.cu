@@ -301,10 +301,21 @@ __global__ void dac_out_kernel(const __half* __restrict__ in, int lin, int c_st,
     if (j0 >= len) { pdl_release(); return; }
     const int ld = c_fin + 1;                         // odd stride: conflict-free column reads
     const int64_t t0 = s0 + j0 - 3;
-    for (int i = threadIdx.x; i < (OUT_TILE + 6) * c_fin; i += blockDim.x) {
-        const int r = i / c_fin, c = i % c_fin;
-        const int64_t t = t0 + r;
-        xs[r * ld + c] = (t >= 0 && t < lin) ? __half2float(in[((size_t)wi * lin + t) * c_st + c]) : 0.0f;
+    // eight loads in flight per thread before their shared-memory stores
+    const int total = (OUT_TILE + 6) * c_fin;
+    for (int i0 = threadIdx.x; i0 < total; i0 += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * blockDim.x, r = i / c_fin, c = i % c_fin;
+            const int64_t t = t0 + r;
+            v[u] = (i < total && t >= 0 && t < lin) ? __half2float(in[((size_t)wi * lin + t) * c_st + c]) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * blockDim.x;
+            if (i < total) xs[(i / c_fin) * ld + i % c_fin] = v[u];
+        }
     }
     for (int i = threadIdx.x; i < 7 * c_fin; i += blockDim.x) ws[i] = __half2float(__float2half_rn(w[i]));
     __syncthreads();
