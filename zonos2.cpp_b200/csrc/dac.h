@@ -94,11 +94,12 @@ struct DacConvIO {
     const __half* in = nullptr;   // [n_win][lin][c_in_st] f16 (already snake-activated)
     int lin = 0, c_in_st = 0, n_win = 0;
     const float* xres = nullptr;  // residual added to the output, [n_win][lout][c_out_st] f32 (may alias xout)
-    float* xout = nullptr;        // f32 output (the residual stream), or null
+    float* xout = nullptr;        // f32 output (the residual stream; rows past lw_out and padding
+                                  // channels are left unwritten, as nothing reads them), or null
     __half* sout = nullptr;       // f16 output after the next snake (or as is), [n_win][lout][c_out_st]
     int lout = 0, c_out_st = 0;
     const DacSnake* snake = nullptr;
-    const int* lw_out = nullptr;  // [n_win] valid output rows per window; rows past it are written as 0
+    const int* lw_out = nullptr;  // [n_win] valid output rows per window; sout rows past it are written as 0
     uint32_t* err = nullptr;
 };
 

@@ -216,7 +216,8 @@ dac_conv_kernel(const ConvK p, const __grid_constant__ CUtensorMap wmap, const _
                     if (m0c + i >= p.m_rows || tt < 0 || tt >= p.lout) continue;
                     const long long idx = base + i * step;
                     if (!ch_ok || tt >= lw) {
-                        if (p.xout) p.xout[idx] = 0.0f;
+                        // the next conv reads these zeros (its zero padding); the residual
+                        // stream there is never read, so xout is left as is
                         p.sout[idx] = __float2half_rn(0.0f);
                         continue;
                     }
