@@ -115,6 +115,32 @@ int z2b_slot_prefill_spk(z2b_ctx* ctx, int slot, const int32_t* ids, int n0, con
 int z2b_logits(z2b_model* model, const int32_t* ids, int n_tokens, float* out_logits, const float* spk, int spk_pos,
                const float* spk_emotion_delta);
 
+/* Options of a TTS prompt (zonos2_prompt_options, src/zonos2.h:181-188); defaults from
+ * z2b_prompt_options_default reproduce the reference's offline prompt. */
+typedef struct z2b_prompt_options {
+    int32_t prepend_silence;           /* 1: append the 17 sheared 0.2 s silence frames */
+    int32_t speaking_rate_bucket;      /* -1: no speaking-rate row */
+    int32_t n_quality;                 /* entries used in quality_buckets; 0: the default
+                                          (trailing_silence_s feature at bucket 3) */
+    int32_t quality_buckets[16];       /* bucket per quality feature, -1 skips the feature */
+    int32_t add_speaker_slot;          /* 1: prepend the speaker slot (+ marker rows) for cloning */
+    int32_t clean_speaker_background;
+    int32_t accurate_mode;
+} z2b_prompt_options;
+void z2b_prompt_options_default(z2b_prompt_options* opt);
+
+/* Build the input rows [n_rows][n_codebooks + 1] of a TTS prompt for the UTF-8 text
+ * (text_len bytes) with the model's hyper-parameters (z2b_model_hparams): optional speaker
+ * slot and marker rows, speaking-rate and quality rows, BOS, one row per byte (id byte + 192),
+ * EOS, then the sheared silence frames. Replaces zonos2_build_prompt (src/zonos2.h:190-195,
+ * src/zonos2-prompt.cpp:54-133), row for row. *n_rows receives the row count and *spk_pos
+ * the speaker slot's row (-1 without one). A call with out_ids NULL and cap_rows 0 only
+ * sizes the prompt (Z2B_OK); otherwise cap_rows < *n_rows writes nothing and returns
+ * Z2B_ERR_ARG. Bucket values are not range-checked, as in the reference. Host-only: no
+ * device is needed. */
+int z2b_build_prompt(const z2b_hparams* hp, const char* text, int64_t text_len, const z2b_prompt_options* opt,
+                     int32_t* out_ids, int cap_rows, int* n_rows, int* spk_pos);
+
 /* One batched step over n streams: rows ids[sum(n_new)][10] are fed in desc order
  * (decode streams feed one row; prompt chunks may be mixed in). For each desc with
  * Z2B_WANT_SAMPLE, out_codes[i*n_codebooks ..] receives the sampled frame; with

@@ -26,7 +26,7 @@ LIB = os.path.join(PKG, "libz2b.so")
 SYNTH_LIB = os.path.join(PKG, "libz2b_synth.so")
 
 HOST_COMMON = ["gguf.cpp", "quant.cpp"]
-Z2B_HOST = ["repack.cpp", "model.cpp", "runtime.cpp", "capi.cpp", "dac.cpp", "capi_dac.cpp"]
+Z2B_HOST = ["repack.cpp", "model.cpp", "runtime.cpp", "capi.cpp", "dac.cpp", "capi_dac.cpp", "prompt.cpp"]
 Z2B_CUDA = ["k_gemv.cu", "k_gemm.cu", "k_attn.cu", "k_router.cu", "k_misc.cu", "k_test.cu", "k_dac.cu"]
 
 

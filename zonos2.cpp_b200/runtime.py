@@ -50,6 +50,14 @@ class Sampling(ctypes.Structure):
                          1 if greedy else 0)
 
 
+class PromptOptions(ctypes.Structure):
+    """zonos2_prompt_options (src/zonos2.h:181-188)."""
+    _fields_ = [("prepend_silence", ctypes.c_int32), ("speaking_rate_bucket", ctypes.c_int32),
+                ("n_quality", ctypes.c_int32), ("quality_buckets", ctypes.c_int32 * 16),
+                ("add_speaker_slot", ctypes.c_int32), ("clean_speaker_background", ctypes.c_int32),
+                ("accurate_mode", ctypes.c_int32)]
+
+
 class SlotDesc(ctypes.Structure):
     _fields_ = [("slot", ctypes.c_int32), ("n_past", ctypes.c_int32), ("n_new", ctypes.c_int32),
                 ("flags", ctypes.c_int32), ("cfg_twin", ctypes.c_int32), ("cfg_scale", ctypes.c_float)]
@@ -106,6 +114,8 @@ def lib():
             "z2b_debug_router_capture": ([P, I], I),
             "z2b_debug_router_inputs": ([P, I, V, V, ctypes.POINTER(ctypes.c_int)], I),
             "z2b_debug_last_sel": ([P, V, I], I),
+            "z2b_prompt_options_default": ([V], None),
+            "z2b_build_prompt": ([ctypes.POINTER(HParams), ctypes.c_char_p, ctypes.c_int64, V, V, I, V, V], I),
             "z2b_dac_load": ([ctypes.c_char_p, I, ctypes.POINTER(P)], I),
             "z2b_dac_free": ([P], I),
             "z2b_dac_get_hparams": ([P, V], I),
@@ -391,6 +401,31 @@ def slot_after_sample(hp: HParams, s: Slot, codes, max_frames: int, keep: bool =
     s.done, s.step, s.eos_frame, s.countdown = bool(st.done), st.step, st.eos_frame, st.countdown
     s.next_ids = [int(x) for x in st.next_ids[:ncb + 1]]
     return bool(rc)
+
+
+def build_prompt(hp: HParams, text, prepend_silence=True, speaking_rate_bucket=-1, quality_buckets=None,
+                 add_speaker_slot=False, clean_speaker_background=True, accurate_mode=True):
+    """zonos2_build_prompt: TTS prompt rows [n][n_codebooks + 1] (int32) and the speaker slot's row
+    (-1 without one) for text (str, encoded as UTF-8, or bytes)."""
+    b = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+    o = PromptOptions()
+    lib().z2b_prompt_options_default(ctypes.byref(o))
+    o.prepend_silence = 1 if prepend_silence else 0
+    o.speaking_rate_bucket = speaking_rate_bucket
+    if quality_buckets:
+        o.n_quality = len(quality_buckets)
+        for i, q in enumerate(quality_buckets):
+            o.quality_buckets[i] = q
+    o.add_speaker_slot = 1 if add_speaker_slot else 0
+    o.clean_speaker_background = 1 if clean_speaker_background else 0
+    o.accurate_mode = 1 if accurate_mode else 0
+    n, sp = ctypes.c_int(), ctypes.c_int()
+    _check(lib().z2b_build_prompt(ctypes.byref(hp), b, len(b), ctypes.byref(o), None, 0, ctypes.byref(n),
+                                  ctypes.byref(sp)))
+    out = np.empty((n.value, hp.n_codebooks + 1), np.int32)
+    _check(lib().z2b_build_prompt(ctypes.byref(hp), b, len(b), ctypes.byref(o), _ptr(out), n.value,
+                                  ctypes.byref(n), ctypes.byref(sp)))
+    return out, sp.value
 
 
 def test_dequant(qtype: int, rows: int, k: int, raw: np.ndarray, from_tiles: bool) -> np.ndarray:
