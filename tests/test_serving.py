@@ -1,0 +1,156 @@
+"""Text-to-PCM serving (zonos2.cpp_b200/serving.py), the server's worker loop without HTTP.
+
+On the CPU a scripted step context stands in for the GPU backbone and the DAC oracle decodes
+the windows: prompt rows come from the prompt builder, the EOS frame and countdown follow
+zonos2_slot_sample (through z2b_slot_after_frame), and each request's PCM, streamed or
+buffered, equals one decode of its codes up to the EOS frame. The GPU test serves real
+requests through the backbone and the GPU DAC and checks the same, bit for bit, plus that a
+request's frames do not depend on the other requests in its steps."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle.dac_oracle import DacOracle
+
+
+class _OracleDecoder:
+    def __init__(self, o):
+        self.o = o
+
+    def decode_windows(self, ws):
+        return [self.o.decode_window(*w) for w in ws]
+
+
+class _ScriptedCtx:
+    """Step context whose sampled frames are scripted per admission (the n-th slot_reset):
+    random codes, with an end-of-audio code at codebook `eoa_cb` of frame `eoa_at[n]` (or
+    never)."""
+
+    def __init__(self, hp, eoa_at, eoa_cb=3, seed=0):
+        self.hp, self.eoa_at, self.eoa_cb = hp, eoa_at, eoa_cb
+        self.g = np.random.default_rng(seed)
+        self.frame, self.eoa, self.adm = {}, {}, {}
+        self.fed = []                      # rows fed, per admission
+        self.n_admitted = 0
+
+    def slot_reset(self, slot, sampling):
+        self.frame[slot] = 0
+        self.eoa[slot] = self.eoa_at.get(self.n_admitted, -1)
+        self.adm[slot] = self.n_admitted
+        self.fed.append([])
+        self.n_admitted += 1
+
+    def step(self, descs, rows, want_logits=False):
+        out, r = [], 0
+        for slot, n_past, n_new, _ in descs:
+            self.fed[self.adm[slot]].append(rows[r:r + n_new].copy())
+            r += n_new
+            f = self.g.integers(0, 1024, self.hp.n_codebooks).astype(np.int32)
+            if self.frame[slot] == self.eoa[slot]:
+                f[self.eoa_cb] = self.hp.eoa_id
+            self.frame[slot] += 1
+            out.append(f)
+        return np.stack(out), None
+
+
+def _hp():
+    import z2b.runtime as R
+    hp = R.HParams()
+    hp.n_codebooks, hp.codebook_size, hp.audio_vocab, hp.eoa_id, hp.audio_pad_id, hp.text_vocab = 9, 1024, 1026, 1024, 1025, 519
+    return hp
+
+
+@pytest.fixture(scope="module")
+def small_dac(model_dir):
+    import z2b.synth as S
+    return S.cached_dac("dac_small", 0, model_dir)
+
+
+def test_serving_with_scripted_backbone(small_dac):
+    import z2b.runtime as R
+    import z2b.serving as SV
+    hp = _hp()
+    o = DacOracle(small_dac)
+    ctx = _ScriptedCtx(hp, eoa_at={0: 70, 1: 5})
+    eng = SV.TtsEngine(ctx, hp, _OracleDecoder(o), n_slots=2)
+    reqs = [SV.TtsRequest(0, "First request.", max_frames=200),
+            SV.TtsRequest(1, "Second, buffered.", max_frames=200, stream=False),
+            SV.TtsRequest(2, "Third waits for a slot.", max_frames=90, fade_out_ms=5.0)]
+    for q in reqs:
+        eng.submit(q)
+    done = eng.run()
+    assert sorted(done) == [0, 1, 2]
+    for q in reqs:
+        d = done[q.rid]
+        codes, eos = d["codes"], d["eos_frame"]
+        nf = len(codes)
+        if q.rid == 2:
+            assert eos == -1 and nf == 90                         # no EOS: max_frames ends it
+        else:                                                     # EOS at codebook 3 of frame k
+            k = {0: 70, 1: 5}[q.rid]
+            assert eos == k - 3 and nf == k + hp.n_codebooks + 1
+        end = eos if 0 <= eos < nf else nf
+        whole = o.decode(codes, eos=end)
+        if q.fade_out_ms:
+            import z2b.streaming as ST
+            whole = ST.apply_fade(whole, q.fade_out_ms, 44100)
+        assert d["pcm"].shape == whole.shape, q.rid
+        assert np.abs(d["pcm"] - whole).max() <= 1e-6, q.rid
+        if q.stream and nf >= 72:                                 # block + context + shear
+            assert len(d["chunks"]) > 1                          # streamed in blocks
+    # the first rows of each admission are the prompt builder's rows of its request, then
+    # one row per step: the previous frame and the text pad
+    for n, q in enumerate(reqs):
+        assert np.array_equal(ctx.fed[n][0], R.build_prompt(hp, q.text)[0])
+        assert all(len(x) == 1 and x[0, 9] == hp.text_vocab for x in ctx.fed[n][1:])
+
+
+def test_eos_frame_follows_slot_sample():
+    """EOS at codebook c of frame k sets eos_frame k - c and ends the stream n_codebooks
+    frames later (the countdown of zonos2_slot_sample)."""
+    import z2b.serving as SV
+    hp = _hp()
+
+    class _Null:
+        def decode_windows(self, ws):
+            return [np.zeros((w[2] - w[1]) * 4, np.float32) for w in ws]
+
+    for k, c in ((40, 3), (2, 5)):
+        ctx = _ScriptedCtx(hp, eoa_at={0: k}, eoa_cb=c)
+        eng = SV.TtsEngine(ctx, hp, _Null(), n_slots=1)
+        eng.submit(SV.TtsRequest(0, "x", max_frames=500))
+        d = eng.run()[0]
+        assert d["eos_frame"] == max(0, k - c)
+        assert len(d["codes"]) == k + hp.n_codebooks + 1
+
+
+@pytest.mark.gpu
+def test_gpu_serving_end_to_end(model_dir, small_dac):
+    import z2b.dac as D
+    import z2b.runtime as R
+    import z2b.serving as SV
+    import z2b.synth as S
+    m = R.Model(S.cached("tiny", directory=model_dir))
+    dac = D.Dac(small_dac)
+    texts = ["Hello there.", "A second, longer request for the batch.", "Third."]
+
+    def serve(idx, n_slots):
+        ctx = R.BatchCtx(m, n_slots, 512)
+        eng = SV.TtsEngine(ctx, m.hp, dac, n_slots=n_slots)
+        for i in idx:
+            eng.submit(SV.TtsRequest(i, texts[i], max_frames=120, stream=i != 1))
+        done = eng.run()
+        ctx.close()
+        return done
+
+    together = serve([0, 1, 2], 2)                     # request 2 waits for a free slot
+    for i in range(3):
+        d = together[i]
+        nf = len(d["codes"])
+        end = d["eos_frame"] if 0 <= d["eos_frame"] < nf else nf
+        assert np.array_equal(d["pcm"], dac.decode(d["codes"], eos=end)), i
+        alone = serve([i], 1)[i]
+        assert np.array_equal(alone["codes"], d["codes"]), i   # batch-invariant frames
+    dac.close()
+    m.close()

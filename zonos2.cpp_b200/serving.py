@@ -1,0 +1,115 @@
+"""Text-to-PCM serving on one GPU: the server's request path without its HTTP layer.
+
+Mirrors the worker loop of src/server.cpp:1034-1275 on this library's calls:
+  - admission: the request's text becomes prompt rows (z2b_build_prompt) in a free slot, and
+    its rows ride in the next batched step with the other streams' decode rows;
+  - each step: one z2b_step over every active stream (device sampling), then per stream
+    zonos2_slot_sample's bookkeeping (z2b_slot_after_frame: EOS frame, countdown,
+    max_frames, next input row), the frame appended to the stream's codes;
+  - audio: streaming requests emit DAC windows on the server's cadence as frames arrive,
+    and every request's tail (or whole buffered decode) goes out when its slot finishes;
+    all pending windows of all requests are decoded in one batched GPU DAC call per step
+    (streaming.DacBatcher), not one window per DAC lane thread.
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .streaming import DacBatcher, PcmStream, StreamCfg
+
+
+@dataclass
+class TtsRequest:
+    rid: int
+    text: str
+    max_frames: int = 1500
+    stream: bool = True                 # False: one buffered decode at the end
+    fade_out_ms: float = 0.0
+    sampling: object = None             # runtime.Sampling; None: greedy
+
+
+@dataclass
+class _Job:
+    req: TtsRequest
+    slot: object                        # runtime.Slot
+    rows: np.ndarray                    # rows fed in the next step
+    pcm: PcmStream
+    chunks: list = field(default_factory=list)
+
+
+class TtsEngine:
+    """Requests in, PCM chunks out. ``ctx`` is a runtime.BatchCtx (or anything with its
+    slot_reset / step calls), ``dac`` a dac.Dac (or anything with decode_windows)."""
+
+    def __init__(self, ctx, hp, dac, n_slots: int, cfg: StreamCfg | None = None):
+        self.ctx, self.hp, self.n_slots = ctx, hp, n_slots
+        self.cfg = cfg or StreamCfg(n_codebooks=hp.n_codebooks)
+        self.batcher = DacBatcher(dac)
+        self.jobs: dict[int, _Job] = {}
+        self.queue: deque[TtsRequest] = deque()
+        self.done: dict[int, dict] = {}     # rid -> codes, eos_frame, pcm
+        self.frames = 0
+
+    def submit(self, req: TtsRequest) -> None:
+        self.queue.append(req)
+
+    def _admit(self) -> None:
+        from . import runtime as R
+        used = {j.slot.index for j in self.jobs.values()}
+        free = [s for s in range(self.n_slots) if s not in used]
+        while self.queue and free:
+            req, slot = self.queue.popleft(), free.pop(0)
+            rows, _ = R.build_prompt(self.hp, req.text)
+            self.ctx.slot_reset(slot, req.sampling or R.Sampling(greedy=True))
+            self.jobs[req.rid] = _Job(req, R.Slot(index=slot), rows, PcmStream(self.cfg))
+
+    def step(self) -> list[int]:
+        """Admit queued requests into free slots, run one batched step, hand out audio.
+        Returns the requests that finished in this step."""
+        from . import runtime as R
+        self._admit()
+        if not self.jobs:
+            return []
+        order = sorted(self.jobs.values(), key=lambda j: j.slot.index)
+        descs = [(j.slot.index, j.slot.n_past, len(j.rows), R.WANT_SAMPLE) for j in order]
+        codes, _ = self.ctx.step(descs, np.concatenate([j.rows for j in order]), want_logits=False)
+        finished = []
+        for i, j in enumerate(order):
+            s = j.slot
+            s.n_past += len(j.rows)
+            frame = np.asarray(codes[i][: self.hp.n_codebooks], np.int32)
+            R.slot_after_sample(self.hp, s, frame, j.req.max_frames)
+            j.pcm.push(frame)
+            self.frames += 1
+            j.rows = np.asarray(s.next_ids, np.int32)[None]
+            if j.req.stream:
+                for w in j.pcm.ready_windows():
+                    self.batcher.submit(j.req.rid, w)
+            if s.done:
+                if j.req.stream:
+                    w = j.pcm.final_window(s.eos_frame)
+                else:                                   # buffered: one decode of [0, end)
+                    nf = len(j.pcm.codes)
+                    end = s.eos_frame if 0 <= s.eos_frame < nf else nf
+                    w = (j.pcm._snapshot(nf), 0, end, 0, 0) if end > 0 else None
+                self.batcher.submit(j.req.rid, w, j.req.fade_out_ms, self.cfg.sample_rate)
+                finished.append(j.req.rid)
+        for rid, pcm in self.batcher.flush():
+            self.jobs[rid].chunks.append(pcm)
+        for rid in finished:
+            j = self.jobs.pop(rid)
+            self.done[rid] = dict(codes=np.asarray(j.pcm.codes, np.int32).reshape(-1, self.hp.n_codebooks),
+                                  eos_frame=j.slot.eos_frame, chunks=j.chunks,
+                                  pcm=np.concatenate(j.chunks) if j.chunks else np.zeros(0, np.float32))
+        return finished
+
+    def run(self, max_steps: int = 1_000_000) -> dict[int, dict]:
+        """Step until every submitted request has finished."""
+        n = 0
+        while (self.queue or self.jobs) and n < max_steps:
+            self.step()
+            n += 1
+        return self.done
