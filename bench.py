@@ -558,6 +558,71 @@ def dac_bench(args):
     dac.close()
 
 
+SERVE_SLOTS, SERVE_FRAMES = 16, (300, 600)
+
+
+def serve_bench(args):
+    """Text to PCM on one GPU (zonos2.cpp_b200/serving.py, the server's worker loop without
+    HTTP): 16 slots kept full from a queue of synthetic text requests (greedy, max_frames
+    U[300, 600], streamed PCM on the server's block 40 / context 24 cadence). Every step is
+    one batched backbone step (z2b_step) plus one batched GPU DAC call for the windows that
+    became ready. value = backbone frames per second; pcm_seconds_per_s = audio out per
+    second. Timed with CUDA events around K steps on the backbone's stream after the slots
+    are full (the DAC runs on its own stream and each call completes inside the step)."""
+    import torch
+    load_pkg()
+    import z2b.dac as D
+    import z2b.runtime as R
+    import z2b.serving as SV
+    import z2b.synth as S
+    model = R.Model(S.cached("zonos2", directory=model_dir()))
+    dac = D.Dac(S.cached_dac("dac44k", 0, model_dir()))
+    ctx = R.BatchCtx(model, SERVE_SLOTS, 1024)
+    ctx.set_logits_readback(False)
+    eng = SV.TtsEngine(ctx, model.hp, dac, n_slots=SERVE_SLOTS)
+    g = np.random.default_rng(11)
+    words = ["speech", "model", "stream", "audio", "the", "quick", "voice", "batch", "frame", "decode"]
+    n_req = SERVE_SLOTS * 8
+    for i in range(n_req):
+        text = " ".join(g.choice(words, int(g.integers(4, 20)))) + "."
+        eng.submit(SV.TtsRequest(i, text, max_frames=int(g.integers(*SERVE_FRAMES))))
+    for _ in range(max(args.warmup, 3) + 100):           # slots full, requests part-way through
+        eng.step()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    clk = ClockSampler(0)
+    clk.start()
+    torch.cuda.synchronize()
+    f0 = eng.frames
+    pcm0 = sum(sum(x.size for x in j.chunks) for j in eng.jobs.values()) + \
+        sum(d["pcm"].size for d in eng.done.values())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1)
+    frames = eng.frames - f0
+    pcm1 = sum(sum(x.size for x in j.chunks) for j in eng.jobs.values()) + \
+        sum(d["pcm"].size for d in eng.done.values())
+    line = {"metric": "text-to-PCM serving: backbone frames/s with streamed audio (16 slots)",
+            "value": frames / (ms * 1e-3), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": max(args.warmup, 3) + 100, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "ZONOS2-scale Q4_K backbone + DAC 44 kHz decoder shapes, 16 slots, "
+                                   "text requests, max_frames U[300,600], streamed PCM",
+                       "parallelism": "replicas x1"},
+            "pcm_seconds_per_s": (pcm1 - pcm0) / 44100 / (ms * 1e-3),
+            "requests_finished": len(eng.done), "clocks": clocks,
+            "timing": "CUDA events on the backbone stream around K host-driven steps (prompt rows, "
+                      "frames D2H, DAC windows decoded and copied to the host inside)"}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    dac.close()
+    model.close()
+
+
 def workload_name():
     return (f"config2: ZONOS2-scale Q4_K backbone, {STREAMS} streams/GPU, ctx U[{CTX_RANGE[0]},{CTX_RANGE[1]}], "
             f"{STEPS_PER_STREAM} frames per stream, continuous refill with {REFILL_PROMPT}-row prompts")
@@ -601,6 +666,8 @@ def main():
                     help="config 3: Q6_K and Q8_0 backbones, 60 decode + 4 prompt streams per step, one JSON line each")
     ap.add_argument("--dac", action="store_true",
                     help="DAC decode of 16 streaming windows per call (codes -> PCM on the GPU)")
+    ap.add_argument("--serve", action="store_true",
+                    help="text-to-PCM serving on one GPU: backbone steps plus batched streamed DAC decode")
     ap.add_argument("--config5", action="store_true",
                     help="config 5: whole-box serving of Poisson arrivals through the replica dispatcher")
     args = ap.parse_args()
@@ -613,6 +680,8 @@ def main():
         return crossover(args)
     if args.dac:
         return dac_bench(args)
+    if args.serve:
+        return serve_bench(args)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
