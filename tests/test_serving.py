@@ -41,6 +41,10 @@ class _ScriptedCtx:
         self.fed.append([])
         self.n_admitted += 1
 
+    def slot_prefill(self, slot, ids, spk=None, spk_pos=0, spk_emotion_delta=None):
+        self.fed[self.adm[slot]].append(("prefill", np.asarray(ids).copy(), spk_pos))
+        return None
+
     def step(self, descs, rows, want_logits=False):
         out, r = [], 0
         for slot, n_past, n_new, _ in descs:
@@ -106,6 +110,37 @@ def test_serving_with_scripted_backbone(small_dac):
         assert all(len(x) == 1 and x[0, 9] == hp.text_vocab for x in ctx.fed[n][1:])
 
 
+def test_speaker_request_prefills_then_steps():
+    """A cloned-voice request: the speaker slot row first, all prompt rows but the last prefilled
+    with the speaker at that row, the last row fed by the next step at n_past = rows - 1."""
+    import z2b.runtime as R
+    import z2b.serving as SV
+    hp = _hp()
+
+    class _Null:
+        def decode_windows(self, ws):
+            return [np.zeros((w[2] - w[1]) * 4, np.float32) for w in ws]
+
+    ctx = _ScriptedCtx(hp, eoa_at={})
+
+    seen = []
+    orig = ctx.step
+
+    def step(descs, rows, want_logits=False):
+        seen.append(list(descs))
+        return orig(descs, rows, want_logits)
+
+    ctx.step = step
+    eng = SV.TtsEngine(ctx, hp, _Null(), n_slots=1)
+    eng.submit(SV.TtsRequest(0, "cloned", max_frames=5, speaker=np.ones(128, np.float32)))
+    eng.run()
+    full, spk_pos = R.build_prompt(hp, "cloned", add_speaker_slot=True)
+    kind, pre, pos = ctx.fed[0][0]
+    assert kind == "prefill" and spk_pos == pos == 0 and np.array_equal(pre, full[:-1])
+    assert np.array_equal(ctx.fed[0][1], full[-1:])
+    assert seen[0][0][1:3] == (len(full) - 1, 1)              # n_past, n_new of the first step
+
+
 def test_eos_frame_follows_slot_sample():
     """EOS at codebook c of frame k sets eos_frame k - c and ends the stream n_codebooks
     frames later (the countdown of zonos2_slot_sample)."""
@@ -145,6 +180,22 @@ def test_gpu_serving_end_to_end(model_dir, small_dac):
         return done
 
     together = serve([0, 1, 2], 2)                     # request 2 waits for a free slot
+    # a cloned voice: the speaker changes the frames, and batching does not
+    spk = np.random.default_rng(4).standard_normal(m.hp.spk_dim).astype(np.float32)
+
+    def serve_spk(extra):
+        ctx = R.BatchCtx(m, 2, 512)
+        eng = SV.TtsEngine(ctx, m.hp, dac, n_slots=2)
+        eng.submit(SV.TtsRequest(9, texts[0], max_frames=60, speaker=spk))
+        if extra:
+            eng.submit(SV.TtsRequest(8, texts[1], max_frames=60))
+        done = eng.run()
+        ctx.close()
+        return done[9]
+
+    a, b = serve_spk(False), serve_spk(True)
+    assert np.array_equal(a["codes"], b["codes"])
+    assert not np.array_equal(a["codes"], together[0]["codes"][:60])
     for i in range(3):
         d = together[i]
         nf = len(d["codes"])

@@ -2,7 +2,11 @@
 
 Mirrors the worker loop of src/server.cpp:1034-1275 on this library's calls:
   - admission: the request's text becomes prompt rows (z2b_build_prompt) in a free slot, and
-    its rows ride in the next batched step with the other streams' decode rows;
+    its rows ride in the next batched step with the other streams' decode rows. A cloned
+    voice (a speaker embedding) gets the speaker slot row; all rows but the last are
+    prefilled with the speaker projected into that row (z2b_slot_prefill_spk, as the
+    reference's admission prefill), and the last row rides in the next step, whose device
+    sampler draws the first frame;
   - each step: one z2b_step over every active stream (device sampling), then per stream
     zonos2_slot_sample's bookkeeping (z2b_slot_after_frame: EOS frame, countdown,
     max_frames, next input row), the frame appended to the stream's codes;
@@ -29,6 +33,8 @@ class TtsRequest:
     stream: bool = True                 # False: one buffered decode at the end
     fade_out_ms: float = 0.0
     sampling: object = None             # runtime.Sampling; None: greedy
+    speaker: object = None              # [spk_dim] f32 speaker embedding (cloned voice), or None
+    emotion_delta: object = None        # [n_embd] f32 added to the speaker row, or None
 
 
 @dataclass
@@ -62,9 +68,14 @@ class TtsEngine:
         free = [s for s in range(self.n_slots) if s not in used]
         while self.queue and free:
             req, slot = self.queue.popleft(), free.pop(0)
-            rows, _ = R.build_prompt(self.hp, req.text)
+            rows, spk_pos = R.build_prompt(self.hp, req.text, add_speaker_slot=req.speaker is not None)
             self.ctx.slot_reset(slot, req.sampling or R.Sampling(greedy=True))
-            self.jobs[req.rid] = _Job(req, R.Slot(index=slot), rows, PcmStream(self.cfg))
+            s = R.Slot(index=slot)
+            if req.speaker is not None:
+                self.ctx.slot_prefill(slot, rows[:-1], spk=req.speaker, spk_pos=spk_pos,
+                                      spk_emotion_delta=req.emotion_delta)
+                s.n_past, rows = len(rows) - 1, rows[-1:]
+            self.jobs[req.rid] = _Job(req, s, rows, PcmStream(self.cfg))
 
     def step(self) -> list[int]:
         """Admit queued requests into free slots, run one batched step, hand out audio.
