@@ -42,12 +42,13 @@ class _ScriptedCtx:
         self.n_admitted += 1
 
     def slot_prefill(self, slot, ids, spk=None, spk_pos=0, spk_emotion_delta=None):
-        self.fed[self.adm[slot]].append(("prefill", np.asarray(ids).copy(), spk_pos))
+        self.fed[self.adm[slot]].append(("prefill", np.asarray(ids).copy(), spk_pos, spk_emotion_delta is not None))
         return None
 
     def step(self, descs, rows, want_logits=False):
         out, r = [], 0
-        for slot, n_past, n_new, _ in descs:
+        for d in descs:
+            slot, n_new = d[0], d[2]
             self.fed[self.adm[slot]].append(rows[r:r + n_new].copy())
             r += n_new
             f = self.g.integers(0, 1024, self.hp.n_codebooks).astype(np.int32)
@@ -135,10 +136,50 @@ def test_speaker_request_prefills_then_steps():
     eng.submit(SV.TtsRequest(0, "cloned", max_frames=5, speaker=np.ones(128, np.float32)))
     eng.run()
     full, spk_pos = R.build_prompt(hp, "cloned", add_speaker_slot=True)
-    kind, pre, pos = ctx.fed[0][0]
-    assert kind == "prefill" and spk_pos == pos == 0 and np.array_equal(pre, full[:-1])
+    kind, pre, pos, has_delta = ctx.fed[0][0]
+    assert kind == "prefill" and spk_pos == pos == 0 and np.array_equal(pre, full[:-1]) and not has_delta
     assert np.array_equal(ctx.fed[0][1], full[-1:])
     assert seen[0][0][1:3] == (len(full) - 1, 1)              # n_past, n_new of the first step
+
+
+def test_emotion_cfg_takes_a_twin_slot():
+    """Emotion CFG (scale != 1): the primary slot prefilled with speaker + delta, a twin slot
+    with the speaker only; every step carries the twin's desc right after the primary's, the
+    primary pointing at it with the scale, the twin asking for logits only, both on the same
+    rows. A request that cannot be served is finished as failed."""
+    import z2b.runtime as R
+    import z2b.serving as SV
+    hp = _hp()
+
+    class _Null:
+        def decode_windows(self, ws):
+            return [np.zeros((w[2] - w[1]) * 4, np.float32) for w in ws]
+
+    ctx = _ScriptedCtx(hp, eoa_at={})
+    seen = []
+    orig = ctx.step
+
+    def step(descs, rows, want_logits=False):
+        seen.append((list(descs), rows.copy()))
+        return orig(descs, rows, want_logits)
+
+    ctx.step = step
+    eng = SV.TtsEngine(ctx, hp, _Null(), n_slots=3)
+    spk, delta = np.ones(128, np.float32), np.ones(256, np.float32)
+    eng.submit(SV.TtsRequest(0, "happy", max_frames=4, speaker=spk, emotion_delta=delta, emotion_cfg_scale=2.5))
+    eng.submit(SV.TtsRequest(1, "plain", max_frames=4))
+    eng.submit(SV.TtsRequest(2, "no speaker", max_frames=4, emotion_delta=delta, emotion_cfg_scale=2.0))
+    done = eng.run()
+    assert done[2]["error"] and done[2]["pcm"] is None
+    assert len(done[0]["codes"]) == 4 and len(done[1]["codes"]) == 4
+    assert ctx.fed[0][0][3] and not ctx.fed[1][0][3]      # primary with the delta, twin without
+    descs, rows = seen[0]
+    assert [d[0] for d in descs] == [0, 1, 2]              # primary, twin, then request 1's slot
+    assert descs[0][3] == R.WANT_SAMPLE and descs[0][4] == 1 and descs[0][5] == 2.5
+    assert descs[1][3] == R.WANT_LOGITS and descs[1][1] == descs[0][1] and descs[1][2] == descs[0][2] == 1
+    assert np.array_equal(rows[0], rows[1])
+    for descs, rows in seen[1:]:
+        assert descs[1][1] == descs[0][1] and np.array_equal(rows[0], rows[1])
 
 
 def test_eos_frame_follows_slot_sample():
@@ -196,6 +237,24 @@ def test_gpu_serving_end_to_end(model_dir, small_dac):
     a, b = serve_spk(False), serve_spk(True)
     assert np.array_equal(a["codes"], b["codes"])
     assert not np.array_equal(a["codes"], together[0]["codes"][:60])
+
+    # emotion CFG against a twin: the scale changes the frames; batching does not
+    delta = np.random.default_rng(5).standard_normal(m.hp.n_embd).astype(np.float32)
+
+    def serve_cfg(scale, extra):
+        ctx = R.BatchCtx(m, 3, 512)
+        eng = SV.TtsEngine(ctx, m.hp, dac, n_slots=3)
+        eng.submit(SV.TtsRequest(7, texts[0], max_frames=60, speaker=spk, emotion_delta=delta,
+                                 emotion_cfg_scale=scale))
+        if extra:
+            eng.submit(SV.TtsRequest(6, texts[2], max_frames=60))
+        done = eng.run()
+        ctx.close()
+        return done[7]["codes"]
+
+    c1, c3, c3b = serve_cfg(1.0, False), serve_cfg(3.0, False), serve_cfg(3.0, True)
+    assert np.array_equal(c3, c3b)
+    assert not np.array_equal(c1, c3)
     for i in range(3):
         d = together[i]
         nf = len(d["codes"])

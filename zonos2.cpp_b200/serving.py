@@ -6,7 +6,10 @@ Mirrors the worker loop of src/server.cpp:1034-1275 on this library's calls:
     voice (a speaker embedding) gets the speaker slot row; all rows but the last are
     prefilled with the speaker projected into that row (z2b_slot_prefill_spk, as the
     reference's admission prefill), and the last row rides in the next step, whose device
-    sampler draws the first frame;
+    sampler draws the first frame. An emotion request with a CFG scale other than 1 also
+    takes a twin slot, prefilled with the speaker but without the emotion delta; the twin
+    steps on the same rows and its logits guide the stream's sampling,
+    u + scale * (c - u) (src/server.cpp:1064-1099, 1125-1142), on the device;
   - each step: one z2b_step over every active stream (device sampling), then per stream
     zonos2_slot_sample's bookkeeping (z2b_slot_after_frame: EOS frame, countdown,
     max_frames, next input row), the frame appended to the stream's codes;
@@ -35,6 +38,10 @@ class TtsRequest:
     sampling: object = None             # runtime.Sampling; None: greedy
     speaker: object = None              # [spk_dim] f32 speaker embedding (cloned voice), or None
     emotion_delta: object = None        # [n_embd] f32 added to the speaker row, or None
+    emotion_cfg_scale: float = 1.0      # with emotion_delta: CFG against an unconditional twin
+
+    def use_cfg(self) -> bool:
+        return self.emotion_delta is not None and self.emotion_cfg_scale != 1.0
 
 
 @dataclass
@@ -44,6 +51,7 @@ class _Job:
     rows: np.ndarray                    # rows fed in the next step
     pcm: PcmStream
     chunks: list = field(default_factory=list)
+    twin: object = None                 # runtime.Slot of the unconditional twin (emotion CFG)
 
 
 class TtsEngine:
@@ -56,7 +64,7 @@ class TtsEngine:
         self.batcher = DacBatcher(dac)
         self.jobs: dict[int, _Job] = {}
         self.queue: deque[TtsRequest] = deque()
-        self.done: dict[int, dict] = {}     # rid -> codes, eos_frame, pcm
+        self.done: dict[int, dict] = {}     # rid -> codes, eos_frame, pcm (or error)
         self.frames = 0
 
     def submit(self, req: TtsRequest) -> None:
@@ -64,18 +72,34 @@ class TtsEngine:
 
     def _admit(self) -> None:
         from . import runtime as R
-        used = {j.slot.index for j in self.jobs.values()}
+        used = {j.slot.index for j in self.jobs.values()} | {j.twin.index for j in self.jobs.values() if j.twin}
         free = [s for s in range(self.n_slots) if s not in used]
-        while self.queue and free:
-            req, slot = self.queue.popleft(), free.pop(0)
+        while self.queue:
+            req = self.queue[0]
+            need = 2 if req.use_cfg() else 1
+            if req.emotion_delta is not None and req.speaker is None or need > self.n_slots:
+                self.queue.popleft()              # cannot be served: finished as failed
+                why = "an emotion delta needs a speaker" if req.speaker is None else "CFG needs two slots"
+                self.done[req.rid] = dict(error=why, codes=None, eos_frame=-1, chunks=[], pcm=None)
+                continue
+            if len(free) < need:
+                break                             # first come, first served: the head waits
+            self.queue.popleft()
             rows, spk_pos = R.build_prompt(self.hp, req.text, add_speaker_slot=req.speaker is not None)
-            self.ctx.slot_reset(slot, req.sampling or R.Sampling(greedy=True))
-            s = R.Slot(index=slot)
+            slots = [free.pop(0) for _ in range(need)]
+            s = R.Slot(index=slots[0])
+            self.ctx.slot_reset(slots[0], req.sampling or R.Sampling(greedy=True))
+            twin = None
             if req.speaker is not None:
-                self.ctx.slot_prefill(slot, rows[:-1], spk=req.speaker, spk_pos=spk_pos,
+                self.ctx.slot_prefill(slots[0], rows[:-1], spk=req.speaker, spk_pos=spk_pos,
                                       spk_emotion_delta=req.emotion_delta)
-                s.n_past, rows = len(rows) - 1, rows[-1:]
-            self.jobs[req.rid] = _Job(req, s, rows, PcmStream(self.cfg))
+                s.n_past = len(rows) - 1
+                if need == 2:
+                    twin = R.Slot(index=slots[1], n_past=len(rows) - 1)
+                    self.ctx.slot_reset(slots[1], R.Sampling(greedy=True))
+                    self.ctx.slot_prefill(slots[1], rows[:-1], spk=req.speaker, spk_pos=spk_pos)
+                rows = rows[-1:]
+            self.jobs[req.rid] = _Job(req, s, rows, PcmStream(self.cfg), twin=twin)
 
     def step(self) -> list[int]:
         """Admit queued requests into free slots, run one batched step, hand out audio.
@@ -85,12 +109,24 @@ class TtsEngine:
         if not self.jobs:
             return []
         order = sorted(self.jobs.values(), key=lambda j: j.slot.index)
-        descs = [(j.slot.index, j.slot.n_past, len(j.rows), R.WANT_SAMPLE) for j in order]
-        codes, _ = self.ctx.step(descs, np.concatenate([j.rows for j in order]), want_logits=False)
+        descs, rows, at = [], [], []
+        for j in order:
+            at.append(len(descs))
+            if j.twin is None:
+                descs.append((j.slot.index, j.slot.n_past, len(j.rows), R.WANT_SAMPLE, -1, 1.0))
+                rows.append(j.rows)
+            else:                                       # the twin's desc follows, logits only
+                descs.append((j.slot.index, j.slot.n_past, len(j.rows), R.WANT_SAMPLE, len(descs) + 1,
+                              j.req.emotion_cfg_scale))
+                descs.append((j.twin.index, j.twin.n_past, len(j.rows), R.WANT_LOGITS, -1, 1.0))
+                rows += [j.rows, j.rows]
+        codes, _ = self.ctx.step(descs, np.concatenate(rows), want_logits=False)
         finished = []
-        for i, j in enumerate(order):
+        for i, j in zip(at, order):
             s = j.slot
             s.n_past += len(j.rows)
+            if j.twin is not None:
+                j.twin.n_past += len(j.rows)
             frame = np.asarray(codes[i][: self.hp.n_codebooks], np.int32)
             R.slot_after_sample(self.hp, s, frame, j.req.max_frames)
             j.pcm.push(frame)
