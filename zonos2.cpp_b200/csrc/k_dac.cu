@@ -302,20 +302,50 @@ __global__ void dac_out_kernel(const __half* __restrict__ in, int lin, int c_st,
     if (j0 >= len) { pdl_release(); return; }
     const int ld = c_fin + 1;                         // odd stride: conflict-free column reads
     const int64_t t0 = s0 + j0 - 3;
-    // eight loads in flight per thread before their shared-memory stores
-    const int total = (OUT_TILE + 6) * c_fin;
-    for (int i0 = threadIdx.x; i0 < total; i0 += 8 * blockDim.x) {
-        float v[8];
+    if (c_fin % 8 == 0 && c_st % 8 == 0) {
+        // 16-byte loads of eight channels (rows start 16-byte aligned: c_st is a multiple of 8),
+        // four in flight per thread before their shared-memory stores
+        const int vpr = c_fin / 8, vtotal = (OUT_TILE + 6) * vpr;
+        for (int i0 = threadIdx.x; i0 < vtotal; i0 += 4 * blockDim.x) {
+            uint4 v[4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * blockDim.x, r = i / c_fin, c = i % c_fin;
-            const int64_t t = t0 + r;
-            v[u] = (i < total && t >= 0 && t < lin) ? __half2float(in[((size_t)wi * lin + t) * c_st + c]) : 0.0f;
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * blockDim.x, r = i / vpr, c8 = i % vpr;
+                const int64_t t = t0 + r;
+                v[u] = (i < vtotal && t >= 0 && t < lin)
+                           ? *reinterpret_cast<const uint4*>(in + ((size_t)wi * lin + t) * c_st + 8 * c8)
+                           : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * blockDim.x;
+                if (i >= vtotal) continue;
+                float* d = xs + (i / vpr) * ld + 8 * (i % vpr);
+                const __half2* h = reinterpret_cast<const __half2*>(&v[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h[e]);
+                    d[2 * e] = f.x;
+                    d[2 * e + 1] = f.y;
+                }
+            }
         }
+    } else {
+        // eight loads in flight per thread before their shared-memory stores
+        const int total = (OUT_TILE + 6) * c_fin;
+        for (int i0 = threadIdx.x; i0 < total; i0 += 8 * blockDim.x) {
+            float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u * blockDim.x;
-            if (i < total) xs[(i / c_fin) * ld + i % c_fin] = v[u];
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * blockDim.x, r = i / c_fin, c = i % c_fin;
+                const int64_t t = t0 + r;
+                v[u] = (i < total && t >= 0 && t < lin) ? __half2float(in[((size_t)wi * lin + t) * c_st + c]) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * blockDim.x;
+                if (i < total) xs[(i / c_fin) * ld + i % c_fin] = v[u];
+            }
         }
     }
     for (int i = threadIdx.x; i < 7 * c_fin; i += blockDim.x) ws[i] = __half2float(__float2half_rn(w[i]));
