@@ -1,6 +1,6 @@
 """DAC decoder, CPU side: the oracle (oracle/dac_o.cpp) pinned against an independent torch
-restatement of the published DAC decoder on synthetic files and, when the reference tree is
-readable, on the reference's own CI fixture tests/fixtures/dummy-dac.gguf; the window
+restatement of the published DAC decoder on synthetic files and, with Z2B_REFERENCE_DIR set to a
+reference checkout, on the reference's own CI fixture tests/fixtures/dummy-dac.gguf; the window
 semantics of dac_decode / dac_decode_window (src/dac.cpp:260-299); the WAV writer
 (src/dac.cpp:318-336); and the C ABI's exports."""
 from __future__ import annotations
@@ -17,7 +17,7 @@ import torch.nn.functional as F
 from oracle.dac_oracle import DacOracle, tensor_names
 from tests.util import cos
 
-REF_FIXTURE = "/root/reference/tests/fixtures/dummy-dac.gguf"
+REF_FIXTURE = os.path.join(os.environ.get("Z2B_REFERENCE_DIR", ""), "tests", "fixtures", "dummy-dac.gguf")
 
 
 def _torch_decode(o: DacOracle, codes, a, b, f16=True):
@@ -110,7 +110,8 @@ def test_oracle_matches_torch_restatement(which, tiny_dac, small_dac):
     assert np.abs(got).max() > 0.05                     # not a degenerate all-zero output
 
 
-@pytest.mark.skipif(not os.path.exists(REF_FIXTURE), reason="reference tree not readable")
+@pytest.mark.skipif(not os.environ.get("Z2B_REFERENCE_DIR") or not os.path.exists(REF_FIXTURE),
+                    reason="Z2B_REFERENCE_DIR not set to a reference checkout")
 def test_oracle_on_reference_fixture():
     """The reference's own CI DAC file (scripts/make-dummy-dac.py output) decodes identically
     through the oracle and the torch restatement."""
