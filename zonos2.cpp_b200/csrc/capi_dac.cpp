@@ -16,15 +16,9 @@ namespace {
 
 int decode(z2b_dac* dac, const std::vector<DacWin>& wins, float* audio, int64_t cap) {
     std::string err;
-    if (!dac_decode_batch(dac->m, wins, audio, cap, err)) {
-        set_error(err);
-        if (err.find("device error") != std::string::npos) return Z2B_ERR_DEVICE;
-        if (err.find("bad window") != std::string::npos || err.find("too small") != std::string::npos ||
-            err.find("too long") != std::string::npos)
-            return Z2B_ERR_ARG;
-        return Z2B_ERR_CUDA;
-    }
-    return Z2B_OK;
+    const int rc = dac_decode_batch(dac->m, wins, audio, cap, err);
+    if (rc != Z2B_OK) set_error(err);
+    return rc;
 }
 
 // The window of dac_decode_window (src/dac.cpp:280-299): latent frames [f_lo - Lc (>= 0),
@@ -57,11 +51,12 @@ int z2b_dac_load(const char* path, int device, z2b_dac** out) {
     z2b_dac* d = new (std::nothrow) z2b_dac;
     if (!d) { set_error("out of host memory"); return Z2B_ERR_OOM; }
     std::string err;
-    if (!dac_load(d->m, path, device, err)) {
+    const int rc = dac_load(d->m, path, device, err);
+    if (rc != Z2B_OK) {
         dac_free(d->m);
         delete d;
         set_error(err);
-        return err.find("cannot open") != std::string::npos ? Z2B_ERR_IO : Z2B_ERR_FORMAT;
+        return rc;
     }
     *out = d;
     return Z2B_OK;

@@ -9,6 +9,7 @@
 #include "dac.h"
 
 #include "gguf.h"
+#include "../../include/z2b.h"
 
 #include <cuda_runtime.h>
 #include <algorithm>
@@ -48,6 +49,7 @@ T* upload(DacModel& m, const std::vector<T>& v, std::string& err) {
         cudaMemcpy(d, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess) {
         err = "dac: device allocation failed";
         if (d) cudaFree(d);
+        m.load_oom = true;
         return nullptr;
     }
     m.allocs.push_back(d);
@@ -143,10 +145,10 @@ int DacModel::samples_per_frame() const {
     return spf;
 }
 
-bool dac_load(DacModel& m, const char* path, int device, std::string& err) {
+int dac_load(DacModel& m, const char* path, int device, std::string& err) {
     GGUFFile f;
-    if (!f.open(path, err)) { err = "dac: cannot open gguf '" + std::string(path) + "': " + err; return false; }
-    if (cudaSetDevice(device) != cudaSuccess) { err = "dac: bad device"; return false; }
+    if (!f.open(path, err)) { err = "dac: cannot open gguf '" + std::string(path) + "': " + err; return Z2B_ERR_IO; }
+    if (cudaSetDevice(device) != cudaSuccess) { err = "dac: bad device"; return Z2B_ERR_CUDA; }
     m.device = device;
     m.n_codebooks = (int)kv_u32(f, "dac.n_codebooks", 9);
     m.codebook_size = (int)kv_u32(f, "dac.codebook_size", 1024);
@@ -160,13 +162,13 @@ bool dac_load(DacModel& m, const char* path, int device, std::string& err) {
         m.rates.assign(r->ai.begin(), r->ai.end());
     if (m.n_codebooks < 1 || m.n_codebooks > 16 || m.codebook_size < 1 || m.latent < 1 || m.decoder_dim < 1) {
         err = "dac: unsupported hyperparameters";
-        return false;
+        return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
     }
     for (int r : m.rates)
-        if (r < 2 || r % 2) { err = "dac: decoder rates must be even"; return false; }
+        if (r < 2 || r % 2) { err = "dac: decoder rates must be even"; return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT; }
     if ((m.decoder_dim >> m.rates.size()) << m.rates.size() != m.decoder_dim) {
         err = "dac: decoder_dim must divide by 2^blocks";
-        return false;
+        return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
     }
 
     // quantizer: tables ne [latent, codebook] -> [codebook][latent], then every codebook
@@ -175,15 +177,15 @@ bool dac_load(DacModel& m, const char* path, int device, std::string& err) {
     all.reserve((size_t)m.n_codebooks * m.codebook_size * m.latent);
     for (int i = 0; i < m.n_codebooks; ++i) {
         const std::string n = "quant." + std::to_string(i) + ".table";
-        if (!read_f32(f, n, t, ne, err)) return false;
-        if (ne[0] != m.latent || ne[1] != m.codebook_size) { err = "dac: " + n + " has the wrong shape"; return false; }
+        if (!read_f32(f, n, t, ne, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
+        if (ne[0] != m.latent || ne[1] != m.codebook_size) { err = "dac: " + n + " has the wrong shape"; return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT; }
         all.insert(all.end(), t.begin(), t.end());
     }
-    if (!read_f32(f, "quant.bias", b, ne, err)) return false;
-    if ((int)b.size() != m.latent) { err = "dac: quant.bias has the wrong length"; return false; }
-    if (!(m.tables = upload(m, all, err)) || !(m.qbias = upload(m, b, err))) return false;
+    if (!read_f32(f, "quant.bias", b, ne, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
+    if ((int)b.size() != m.latent) { err = "dac: quant.bias has the wrong length"; return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT; }
+    if (!(m.tables = upload(m, all, err)) || !(m.qbias = upload(m, b, err))) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
 
-    if (!load_conv(m, f, "dec.conv_in", m.latent, m.decoder_dim, 7, 1, m.conv_in, err)) return false;
+    if (!load_conv(m, f, "dec.conv_in", m.latent, m.decoder_dim, 7, 1, m.conv_in, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
     m.blocks.resize(m.rates.size());
     for (size_t bi = 0; bi < m.rates.size(); ++bi) {
         DacBlock& B = m.blocks[bi];
@@ -191,8 +193,8 @@ bool dac_load(DacModel& m, const char* path, int device, std::string& err) {
         B.stride = m.rates[bi];
         B.c_in = m.decoder_dim >> bi;
         B.c_out = m.decoder_dim >> (bi + 1);
-        if (!load_snake(m, f, p + ".snake", B.c_in, B.snake, err)) return false;
-        if (!load_convt(m, f, p + ".convt", B.c_in, B.c_out, B.stride, B.convt, err)) return false;
+        if (!load_snake(m, f, p + ".snake", B.c_in, B.snake, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
+        if (!load_convt(m, f, p + ".convt", B.c_in, B.c_out, B.stride, B.convt, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
         static const int dils[3] = {1, 3, 9};
         for (int r = 0; r < 3; ++r) {
             const std::string q = p + ".res" + std::to_string(r);
@@ -201,32 +203,32 @@ bool dac_load(DacModel& m, const char* path, int device, std::string& err) {
                 !load_conv(m, f, q + ".conv1", B.c_out, B.c_out, 7, dils[r], R.c1, err) ||
                 !load_snake(m, f, q + ".snake2", B.c_out, R.s2, err) ||
                 !load_conv(m, f, q + ".conv2", B.c_out, B.c_out, 1, 1, R.c2, err))
-                return false;
+                return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
         }
     }
     m.c_fin = m.decoder_dim >> m.rates.size();
-    if (!load_snake(m, f, "dec.snake_out", m.c_fin, m.snake_out, err)) return false;
+    if (!load_snake(m, f, "dec.snake_out", m.c_fin, m.snake_out, err)) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
     {
         std::vector<float> w, bo;
         int64_t nw[4], nb[4];
         if (!read_f32(f, "dec.conv_out.weight", w, nw, err) || !read_f32(f, "dec.conv_out.bias", bo, nb, err))
-            return false;
+            return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
         if (nw[0] != 7 || nw[1] != m.c_fin || nw[2] != 1 || bo.size() != 1) {
             err = "dac: dec.conv_out has the wrong shape";
-            return false;
+            return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
         }
         std::vector<float> wt((size_t)7 * m.c_fin);
         for (int c = 0; c < m.c_fin; ++c)
             for (int k = 0; k < 7; ++k) wt[(size_t)k * m.c_fin + c] = w[(size_t)c * 7 + k];
-        if (!(m.w_out = upload(m, wt, err))) return false;
+        if (!(m.w_out = upload(m, wt, err))) return m.load_oom ? Z2B_ERR_OOM : Z2B_ERR_FORMAT;
         m.b_out = bo[0];
     }
     if (cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&m.err, sizeof(uint32_t)) != cudaSuccess) {
         err = "dac: stream or error word allocation failed";
-        return false;
+        return Z2B_ERR_CUDA;
     }
-    return true;
+    return Z2B_OK;
 }
 
 void dac_free(DacModel& m) {
@@ -251,11 +253,11 @@ void dac_free(DacModel& m) {
     m.cap_s[0] = m.cap_s[1] = m.cap_x = m.cap_audio = m.cap_codes = m.cap_h = 0;
 }
 
-bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio, int64_t cap, std::string& err,
+int dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio, int64_t cap, std::string& err,
                       bool audio_on_device) {
     const int n = (int)wins.size();
-    if (n == 0) return true;
-    if (cudaSetDevice(m.device) != cudaSuccess) { err = "dac: bad device"; return false; }
+    if (n == 0) return Z2B_OK;
+    if (cudaSetDevice(m.device) != cudaSuccess) { err = "dac: bad device"; return Z2B_ERR_CUDA; }
     const int spf = m.samples_per_frame(), W = m.n_codebooks, nb = (int)m.blocks.size();
     int lmax = 0;
     int64_t total = 0, max_span = 0;
@@ -266,7 +268,7 @@ bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio
         if (w.a < 0 || w.b <= w.a || w.H < 0 || (w.H > 0 && !w.codes) || w.s0 < 0 || w.s1 < w.s0 ||
             w.s1 > (int64_t)(w.b - w.a) * spf) {
             err = "dac: bad window " + std::to_string(i);
-            return false;
+            return Z2B_ERR_ARG;
         }
         lmax = std::max(lmax, w.b - w.a);
         total += w.s1 - w.s0;
@@ -274,15 +276,15 @@ bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio
         rows[i] = std::max(0, std::min(w.H, w.b + W - 1) - w.a);   // code rows the shear reads
         code_rows += rows[i];
     }
-    if (total > cap) { err = "dac: output buffer too small"; return false; }
-    if (total == 0) return true;
+    if (total > cap) { err = "dac: output buffer too small"; return Z2B_ERR_ARG; }
+    if (total == 0) return Z2B_OK;
 
     // stage lengths (rows per window) and channel strides
     std::vector<int> L(nb + 1), st(nb + 1);
     L[0] = lmax;
     st[0] = m.conv_in.oc_pad;
     for (int b = 0; b < nb; ++b) {
-        if ((int64_t)L[b] * m.blocks[b].stride > (1 << 30)) { err = "dac: window too long"; return false; }
+        if ((int64_t)L[b] * m.blocks[b].stride > (1 << 30)) { err = "dac: window too long"; return Z2B_ERR_ARG; }
         L[b + 1] = L[b] * m.blocks[b].stride;
         st[b + 1] = m.blocks[b].convt.oc_pad;
     }
@@ -300,7 +302,7 @@ bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio
         !ensure(m.X, m.cap_x, std::max<size_t>(need_x, 1)) || !ensure(m.audio, m.cap_audio, (size_t)total) ||
         !ensure(m.codes, m.cap_codes, up_bytes / 4)) {
         err = "dac: workspace allocation failed";
-        return false;
+        return Z2B_ERR_OOM;
     }
     if (up_bytes > m.cap_h) {
         if (m.h_stage) cudaFreeHost(m.h_stage);
@@ -308,7 +310,7 @@ bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio
         m.cap_h = 0;
         if (cudaHostAlloc(&m.h_stage, up_bytes, cudaHostAllocDefault) != cudaSuccess) {
             err = "dac: pinned staging allocation failed";
-            return false;
+            return Z2B_ERR_OOM;
         }
         m.cap_h = up_bytes;
     }
@@ -378,16 +380,16 @@ bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio
     if (!ok) {
         cudaStreamSynchronize(s);
         err = "dac: launch failed: " + std::string(cudaGetErrorString(cudaGetLastError()));
-        return false;
+        return Z2B_ERR_CUDA;
     }
     uint32_t derr = 0;
     ok = cudaMemcpyAsync(audio, m.audio, (size_t)total * 4,
                          audio_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, s) == cudaSuccess &&
          cudaMemcpyAsync(&derr, m.err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s) == cudaSuccess &&
          cudaStreamSynchronize(s) == cudaSuccess;
-    if (!ok) { err = "dac: " + std::string(cudaGetErrorString(cudaGetLastError())); return false; }
-    if (derr) { err = "dac: device error " + std::to_string(derr); return false; }
-    return true;
+    if (!ok) { err = "dac: " + std::string(cudaGetErrorString(cudaGetLastError())); return Z2B_ERR_CUDA; }
+    if (derr) { err = "dac: device error " + std::to_string(derr); return Z2B_ERR_DEVICE; }
+    return Z2B_OK;
 }
 
 }  // namespace z2b

@@ -78,14 +78,18 @@ struct DacModel {
     void* h_stage = nullptr;          // pinned host staging
     size_t cap_h = 0;
     long last_launches = 0;
+    bool load_oom = false;            // a device allocation failed while loading
     int samples_per_frame() const;
 };
 
-bool dac_load(DacModel& m, const char* path, int device, std::string& err);
+// Returns Z2B_OK or a Z2B_ERR_* code (IO: unreadable file, FORMAT: not a usable DAC GGUF,
+// OOM: device memory, CUDA: device set-up) with err set.
+int dac_load(DacModel& m, const char* path, int device, std::string& err);
 void dac_free(DacModel& m);
 // Decode the windows in one batched pass; audio receives each window's kept samples in order.
-bool dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio, int64_t cap,
-                      std::string& err, bool audio_on_device = false);
+// Returns Z2B_OK or a Z2B_ERR_* code (include/z2b.h) with err set.
+int dac_decode_batch(DacModel& m, const std::vector<DacWin>& wins, float* audio, int64_t cap,
+                     std::string& err, bool audio_on_device = false);
 
 // ---- kernel launchers (k_dac.cu) ----
 

@@ -106,31 +106,27 @@ def kl_base(model, seqs: list[Sequence], path: str) -> dict:
 
 
 def read_base(path: str) -> tuple[dict, list[Sequence], np.ndarray]:
-    """Header, sequences and the [E][audio_vocab] event log-probabilities of a base file."""
+    """Header, sequences and the [E][audio_vocab] event log-probabilities of a base file (the
+    event block memory-mapped: bases of large corpora run to gigabytes)."""
     with open(path, "rb") as f:
-        buf = f.read()
-    if buf[:8] != MAGIC:
-        raise ValueError(f"{path}: bad magic")
-    version, ncb, av, pad, n_seq = struct.unpack_from("<5I", buf, 8)
-    if version != VERSION:
-        raise ValueError(f"{path}: version {version} != {VERSION} (regenerate base)")
-    off = 28
-    meta = []
-    for _ in range(n_seq):
-        meta.append(struct.unpack_from("<IiI", buf, off))
-        off += 12
-    seqs = []
-    for n, spk_pos, sdim in meta:
-        ids = np.frombuffer(buf, np.float32, n * (ncb + 1), off).reshape(n, ncb + 1)
-        off += 4 * n * (ncb + 1)
-        spk = None
-        if sdim:
-            spk = np.frombuffer(buf, np.float32, sdim, off).copy()
-            off += 4 * sdim
-        seqs.append(Sequence(ids.copy(), spk, spk_pos))
-    if (len(buf) - off) % (4 * av):
+        head = f.read(28)
+        if len(head) < 28 or head[:8] != MAGIC:
+            raise ValueError(f"{path}: bad magic")
+        version, ncb, av, pad, n_seq = struct.unpack_from("<5I", head, 8)
+        if version != VERSION:
+            raise ValueError(f"{path}: version {version} != {VERSION} (regenerate base)")
+        meta = [struct.unpack("<IiI", f.read(12)) for _ in range(n_seq)]
+        seqs = []
+        for n, spk_pos, sdim in meta:
+            ids = np.frombuffer(f.read(4 * n * (ncb + 1)), np.float32).reshape(n, ncb + 1).copy()
+            spk = np.frombuffer(f.read(4 * sdim), np.float32).copy() if sdim else None
+            seqs.append(Sequence(ids, spk, spk_pos))
+        off = f.tell()
+        size = f.seek(0, 2)
+    if (size - off) % (4 * av):
         raise ValueError(f"{path}: truncated event block")
-    lp = np.frombuffer(buf, np.float32, (len(buf) - off) // 4, off).reshape(-1, av)
+    n_ev = (size - off) // (4 * av)
+    lp = np.memmap(path, np.float32, "r", off, (n_ev, av)) if n_ev else np.zeros((0, av), np.float32)
     return {"n_codebooks": ncb, "audio_vocab": av, "audio_pad_id": pad}, seqs, lp
 
 

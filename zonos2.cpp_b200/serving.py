@@ -141,7 +141,7 @@ class TtsEngine:
                 else:                                   # buffered: one decode of [0, end)
                     nf = len(j.pcm.codes)
                     end = s.eos_frame if 0 <= s.eos_frame < nf else nf
-                    w = (j.pcm._snapshot(nf), 0, end, 0, 0) if end > 0 else None
+                    w = (j.pcm.snapshot(nf), 0, end, 0, 0) if end > 0 else None
                 self.batcher.submit(j.req.rid, w, j.req.fade_out_ms, self.cfg.sample_rate)
                 finished.append(j.req.rid)
         for rid, pcm in self.batcher.flush():

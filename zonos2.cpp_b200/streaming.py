@@ -41,7 +41,8 @@ class PcmStream:
         for f in np.asarray(frames, np.int32).reshape(-1, self.cfg.n_codebooks):
             self.codes.append(f)
 
-    def _snapshot(self, n):
+    def snapshot(self, n):
+        """The first n frames as an [n][n_codebooks] array (a copy: the stream keeps growing)."""
         return np.asarray(self.codes[:n], np.int32).reshape(n, self.cfg.n_codebooks)
 
     def ready_windows(self) -> list[tuple]:
@@ -53,7 +54,7 @@ class PcmStream:
         out = []
         while H - self.emitted >= c.block + c.ctx + shear:
             f_hi = H - c.ctx - shear
-            out.append((self._snapshot(H), self.emitted, f_hi, c.ctx, c.ctx))
+            out.append((self.snapshot(H), self.emitted, f_hi, c.ctx, c.ctx))
             self.emitted = f_hi
         return out
 
@@ -65,7 +66,7 @@ class PcmStream:
         end = eos_frame if 0 <= eos_frame < nf else nf
         if end <= self.emitted:
             return None
-        w = (self._snapshot(nf), self.emitted, end, self.cfg.ctx, 0)
+        w = (self.snapshot(nf), self.emitted, end, self.cfg.ctx, 0)
         self.emitted = end
         return w
 
