@@ -8,10 +8,18 @@ requests through the backbone and the GPU DAC and checks the same, bit for bit, 
 request's frames do not depend on the other requests in its steps."""
 from __future__ import annotations
 
+import os
+import socket
+
 import numpy as np
 import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
 
 from oracle.dac_oracle import DacOracle
+from tests.conftest import load_pkg
+
+load_pkg()                                            # spawned ranks import this module afresh
 
 
 class _OracleDecoder:
@@ -199,6 +207,75 @@ def test_eos_frame_follows_slot_sample():
         d = eng.run()[0]
         assert d["eos_frame"] == max(0, k - c)
         assert len(d["codes"]) == k + hp.n_codebooks + 1
+
+
+class _NullDecoder:
+    def decode_windows(self, ws):
+        return [np.zeros((w[2] - w[1]) * 4, np.float32) for w in ws]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+FORBIDDEN = ("broadcast_object_list", "all_gather_object", "barrier", "broadcast", "all_gather", "send", "recv")
+
+
+def _tts_worker(rank, world, port, q):
+    import z2b.serving as SV
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    saved = {nm: getattr(dist, nm) for nm in FORBIDDEN}
+    try:
+        hp = _hp()
+        ctx = _ScriptedCtx(hp, eoa_at={}, seed=rank)
+        eng = SV.TtsEngine(ctx, hp, _NullDecoder(), n_slots=3)
+
+        def forbid(name):
+            def f(*a, **k):
+                raise AssertionError(f"collective {name} while serving")
+            return f
+
+        for nm in FORBIDDEN:                          # a replica never waits for another
+            setattr(dist, nm, forbid(nm))
+        reqs = [SV.TtsRequest(i, f"request {i}", max_frames=5 + i) for i in range(11)]
+        try:
+            r = SV.serve_tts(eng, reqs)
+        finally:
+            for nm, f in saved.items():
+                setattr(dist, nm, f)
+        q.put((rank, r["steps"], r["frames"], r["pcm_samples"], sorted(r["done"]),
+               sum(len(d["codes"]) for d in r["done"].values())))
+    except Exception as e:                            # report instead of hanging the parent
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_split_the_requests():
+    """Two replicas: each request served once, on rank rid mod 2, with no collective while
+    serving; the reduced frame total is every request's frame count."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tts_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r = q.get(timeout=120)
+        assert len(r) > 2, r
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, s0, f0, p0, d0, n0), (_, s1, f1, p1, d1, n1) = res[0], res[1]
+    assert d0 == list(range(0, 11, 2)) and d1 == list(range(1, 11, 2))
+    assert s0 == s1 and f0 == f1 == n0 + n1 == sum(5 + i for i in range(11))
+    assert p0 == p1 == f0 * 4                             # the null decoder's 4 samples per frame
 
 
 @pytest.mark.gpu

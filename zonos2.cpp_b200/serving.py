@@ -160,3 +160,30 @@ class TtsEngine:
             self.step()
             n += 1
         return self.done
+
+
+def serve_tts(engine: TtsEngine, requests: list[TtsRequest], max_steps: int = 1_000_000) -> dict:
+    """Serve `requests` over every rank of the default process group (or this process alone
+    without one), one engine per GPU: request i (in rid order) goes to rank i mod N, each rank
+    serves its share with no communication, then one all-reduce takes the longest step count
+    and another sums the frames and PCM samples. Returns those totals and this rank's results."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+    rank = dist.get_rank() if world > 1 else 0
+    for i, r in enumerate(sorted(requests, key=lambda r: r.rid)):
+        if i % world == rank:
+            engine.submit(r)
+    steps = 0
+    while (engine.queue or engine.jobs) and steps < max_steps:
+        engine.step()
+        steps += 1
+    pcm = sum(d["pcm"].size for d in engine.done.values() if d.get("pcm") is not None)
+    out = {"steps": steps, "frames": engine.frames, "pcm_samples": pcm, "done": engine.done}
+    if world > 1:
+        mx = torch.tensor([steps], dtype=torch.int64)
+        tot = torch.tensor([engine.frames, pcm], dtype=torch.int64)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        out.update(steps=int(mx[0]), frames=int(tot[0]), pcm_samples=int(tot[1]))
+    return out
